@@ -1,0 +1,223 @@
+// C ABI entry points of libdgx: argument validation, dispatch to the sm_100a
+// kernels, error reporting. See include/dgx.h for the contract.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.h"
+#include "gemm.h"
+
+namespace dgx {
+
+static thread_local char g_err[512] = "";
+
+dgx_status set_error(dgx_status st, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+dgx_status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return DGX_OK;
+  return set_error(DGX_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+TensorMapEncodeFn get_tensor_map_encoder() {
+  static TensorMapEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<TensorMapEncodeFn>(p);
+  });
+  return fn;
+}
+
+static int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int num_sms() {
+  static int cache[64] = {0};
+  const int d = current_device();
+  if (d < 0 || d >= 64) return 148;
+  if (!cache[d]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+    cache[d] = n > 0 ? n : 148;
+  }
+  return cache[d];
+}
+
+struct DeviceState {
+  uint32_t* err_word = nullptr;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+};
+static std::mutex g_dev_mu;
+static DeviceState g_dev[64];
+
+uint32_t* device_error_word() {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceState& st = g_dev[d & 63];
+  if (!st.err_word) {
+    if (cudaMalloc(&st.err_word, sizeof(uint32_t)) != cudaSuccess) return nullptr;
+    cudaMemset(st.err_word, 0, sizeof(uint32_t));
+  }
+  return st.err_word;
+}
+
+void* library_scratch(size_t bytes, cudaStream_t s) {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceState& st = g_dev[d & 63];
+  if (st.scratch_bytes < bytes) {
+    // The old buffer may still be read by queued work on `s`.
+    if (st.scratch) {
+      cudaStreamSynchronize(s);
+      cudaFree(st.scratch);
+      st.scratch = nullptr;
+      st.scratch_bytes = 0;
+    }
+    size_t want = bytes < (64u << 20) ? (64u << 20) : bytes;
+    if (cudaMalloc(&st.scratch, want) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    st.scratch_bytes = want;
+  }
+  return st.scratch;
+}
+
+}  // namespace dgx
+
+using namespace dgx;
+
+extern "C" {
+
+const char* dgx_version(void) { return "libdgx 0.1 (sm_100a)"; }
+
+const char* dgx_last_error(void) { return g_err; }
+
+dgx_status dgx_init(int device) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return set_error(DGX_EINVAL, "dgx_init: device %d of %d", device, n);
+  e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  cudaDeviceProp p;
+  e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceProperties");
+  if (p.major != 10) return set_error(DGX_EUNSUPPORTED, "dgx_init: device is sm_%d%d, libdgx is built for sm_100a",
+                                      p.major, p.minor);
+  if (!get_tensor_map_encoder()) return set_error(DGX_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if (!device_error_word()) return set_error(DGX_ENOMEM, "dgx_init: cannot allocate the error word");
+  return DGX_OK;
+}
+
+dgx_status dgx_sync_check(void* stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e, "dgx_sync_check");
+  uint32_t* w = device_error_word();
+  if (!w) return set_error(DGX_ENOMEM, "dgx_sync_check: no error word");
+  uint32_t v = 0;
+  e = cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "dgx_sync_check: read error word");
+  if (v) {
+    cudaMemset(w, 0, sizeof(uint32_t));
+    return set_error(DGX_ETIMEOUT, "device error word 0x%x (1=wait timeout, 2=tmem, 4=bounds)", v);
+  }
+  return DGX_OK;
+}
+
+size_t dgx_gemm_workspace_size(int M, int N, int K, int transA, int transB, dgx_dtype ab_type, int f32_mode) {
+  if (ab_type != DGX_F32 || f32_mode != DGX_F32_3XTF32 || M <= 0 || N <= 0 || K <= 0) return 0;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.transA = transA;
+  a.transB = transB;
+  return gemm_f32_scratch_floats(a) * sizeof(float);
+}
+
+dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb, int ldc,
+                    int transA, int transB, dgx_dtype ab_type, dgx_dtype c_type, int f32_mode, const float* bias,
+                    int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm: negative size %dx%dx%d", M, N, K);
+  if (M == 0 || N == 0) return DGX_OK;
+  if (!A || !B || !C) return set_error(DGX_EINVAL, "dgx_gemm: null operand");
+  if (ab_type != DGX_F32 && ab_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gemm: ab_type %d", ab_type);
+  if (c_type != DGX_F32 && c_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gemm: c_type %d", c_type);
+  if (epilogue < DGX_EPI_NONE || epilogue > DGX_EPI_RELU) return set_error(DGX_EINVAL, "dgx_gemm: epilogue");
+  if ((epilogue == DGX_EPI_BIAS || epilogue == DGX_EPI_BIAS_RELU) && !bias)
+    return set_error(DGX_EINVAL, "dgx_gemm: bias epilogue without bias");
+  const int min_lda = transA ? M : K, min_ldb = transB ? K : N;
+  if (lda < min_lda || ldb < min_ldb || ldc < N)
+    return set_error(DGX_EINVAL, "dgx_gemm: leading dimension too small (lda %d ldb %d ldc %d)", lda, ldb, ldc);
+  cudaStream_t s = (cudaStream_t)stream;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.lda = lda;
+  a.ldb = ldb;
+  a.ldc = ldc;
+  a.transA = transA ? 1 : 0;
+  a.transB = transB ? 1 : 0;
+  a.C = C;
+  a.c_bf16 = c_type == DGX_BF16;
+  a.bias = (epilogue == DGX_EPI_BIAS || epilogue == DGX_EPI_BIAS_RELU) ? bias : nullptr;
+  a.relu = (epilogue == DGX_EPI_BIAS_RELU || epilogue == DGX_EPI_RELU);
+  a.beta = beta;
+  a.err = device_error_word();
+  if (K == 0) {
+    // Degenerate contraction: C = beta*C (+bias)(relu); the SIMT kernel handles it.
+    return cuda_status(gemm_simt(a, A, B, ab_type == DGX_BF16, s), "dgx_gemm simt");
+  }
+  const int esz = ab_type == DGX_BF16 ? 2 : 4;
+  const bool tc = gemm_tc_supported(a, esz, A, B);
+  if (ab_type == DGX_BF16) {
+    if (tc) return cuda_status(gemm_bf16_tc(a, A, B, s), "dgx_gemm bf16");
+    return cuda_status(gemm_simt(a, A, B, 1, s), "dgx_gemm bf16 simt");
+  }
+  // f32 inputs
+  if (f32_mode == DGX_F32_3XTF32) {
+    const size_t need = gemm_f32_scratch_floats(a) * sizeof(float);
+    void* ws = workspace;
+    if (ws && workspace_bytes < need)
+      return set_error(DGX_ENOMEM, "dgx_gemm: workspace %zu bytes < %zu", workspace_bytes, need);
+    if (!ws) ws = library_scratch(need, s);
+    if (!ws) return set_error(DGX_ENOMEM, "dgx_gemm: cannot allocate %zu bytes of scratch", need);
+    return cuda_status(gemm_f32_3xtf32(a, (const float*)A, (const float*)B, (float*)ws, s), "dgx_gemm 3xtf32");
+  }
+  if (f32_mode != DGX_F32_3XTF32 && f32_mode != DGX_F32_FFMA)
+    return set_error(DGX_EINVAL, "dgx_gemm: f32_mode %d", f32_mode);
+  return cuda_status(gemm_simt(a, A, B, 0, s), "dgx_gemm f32 simt");
+}
+
+dgx_status dgx_bmm(const void* A, const void* B, void* C, int batch, int M, int N, int K, dgx_dtype ab_type,
+                   dgx_dtype c_type, void* stream) {
+  if (batch < 0) return set_error(DGX_EINVAL, "dgx_bmm: negative batch");
+  const size_t esz = ab_type == DGX_BF16 ? 2 : 4, csz = c_type == DGX_BF16 ? 2 : 4;
+  for (int b = 0; b < batch; ++b) {
+    dgx_status st = dgx_gemm((const char*)A + (size_t)b * M * K * esz, (const char*)B + (size_t)b * K * N * esz,
+                             (char*)C + (size_t)b * M * N * csz, M, N, K, K, N, N, 0, 0, ab_type, c_type,
+                             DGX_F32_3XTF32, nullptr, DGX_EPI_NONE, 0.f, nullptr, 0, stream);
+    if (st != DGX_OK) return st;
+  }
+  return DGX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,32 @@
+// Host-side plumbing shared by the libdgx translation units: the driver-API
+// tensor-map encoder (fetched through the runtime, so libdgx does not link
+// libcuda directly), SM count, the per-thread error string and the device
+// error word that bounded waits report into.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/dgx.h"
+
+namespace dgx {
+
+typedef CUresult (*TensorMapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                      CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                      CUtensorMapFloatOOBfill);
+
+TensorMapEncodeFn get_tensor_map_encoder();
+int num_sms();
+uint32_t* device_error_word();  // per-device word in global memory
+
+// Record a message as the calling thread's last error and return `st`.
+dgx_status set_error(dgx_status st, const char* fmt, ...);
+dgx_status cuda_status(cudaError_t e, const char* what);
+
+// Per-device scratch buffer owned by the library (grown on demand with
+// cudaMalloc, reused across calls on the same stream order).
+void* library_scratch(size_t bytes, cudaStream_t s);
+
+}  // namespace dgx

@@ -1,0 +1,50 @@
+// Internal interface of the FlashAttention kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dgx {
+
+struct FlashFwdArgs {
+  const void* Q;
+  const void* K;
+  const void* V;
+  void* O;
+  float* lse;  // [BH*S] natural log, or null
+  int BH, S, D;
+  float scale;
+  int causal;
+  uint32_t* err;
+};
+
+struct FlashBwdArgs {
+  const void* Q;
+  const void* K;
+  const void* V;
+  const void* O;
+  const void* dO;
+  const float* lse;
+  void* dQ;
+  void* dK;
+  void* dV;
+  float* dq_acc;   // [BH*S*D] fp32 scratch
+  float* rowstat;  // [2][BH*S] scratch: D_i = dO_i.O_i, then LSE_i*log2(e)
+  int BH, S, D;
+  float scale;
+  int causal;
+  uint32_t* err;
+};
+
+// Scratch bytes the backward needs (dQ accumulator + row statistics).
+size_t flash_bwd_scratch_bytes(int BH, int S, int D);
+
+bool flash_tc_supported(int D, const void* const* ptrs, int n);
+cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s);
+cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s);
+// SIMT kernels for head dims the tensor-core kernels do not take (D % 8 != 0
+// or D > 64): fp32 math, one thread per query row / key row.
+cudaError_t flash_fwd_simt(const FlashFwdArgs& a, cudaStream_t s);
+cudaError_t flash_bwd_simt(const FlashBwdArgs& a, cudaStream_t s);
+
+}  // namespace dgx

@@ -1,0 +1,506 @@
+// FlashAttention backward on sm_100a (tcgen05 + TMEM + TMA).
+//
+// Replaces the "flash_attention" branch of backward()
+// (runtime/ops/autograd.inc:779-840). The reference recomputes each row's
+// softmax statistics (pass 1), D_i = dO_i.O_i (pass 2) and then P, dS and the
+// three gradients (pass 3) in f64 scalar loops. Here the forward's LSE
+// replaces pass 1, a small kernel computes D_i (pass 2), and one tensor-core
+// kernel does pass 3 with the same identities:
+//   P = exp(scale*QK^T - LSE),  dV = P^T dO,  dP = dO V^T,
+//   dS = P o (dP - D),  dQ = scale * dS K,  dK = scale * dS^T Q.
+//
+// One CTA keeps a 128-key K/V tile resident and walks the 128-row Q tiles
+// that can see it (causal: i >= j). Per Q tile the MMA warp issues
+//   S^T = K Q^T, dP^T = V dO^T           (TMEM, lanes = keys)
+//   dV += P^T dO, dK += dS^T Q           (P^T, dS^T read from TMEM)
+//   dQ_part = dS K                       (dS staged in shared memory)
+// in the order S(i) dP(i) | dV(i) S(i+1) | dK(i) dQ(i) dP(i+1) so the tensor
+// core overlaps the element-wise work of the 8 compute warps. dQ partials go
+// through two TMEM buffers to 4 drain warps that add them into an fp32
+// accumulator with vector atomics; a last kernel scales it and casts to bf16.
+#include <math.h>
+
+#include "common.h"
+#include "flash.h"
+#include "sm100.cuh"
+
+namespace dgx {
+
+namespace {
+
+constexpr int BKV = 128;  // keys per CTA
+constexpr int BQ = 128;   // queries per step
+constexpr int DP = 64;
+constexpr int Q_STAGES = 2;
+constexpr int TILE = 128 * DP * 2;  // 16 KB
+constexpr int NUM_THREADS = 448;    // 8 compute + 4 dQ-drain + TMA + MMA warps
+
+constexpr int SM_K = 0, SM_V = TILE, SM_Q = 2 * TILE, SM_DO = SM_Q + Q_STAGES * TILE;
+constexpr int SM_DS = SM_DO + Q_STAGES * TILE;  // 128 queries x 128 keys bf16, MN-major (2 x 16 KB)
+constexpr int SM_BAR = SM_DS + 2 * TILE;
+constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+
+constexpr uint32_t T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384;  // T_DQ: 2 x 64
+constexpr uint32_t TMEM_COLS = 512;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+struct BwdBars {
+  uint64_t kv_full, q_full[Q_STAGES], q_empty[Q_STAGES];
+  uint64_t s_full, dp_full, p_ready, ds_ready, dq_full[2], dq_empty[2], acc_done;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                     FlashBwdArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  BwdBars* bars = reinterpret_cast<BwdBars*>(smem + SM_BAR);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WaitCtx wc{&bars->abort, args.err};
+
+  const int nq = (args.S + BQ - 1) / BQ;
+  const int j = blockIdx.x / args.BH;  // key tile (heaviest first under causal)
+  const int bh = blockIdx.x % args.BH;
+  const int i0 = args.causal ? (j * BKV) / BQ : 0;
+  const int n = nq - i0;  // Q tiles this CTA walks
+  const size_t row0 = (size_t)bh * args.S;
+  const float* Dstat = args.rowstat;
+  const float* L2stat = args.rowstat + (size_t)args.BH * args.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    for (int s = 0; s < Q_STAGES; ++s) {
+      mbar_init(&bars->q_full[s], 1);
+      mbar_init(&bars->q_empty[s], 1);
+    }
+    mbar_init(&bars->s_full, 1);
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->p_ready, 8);
+    mbar_init(&bars->ds_ready, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->dq_full[b], 1);
+      mbar_init(&bars->dq_empty[b], 4);
+    }
+    mbar_init(&bars->acc_done, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 13) {
+    tmem_alloc(&bars->tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 12) {
+    // ---------------------------------------------------------------- TMA
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      mbar_arrive_expect_tx(&bars->kv_full, 2 * TILE);
+      tma_load_3d(smem + SM_K, &tmK, &bars->kv_full, 0, j * BKV, bh);
+      tma_load_3d(smem + SM_V, &tmV, &bars->kv_full, 0, j * BKV, bh);
+      int it = 0;
+      for (; it < n; ++it) {
+        const int s = it % Q_STAGES;
+        if (!mbar_wait(&bars->q_empty[s], ((it / Q_STAGES) & 1) ^ 1, wc)) break;
+        mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE);
+        tma_load_3d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, (i0 + it) * BQ, bh);
+        tma_load_3d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, (i0 + it) * BQ, bh);
+      }
+      mbar_drain(&bars->kv_full, 0);
+      for (int f = max(0, it - Q_STAGES); f < it; ++f) mbar_drain(&bars->q_full[f % Q_STAGES], (f / Q_STAGES) & 1);
+    }
+  } else if (warp == 13) {
+    // ---------------------------------------------------------------- MMA
+    if (elect_one_lane()) {
+      constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);   // K-major x K-major, N = 128 queries
+      constexpr uint32_t id_acc = make_idesc(1, 0, 1, 128, DP);  // TMEM A x MN-major B, N = D
+      constexpr uint32_t id_dq = make_idesc(1, 1, 1, 128, DP);   // MN-major dS x MN-major K
+      const uint32_t sK = smem_u32(smem + SM_K), sV = smem_u32(smem + SM_V);
+      const uint32_t sQ = smem_u32(smem + SM_Q), sdO = smem_u32(smem + SM_DO), sdS = smem_u32(smem + SM_DS);
+      auto kmajor_pair = [&](uint32_t d, uint32_t a, uint32_t b) {  // d = a . b^T over D
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk)
+          mma_f16_ss(d, sw128_desc(a + kk * 32, 16, 1024), sw128_desc(b + kk * 32, 16, 1024), id_s, kk > 0);
+      };
+      auto tmem_a_acc = [&](uint32_t d, uint32_t a_tmem, uint32_t b, bool first) {  // d += A(tmem) . B
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          mma_f16_ts(d, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), sw128_desc(b + kk * 2048, DP * 128, 1024), id_acc,
+                     (!first || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&bars->kv_full, 0, wc) && mbar_wait(&bars->q_full[0], 0, wc);
+      if (ok) {
+        tc_fence_after();
+        kmajor_pair(tmem + T_ST, sK, sQ);
+        tc_commit(&bars->s_full);
+        kmajor_pair(tmem + T_DPT, sV, sdO);
+        tc_commit(&bars->dp_full);
+      }
+      for (int it = 0; ok && it < n; ++it) {
+        const int s = it % Q_STAGES;
+        const uint32_t q_s = sQ + s * TILE, do_s = sdO + s * TILE;
+        const bool next = it + 1 < n;
+        const int s1 = (it + 1) % Q_STAGES;
+        if (!(ok = mbar_wait(&bars->p_ready, it & 1, wc))) break;
+        tc_fence_after();
+        tmem_a_acc(tmem + T_DV, tmem + T_ST, do_s, it == 0);  // dV += P^T dO
+        if (next) {
+          if (!(ok = mbar_wait(&bars->q_full[s1], ((it + 1) / Q_STAGES) & 1, wc))) break;
+          tc_fence_after();
+          kmajor_pair(tmem + T_ST, sK, sQ + s1 * TILE);  // S^T(i+1)
+          tc_commit(&bars->s_full);
+        }
+        if (!(ok = mbar_wait(&bars->ds_ready, it & 1, wc))) break;
+        tc_fence_after();
+        tmem_a_acc(tmem + T_DK, tmem + T_DPT, q_s, it == 0);  // dK += dS^T Q
+        const int b = it & 1;
+        if (!(ok = mbar_wait(&bars->dq_empty[b], ((it >> 1) & 1) ^ 1, wc))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)  // dQ_part = dS K
+          mma_f16_ss(tmem + T_DQ + 64 * b, sw128_desc(sdS + kk * 2048, BKV * 128, 1024),
+                     sw128_desc(sK + kk * 2048, DP * 128, 1024), id_dq, kk > 0);
+        tc_commit(&bars->dq_full[b]);
+        tc_commit(&bars->q_empty[s]);
+        if (next) {
+          kmajor_pair(tmem + T_DPT, sV, sdO + s1 * TILE);  // dP^T(i+1)
+          tc_commit(&bars->dp_full);
+        }
+      }
+      if (ok) tc_commit(&bars->acc_done);
+    }
+    __syncwarp();
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------------- dQ drain
+    const int qw = warp & 3;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    for (int it = 0; it < n; ++it) {
+      const int b = it & 1;
+      if (!mbar_wait(&bars->dq_full[b], (it >> 1) & 1, wc)) break;
+      tc_fence_after();
+      uint32_t v[DP];
+      tmem_ld32(tmem + lane_off + T_DQ + 64 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(tmem + lane_off + T_DQ + 64 * b + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->dq_empty[b]);
+      const int q = (i0 + it) * BQ + qw * 32 + lane;
+      if (q < args.S) {
+        float* dst = args.dq_acc + (row0 + q) * args.D;
+        if (args.D == DP) {
+#pragma unroll
+          for (int c = 0; c < DP; c += 4)
+            red_add_v4(dst + c, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
+                       __uint_as_float(v[c + 3]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < DP; ++c)
+            if (c < args.D) atomicAdd(dst + c, __uint_as_float(v[c]));
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- compute (P, dS)
+    const int qw = warp & 3, h = warp >> 2;
+    const int kr = qw * 32 + lane;
+    const int key = j * BKV + kr;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const float sl2 = args.scale * 1.4426950408889634f;
+    uint8_t* ds_tile = smem + SM_DS + h * TILE;  // queries [64h, 64h+64)
+    for (int it = 0; it < n; ++it) {
+      const int qbase = (i0 + it) * BQ + 64 * h;
+      const bool need_mask = (args.causal && (i0 + it) * BQ < j * BKV + BKV - 1) || (qbase + 64 > args.S) ||
+                             (j * BKV + BKV > args.S);
+      if (!mbar_wait(&bars->s_full, it & 1, wc)) break;
+      tc_fence_after();
+      float p[64];
+#pragma unroll
+      for (int cc = 0; cc < 64; cc += 32) {
+        uint32_t sv[32];
+        tmem_ld32(tmem + lane_off + T_ST + 64 * h + cc, sv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int q = qbase + cc + t;
+          const float l2 = q < args.S ? __ldg(L2stat + row0 + q) : 0.f;
+          float e = ex2(fmaf(__uint_as_float(sv[t]), sl2, -l2));
+          if (need_mask && (q >= args.S || key >= args.S || (args.causal && q < key))) e = 0.f;
+          p[cc + t] = e;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(p[cc + 2 * t], p[cc + 2 * t + 1]);
+        tmem_st16(tmem + lane_off + T_ST + 64 * h + cc / 2, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_ready);
+
+      if (!mbar_wait(&bars->dp_full, it & 1, wc)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 64; cc += 32) {
+        uint32_t dv[32];
+        tmem_ld32(tmem + lane_off + T_DPT + 64 * h + cc, dv);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const int q = qbase + cc + t;
+          const float d0 = q < args.S ? __ldg(Dstat + row0 + q) : 0.f;
+          const float d1 = q + 1 < args.S ? __ldg(Dstat + row0 + q + 1) : 0.f;
+          const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - d0);
+          const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - d1);
+          pk[t / 2] = pack_bf16x2(ds0, ds1);
+        }
+        tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
+        // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
+        // [64h, 64h+64) of this half, 16-byte units XOR-swizzled by (kr & 7).
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int unit = cc / 8 + u;
+          uint4* dst = reinterpret_cast<uint4*>(ds_tile + kr * 128 + ((unit ^ (kr & 7)) << 4));
+          *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ds_ready);
+    }
+    // ------------------------------------------------------------ epilogue: dV (h=0), dK (h=1)
+    if (mbar_wait(&bars->acc_done, 0, wc)) {
+      tc_fence_after();
+      uint32_t v[DP];
+      const uint32_t col = h ? T_DK : T_DV;
+      tmem_ld32(tmem + lane_off + col, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(tmem + lane_off + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_ld_wait();
+      if (key < args.S) {
+        const float mul = h ? args.scale : 1.f;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) + (row0 + key) * args.D;
+        if (args.D == DP) {
+#pragma unroll
+          for (int c = 0; c < DP; c += 8) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[c + 0]) * mul, __uint_as_float(v[c + 1]) * mul);
+            w.y = pack_bf16x2(__uint_as_float(v[c + 2]) * mul, __uint_as_float(v[c + 3]) * mul);
+            w.z = pack_bf16x2(__uint_as_float(v[c + 4]) * mul, __uint_as_float(v[c + 5]) * mul);
+            w.w = pack_bf16x2(__uint_as_float(v[c + 6]) * mul, __uint_as_float(v[c + 7]) * mul);
+            *reinterpret_cast<uint4*>(dst + c) = w;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < DP; ++c)
+            if (c < args.D) dst[c] = __float2bfloat16_rn(__uint_as_float(v[c]) * mul);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 13) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// D_i = dO_i . O_i (fp32), L2_i = LSE_i * log2(e); zero the dQ accumulator.
+// One warp per row.
+__global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
+  const long long rows = (long long)a.BH * a.S;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.O) + r * a.D;
+    const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.dO) + r * a.D;
+    float s = 0.f;
+    for (int c = lane; c < a.D; c += 32) s = fmaf(__bfloat162float(o[c]), __bfloat162float(g[c]), s);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    float* dq = a.dq_acc + r * a.D;
+    for (int c = lane; c < a.D; c += 32) dq[c] = 0.f;
+    if (lane == 0) {
+      a.rowstat[r] = s;
+      a.rowstat[rows + r] = a.lse[r] * 1.4426950408889634f;
+    }
+  }
+}
+
+// dQ = bf16(scale * dQ_acc)
+__global__ void flash_bwd_post_kernel(FlashBwdArgs a) {
+  const long long total = (long long)a.BH * a.S * a.D;
+  __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(a.dQ);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x)
+    dq[i] = __float2bfloat16_rn(a.dq_acc[i] * a.scale);
+}
+
+bool make_map(CUtensorMap* map, const void* base, int BH, int S, int D) {
+  auto enc = get_tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
+  cuuint32_t box[3] = {DP, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t flash_bwd_scratch_bytes(int BH, int S, int D) {
+  return ((size_t)BH * S * D + 2 * (size_t)BH * S) * sizeof(float);
+}
+
+cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
+  CUtensorMap mq{}, mk{}, mv{}, mdo{};
+  if (!make_map(&mq, a.Q, a.BH, a.S, a.D) || !make_map(&mk, a.K, a.BH, a.S, a.D) ||
+      !make_map(&mv, a.V, a.BH, a.S, a.D) || !make_map(&mdo, a.dO, a.BH, a.S, a.D))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int sms = num_sms();
+  flash_bwd_pre_kernel<<<4 * sms, 256, 0, s>>>(a);
+  const int nkv = (a.S + BKV - 1) / BKV;
+  flash_bwd_kernel<<<nkv * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+  flash_bwd_post_kernel<<<4 * sms, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// SIMT kernels (any D <= 256): the reference's recurrences in fp32, one
+// thread per query row (forward, dQ) or key row (dK, dV).
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int SIMT_DMAX = 256;
+
+__device__ __forceinline__ float bf(const void* p, size_t i) {
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+__global__ void flash_fwd_simt_kernel(FlashFwdArgs a) {
+  const int bh = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.S) return;
+  const size_t base = (size_t)bh * a.S * a.D;
+  float acc[SIMT_DMAX];
+  for (int d = 0; d < a.D; ++d) acc[d] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  const int jend = a.causal ? i : a.S - 1;
+  for (int jj = 0; jj <= jend; ++jj) {
+    float s = 0.f;
+    for (int d = 0; d < a.D; ++d) s = fmaf(bf(a.Q, base + (size_t)i * a.D + d), bf(a.K, base + (size_t)jj * a.D + d), s);
+    s *= a.scale;
+    const float mn = fmaxf(m, s), corr = __expf(m - mn), p = __expf(s - mn);
+    l = l * corr + p;
+    for (int d = 0; d < a.D; ++d) acc[d] = acc[d] * corr + p * bf(a.V, base + (size_t)jj * a.D + d);
+    m = mn;
+  }
+  const float inv = 1.f / l;
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.O) + base + (size_t)i * a.D;
+  for (int d = 0; d < a.D; ++d) o[d] = __float2bfloat16_rn(acc[d] * inv);
+  if (a.lse) a.lse[(size_t)bh * a.S + i] = m + __logf(l);
+}
+
+// dQ_i = scale * sum_j dS_ij K_j  (thread per query row)
+__global__ void flash_bwd_simt_dq_kernel(FlashBwdArgs a) {
+  const int bh = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.S) return;
+  const size_t base = (size_t)bh * a.S * a.D, r = (size_t)bh * a.S + i;
+  const float lse = a.lse[r], Di = a.rowstat[r];
+  float acc[SIMT_DMAX];
+  for (int d = 0; d < a.D; ++d) acc[d] = 0.f;
+  const int jend = a.causal ? i : a.S - 1;
+  for (int jj = 0; jj <= jend; ++jj) {
+    float s = 0.f, dp = 0.f;
+    for (int d = 0; d < a.D; ++d) {
+      s = fmaf(bf(a.Q, base + (size_t)i * a.D + d), bf(a.K, base + (size_t)jj * a.D + d), s);
+      dp = fmaf(bf(a.dO, base + (size_t)i * a.D + d), bf(a.V, base + (size_t)jj * a.D + d), dp);
+    }
+    const float p = __expf(s * a.scale - lse), ds = p * (dp - Di);
+    for (int d = 0; d < a.D; ++d) acc[d] = fmaf(ds, bf(a.K, base + (size_t)jj * a.D + d), acc[d]);
+  }
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.dQ) + base + (size_t)i * a.D;
+  for (int d = 0; d < a.D; ++d) o[d] = __float2bfloat16_rn(acc[d] * a.scale);
+}
+
+// dV_j = sum_i P_ij dO_i, dK_j = scale * sum_i dS_ij Q_i  (thread per key row)
+__global__ void flash_bwd_simt_dkdv_kernel(FlashBwdArgs a) {
+  const int bh = blockIdx.y;
+  const int jj = blockIdx.x * blockDim.x + threadIdx.x;
+  if (jj >= a.S) return;
+  const size_t base = (size_t)bh * a.S * a.D;
+  float dk[SIMT_DMAX], dv[SIMT_DMAX];
+  for (int d = 0; d < a.D; ++d) dk[d] = dv[d] = 0.f;
+  for (int i = a.causal ? jj : 0; i < a.S; ++i) {
+    const size_t r = (size_t)bh * a.S + i;
+    float s = 0.f, dp = 0.f;
+    for (int d = 0; d < a.D; ++d) {
+      s = fmaf(bf(a.Q, base + (size_t)i * a.D + d), bf(a.K, base + (size_t)jj * a.D + d), s);
+      dp = fmaf(bf(a.dO, base + (size_t)i * a.D + d), bf(a.V, base + (size_t)jj * a.D + d), dp);
+    }
+    const float p = __expf(s * a.scale - a.lse[r]), ds = p * (dp - a.rowstat[r]);
+    for (int d = 0; d < a.D; ++d) {
+      dv[d] = fmaf(p, bf(a.dO, base + (size_t)i * a.D + d), dv[d]);
+      dk[d] = fmaf(ds, bf(a.Q, base + (size_t)i * a.D + d), dk[d]);
+    }
+  }
+  __nv_bfloat16* ok = reinterpret_cast<__nv_bfloat16*>(a.dK) + base + (size_t)jj * a.D;
+  __nv_bfloat16* ov = reinterpret_cast<__nv_bfloat16*>(a.dV) + base + (size_t)jj * a.D;
+  for (int d = 0; d < a.D; ++d) {
+    ok[d] = __float2bfloat16_rn(dk[d] * a.scale);
+    ov[d] = __float2bfloat16_rn(dv[d]);
+  }
+}
+}  // namespace
+
+cudaError_t flash_fwd_simt(const FlashFwdArgs& a, cudaStream_t s) {
+  if (a.D > SIMT_DMAX) return cudaErrorInvalidValue;
+  dim3 grid((a.S + 63) / 64, a.BH);
+  flash_fwd_simt_kernel<<<grid, 64, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t flash_bwd_simt(const FlashBwdArgs& a, cudaStream_t s) {
+  if (a.D > SIMT_DMAX) return cudaErrorInvalidValue;
+  flash_bwd_pre_kernel<<<4 * num_sms(), 256, 0, s>>>(a);
+  dim3 grid((a.S + 63) / 64, a.BH);
+  flash_bwd_simt_dq_kernel<<<grid, 64, 0, s>>>(a);
+  flash_bwd_simt_dkdv_kernel<<<grid, 64, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace dgx

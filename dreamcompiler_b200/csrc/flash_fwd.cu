@@ -1,0 +1,336 @@
+// Causal / full FlashAttention forward on sm_100a (tcgen05 + TMEM + TMA).
+//
+// Replaces dream_flash_attention (runtime/nn/training.inc:284-401): the same
+// online-softmax recurrence (running max m, normaliser l, rescaled
+// accumulator), restated for tensor cores. Layout [BH][S][D] bf16, heads
+// folded into the batch as in the reference's `(B, S*dk)` tensors.
+//
+// One CTA owns 256 query rows as two 128-row tiles (A, B) that share every
+// K/V tile load. Warps 0-3 run tile A's softmax, warps 4-7 tile B's, warp 8
+// issues TMA loads, warp 9 issues tcgen05.mma. TMEM holds S_A, S_B (128
+// fp32 columns each; P is written back over S as packed bf16 and read by the
+// P.V MMA straight from TMEM) and O_A, O_B (D fp32 columns each). The MMA
+// issue order  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)  lets the tensor core
+// work on one tile while the other tile's softmax runs.
+//
+// O is rescaled lazily: a row keeps its stale max until the new max exceeds
+// it by more than 8 (log2 units), so P stays <= 256 and the TMEM read-modify-
+// write of O is rare. The final O/l and LSE use the max actually applied, so
+// the result is exact up to rounding.
+#include <math.h>
+
+#include "common.h"
+#include "flash.h"
+#include "sm100.cuh"
+
+namespace dgx {
+
+namespace {
+
+constexpr int BLOCK_M = 128;   // rows per Q tile
+constexpr int BLOCK_N = 128;   // keys per K/V tile
+constexpr int DP = 64;         // head dim held in shared memory / TMEM (D <= 64 zero-padded)
+constexpr int KV_STAGES = 3;
+constexpr int TILE_BYTES = BLOCK_M * DP * 2;  // 16 KB for every Q/K/V tile
+constexpr int NUM_THREADS = 320;
+constexpr float RESCALE_LOG2 = 8.0f;
+
+// shared memory map (offsets from a 1024-aligned base)
+constexpr int SM_Q = 0;                               // Q_A, Q_B
+constexpr int SM_K = SM_Q + 2 * TILE_BYTES;           // K stages
+constexpr int SM_V = SM_K + KV_STAGES * TILE_BYTES;   // V stages
+constexpr int SM_BAR = SM_V + KV_STAGES * TILE_BYTES;
+constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+
+// TMEM columns
+constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + DP;
+constexpr uint32_t TMEM_COLS = 512;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct FwdBars {
+  uint64_t q_full, k_full[KV_STAGES], v_full[KV_STAGES], kv_empty[KV_STAGES];
+  uint64_t s_full[2], p_full[2], o_done[2];
+  uint32_t tmem_slot;
+  int abort;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, FlashFwdArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  FwdBars* bars = reinterpret_cast<FwdBars*>(smem + SM_BAR);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WaitCtx wc{&bars->abort, args.err};
+
+  // Heavy (late) query blocks first: block id -> (query block, head).
+  const int nqb = (args.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M);
+  const int qb = args.causal ? (nqb - 1 - (int)(blockIdx.x / args.BH)) : (int)(blockIdx.x / args.BH);
+  const int bh = blockIdx.x % args.BH;
+  const int q0 = qb * 2 * BLOCK_M;
+  const int nkv = (args.S + BLOCK_N - 1) / BLOCK_N;
+  int ntile[2];
+  for (int x = 0; x < 2; ++x) {
+    const int qs = q0 + x * BLOCK_M;
+    const int qe = min(qs + BLOCK_M, args.S);  // exclusive
+    ntile[x] = args.causal ? min((qe + BLOCK_N - 1) / BLOCK_N, nkv) : nkv;
+  }
+  if (q0 + BLOCK_M >= args.S) ntile[1] = ntile[0];  // tile B has no valid rows: shadow A
+  const int nA = ntile[0], nB = ntile[1];
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->s_full[x], 1);
+      mbar_init(&bars->p_full[x], 4);
+      mbar_init(&bars->o_done[x], 1);
+    }
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+  const int row_base = bh * args.S;  // row of the [BH*S, D] view
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- TMA
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
+      tma_load_3d(smem + SM_Q, &tmQ, &bars->q_full, 0, q0, bh);
+      tma_load_3d(smem + SM_Q + TILE_BYTES, &tmQ, &bars->q_full, 0, q0 + BLOCK_M, bh);
+      int j = 0;
+      for (; j < nB; ++j) {
+        const int s = j % KV_STAGES;
+        if (!mbar_wait(&bars->kv_empty[s], ((j / KV_STAGES) & 1) ^ 1, wc)) break;
+        mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
+        tma_load_3d(smem + SM_K + s * TILE_BYTES, &tmK, &bars->k_full[s], 0, j * BLOCK_N, bh);
+        mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
+        tma_load_3d(smem + SM_V + s * TILE_BYTES, &tmV, &bars->v_full[s], 0, j * BLOCK_N, bh);
+      }
+      mbar_drain(&bars->q_full, 0);
+      for (int f = max(0, j - KV_STAGES); f < j; ++f) {
+        mbar_drain(&bars->k_full[f % KV_STAGES], (f / KV_STAGES) & 1);
+        mbar_drain(&bars->v_full[f % KV_STAGES], (f / KV_STAGES) & 1);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA
+    if (elect_one_lane()) {
+      constexpr uint32_t idesc_s = make_idesc(1, 0, 0, BLOCK_M, BLOCK_N);  // Q.K^T, both K-major
+      constexpr uint32_t idesc_o = make_idesc(1, 0, 1, BLOCK_M, DP);       // P.V, V MN-major
+      const uint32_t sq = smem_u32(smem + SM_Q), sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V);
+      auto issue_s = [&](int x, int j) {
+        const uint32_t qa = sq + x * TILE_BYTES, ka = sk + (j % KV_STAGES) * TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk)
+          mma_f16_ss(tmem + (x ? T_S1 : T_S0), sw128_desc(qa + kk * 32, 16, 1024), sw128_desc(ka + kk * 32, 16, 1024),
+                     idesc_s, kk > 0 ? 1u : 0u);
+        tc_commit(&bars->s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t va = sv + (j % KV_STAGES) * TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BLOCK_N / 16; ++kk)
+          mma_f16_ts(tmem + (x ? T_O1 : T_O0), tmem + (x ? T_S1 : T_S0) + kk * 8,
+                     sw128_desc(va + kk * 16 * 128, DP * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&bars->q_full, 0, wc) && mbar_wait(&bars->k_full[0], 0, wc);
+      if (ok) {
+        tc_fence_after();
+        if (nA > 0) issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; ok && j < nB; ++j) {
+        const int s = j % KV_STAGES;
+        if (!(ok = mbar_wait(&bars->v_full[s], (j / KV_STAGES) & 1, wc))) break;
+        const bool next = j + 1 < nB;
+        if (j < nA) {
+          if (!(ok = mbar_wait(&bars->p_full[0], j & 1, wc))) break;
+          tc_fence_after();
+          issue_pv(0, j);
+          if (j == nA - 1) tc_commit(&bars->o_done[0]);
+        }
+        if (next) {
+          if (!(ok = mbar_wait(&bars->k_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, wc))) break;
+          tc_fence_after();
+          if (j + 1 < nA) issue_s(0, j + 1);
+        }
+        if (!(ok = mbar_wait(&bars->p_full[1], j & 1, wc))) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        tc_commit(&bars->kv_empty[s]);
+        if (j == nB - 1) tc_commit(&bars->o_done[1]);
+        if (next) issue_s(1, j + 1);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- softmax (warps 0-3: A, 4-7: B)
+    const int x = warp >> 2;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int qrow = q0 + x * BLOCK_M + r;
+    const int n = ntile[x];
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + (x ? T_S1 : T_S0);
+    const uint32_t t_o = tmem + lane_off + (x ? T_O1 : T_O0);
+    const float sl2 = args.scale * 1.4426950408889634f;  // scores -> log2 units
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!(ok = mbar_wait(&bars->s_full[x], j & 1, wc))) break;
+      tc_fence_after();
+      float s[BLOCK_N];
+#pragma unroll
+      for (int c = 0; c < BLOCK_N; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&s[c]));
+      tmem_ld_wait();
+      const int k0 = j * BLOCK_N;
+      const bool need_mask = (args.causal && k0 + BLOCK_N - 1 > q0 + x * BLOCK_M) || (k0 + BLOCK_N > args.S);
+      float mt = -INFINITY;
+      if (need_mask) {
+        const int lim = args.causal ? min(qrow, args.S - 1) : args.S - 1;  // last visible key
+#pragma unroll
+        for (int c = 0; c < BLOCK_N; ++c) {
+          s[c] = (k0 + c <= lim) ? s[c] * sl2 : -INFINITY;
+          mt = fmaxf(mt, s[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BLOCK_N; ++c) {
+          s[c] *= sl2;
+          mt = fmaxf(mt, s[c]);
+        }
+      }
+      // lazy rescale
+      float factor = 1.f;
+      if (mt > m_run + RESCALE_LOG2 || m_run == -INFINITY) {
+        factor = (m_run == -INFINITY) ? 0.f : ex2(m_run - mt);
+        m_run = mt;
+      }
+      const float mb = (m_run == -INFINITY) ? 0.f : m_run;
+      float rs = 0.f;
+      uint32_t p[BLOCK_N / 2];
+#pragma unroll
+      for (int c = 0; c < BLOCK_N; c += 2) {
+        const float e0 = ex2(s[c] - mb), e1 = ex2(s[c + 1] - mb);
+        rs += e0 + e1;
+        p[c / 2] = pack_bf16x2(e0, e1);
+      }
+      l_run = l_run * factor + rs;
+      if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+        // O_x is stable here: S_x(j) completing implies PV_x(j-1) completed.
+        uint32_t o[32];
+#pragma unroll
+        for (int c = 0; c < DP; c += 32) {
+          tmem_ld32(t_o + c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st16(t_o + c, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+          tmem_st16(t_o + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < BLOCK_N / 2; c += 16) tmem_st16(t_s + c, *reinterpret_cast<uint32_t(*)[16]>(&p[c]));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[x]);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok && mbar_wait(&bars->o_done[x], 0, wc)) {
+      tc_fence_after();
+      uint32_t o[DP];
+#pragma unroll
+      for (int c = 0; c < DP; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
+      tmem_ld_wait();
+      if (qrow < args.S) {
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.O) + ((size_t)row_base + qrow) * args.D;
+        if (args.D == DP) {
+#pragma unroll
+          for (int c = 0; c < DP; c += 8) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c) = w;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < DP; ++c)
+            if (c < args.D) orow[c] = __float2bfloat16_rn(__uint_as_float(o[c]) * inv);
+        }
+        if (args.lse) args.lse[(size_t)row_base + qrow] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+bool make_qkv_map(CUtensorMap* map, const void* base, int BH, int S, int D) {
+  auto enc = get_tensor_map_encoder();
+  if (!enc) return false;
+  // 3-D view [BH][S][D]: a box of 128 rows x 64 columns never crosses a head,
+  // rows past S and columns past D read as zero.
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
+  cuuint32_t box[3] = {DP, BLOCK_M, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool flash_tc_supported(int D, const void* const* ptrs, int n) {
+  if (D < 8 || D > DP || D % 8) return false;
+  for (int i = 0; i < n; ++i)
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) & 15) return false;
+  return true;
+}
+
+cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s) {
+  CUtensorMap mq{}, mk{}, mv{};
+  if (!make_qkv_map(&mq, a.Q, a.BH, a.S, a.D) || !make_qkv_map(&mk, a.K, a.BH, a.S, a.D) ||
+      !make_qkv_map(&mv, a.V, a.BH, a.S, a.D))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int nqb = (a.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M);
+  flash_fwd_kernel<<<nqb * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, a);
+  return cudaGetLastError();
+}
+
+}  // namespace dgx

@@ -1,0 +1,466 @@
+// Dense GEMM for the Dream `@` operator and its autograd GEMMs on sm_100a.
+//
+//   C[M,N] = op(A)[M,K] . op(B)[K,N]  (+ beta*C) (+ bias[N]) (ReLU)
+//
+// Replaces the reference's CPU/OpenCL/cuBLAS dispatch in `tensor_matmul`
+// (runtime/ops/elementwise.inc:971-1213), the "matmul" backward GEMMs
+// dA = dY.B^T and dB = A^T.dY (runtime/ops/autograd.inc:91-125) and the fused
+// `dream_linear` Y = X.W^T + b (+ReLU) (runtime/ops/elementwise.inc:1432-1521).
+//
+// Design: one persistent CTA per SM. Warp 0 issues TMA tile loads into a
+// ring of shared-memory stages; warp 1 issues tcgen05.mma into one of two TMEM
+// accumulators; warps 2-5 drain the other accumulator (tcgen05.ld), apply the
+// epilogue and store, so the epilogue of tile i overlaps the main loop of
+// tile i+1. Transposed operands are handled by the shared-memory descriptor's
+// major-ness (K-major or MN-major), never by a copy.
+//
+// bf16 inputs run kind::f16 with fp32 accumulation. f32 inputs run the
+// 3xTF32 split (a = a_hi + a_lo, C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi) on
+// kind::tf32, which keeps the error near fp32 level (<= 1e-4 normwise); the
+// hi/lo planes are produced by `split_tf32_kernel` into caller-visible scratch.
+#include "sm100.cuh"
+#include "gemm.h"
+
+namespace dgx {
+
+// ---------------------------------------------------------------------------
+// Tile configuration
+// ---------------------------------------------------------------------------
+template <bool TF32>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = TF32 ? 128 : 256;
+  static constexpr int ESZ = TF32 ? 4 : 2;                 // bytes per element
+  static constexpr int BK = 128 / ESZ;                       // one 128-byte swizzle row of K
+  static constexpr int MMA_K = 32 / ESZ;                     // K per tcgen05.mma (32 bytes)
+  static constexpr int A_BYTES = BM * BK * ESZ;              // 16 KB
+  static constexpr int B_BYTES = BN * BK * ESZ;              // 32 KB (bf16) / 16 KB (tf32)
+  static constexpr int PLANES = TF32 ? 2 : 1;                // hi (+ lo) planes per operand
+  static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
+  static constexpr int STAGES = TF32 ? 3 : 4;
+  static constexpr int TMEM_COLS = 2 * BN;                   // double-buffered accumulator
+  static constexpr int CHUNK = 128 / ESZ;                    // MN elements per 128-byte chunk
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t FMT = TF32 ? 2u : 1u;
+};
+
+struct TileSched {
+  int tiles_m, tiles_n, group_m;
+  __device__ __forceinline__ void coords(int t, int& tm, int& tn) const {
+    const int per_group = group_m * tiles_n;
+    const int g = t / per_group;
+    const int first_m = g * group_m;
+    const int gsize = min(tiles_m - first_m, group_m);
+    const int r = t - g * per_group;
+    tm = first_m + r % gsize;
+    tn = r / gsize;
+  }
+};
+
+// Shared-memory offset of the K-major or MN-major operand tile for MMA step kk
+// (each step consumes 32 bytes of K).
+template <bool MN, int ESZ>
+__device__ __forceinline__ uint32_t kstep_offset(int kk) {
+  // K-major: advance 32 bytes inside the 128-byte swizzled row.
+  // MN-major: advance (32/ESZ) K rows of 128 bytes each.
+  return MN ? (uint32_t)kk * (32 / ESZ) * 128 : (uint32_t)kk * 32;
+}
+
+template <bool TF32, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                   GemmArgs args) {
+  using Cfg = GemmCfg<TF32>;
+  constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;        // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  WaitCtx wc{abort_flag, args.err};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (TF32) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmB2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const TileSched sched{args.tiles_m, args.tiles_n, args.group_m};
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int nk = (args.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one_lane()) {
+      uint32_t fill = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int tm, tn;
+        sched.coords(t, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < nk; ++kb, ++fill) {
+          const int s = fill % STAGES;
+          const uint32_t round = fill / STAGES;
+          if (!mbar_wait(&empty_bar[s], (round & 1) ^ 1, wc)) break;
+          uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::PLANES * Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[s], Cfg::STAGE_BYTES);
+          const int k0 = kb * BK;
+#pragma unroll
+          for (int p = 0; p < Cfg::PLANES; ++p) {
+            const CUtensorMap* ma = p == 0 ? &tmA : &tmA2;
+            const CUtensorMap* mb = p == 0 ? &tmB : &tmB2;
+            uint8_t* pa = sa + p * Cfg::A_BYTES;
+            uint8_t* pb = sb + p * Cfg::B_BYTES;
+            if (A_MN) {
+#pragma unroll
+              for (int c = 0; c < BM / Cfg::CHUNK; ++c)
+                tma_load_2d(pa + c * BK * 128, ma, &full_bar[s], m0 + c * Cfg::CHUNK, k0);
+            } else {
+              tma_load_2d(pa, ma, &full_bar[s], k0, m0);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int c = 0; c < BN / Cfg::CHUNK; ++c)
+                tma_load_2d(pb + c * BK * 128, mb, &full_bar[s], n0 + c * Cfg::CHUNK, k0);
+            } else {
+              tma_load_2d(pb, mb, &full_bar[s], k0, n0);
+            }
+          }
+        }
+        if (*abort_flag) break;
+      }
+      // Teardown: every stage we filled must have landed before we leave.
+      const uint32_t first = fill > (uint32_t)STAGES ? fill - STAGES : 0;
+      for (uint32_t f = first; f < fill; ++f) mbar_drain(&full_bar[f % STAGES], (f / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = make_idesc(Cfg::FMT, A_MN ? 1u : 0u, B_MN ? 1u : 0u, BM, BN);
+    const uint32_t a_lbo = A_MN ? BK * 128 : 16, b_lbo = B_MN ? BK * 128 : 16;
+    if (elect_one_lane()) {
+      uint32_t fill = 0, use = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++use) {
+        const int buf = use & 1;
+        if (!mbar_wait(&acce_bar[buf], ((use >> 1) & 1) ^ 1, wc)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++fill) {
+          const int s = fill % STAGES;
+          if (!mbar_wait(&full_bar[s], (fill / STAGES) & 1, wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::PLANES * Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / Cfg::MMA_K; ++kk) {
+            const uint32_t ao = kstep_offset<A_MN, Cfg::ESZ>(kk), bo = kstep_offset<B_MN, Cfg::ESZ>(kk);
+            const uint64_t adesc = sw128_desc(sa + ao, a_lbo, 1024);
+            const uint64_t bdesc = sw128_desc(sb + bo, b_lbo, 1024);
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            if (TF32) {
+              const uint64_t adesc_lo = sw128_desc(sa + Cfg::A_BYTES + ao, a_lbo, 1024);
+              const uint64_t bdesc_lo = sw128_desc(sb + Cfg::B_BYTES + bo, b_lbo, 1024);
+              // small terms first, then the dominant hi.hi product
+              mma_tf32_ss(d_tmem, adesc_lo, bdesc, idesc, acc);
+              mma_tf32_ss(d_tmem, adesc, bdesc_lo, idesc, 1u);
+              mma_tf32_ss(d_tmem, adesc, bdesc, idesc, 1u);
+            } else {
+              mma_f16_ss(d_tmem, adesc, bdesc, idesc, acc);
+            }
+          }
+          tc_commit(&empty_bar[s]);  // stage is free once these MMAs have read it
+        }
+        if (!ok) break;
+        tc_commit(&accf_bar[buf]);  // accumulator ready for the epilogue
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    uint32_t use = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++use) {
+      const int buf = use & 1;
+      if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
+      tc_fence_after();
+      int tm, tn;
+      sched.coords(t, tm, tn);
+      const int m = tm * BM + row_in_tile;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_ld_wait();
+        const int n0 = tn * BN + c;
+        if (m < args.M && n0 < args.N) gemm_store_row32(args, m, n0, reinterpret_cast<float*>(r));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3xTF32 operand split: hi = x with the low 13 mantissa bits cleared (exactly
+// representable in tf32), lo = x - hi (exact in fp32). The planes are always
+// written K-major ([rows][kpad], kpad = K rounded up to 4 with zero fill), so
+// the tf32 MMA only ever reads K-major tiles: 32-bit MN-major operands would
+// need the 32-byte-atom swizzle, which the plain 128B TMA swizzle does not
+// produce. `src_t` = the source is stored [K][rows] (transposed); a 32x32
+// shared-memory tile keeps both the read and the write coalesced.
+// ---------------------------------------------------------------------------
+__global__ void split_tf32_kernel(const float* __restrict__ x, int rows, int K, int ld, int src_t,
+                                  float* __restrict__ hi, float* __restrict__ lo, int kpad) {
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  for (int i = ty; i < 32; i += 8) {
+    float v = 0.f;
+    if (src_t) {  // coalesced along rows: x[k*ld + r]
+      const int k = k0 + i, r = r0 + tx;
+      if (k < K && r < rows) v = x[(long long)k * ld + r];
+      tile[tx][i] = v;
+    } else {      // coalesced along K: x[r*ld + k]
+      const int r = r0 + i, k = k0 + tx;
+      if (k < K && r < rows) v = x[(long long)r * ld + k];
+      tile[i][tx] = v;
+    }
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, k = k0 + tx;
+    if (r < rows && k < kpad) {
+      const float v = tile[i][tx];
+      const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+      hi[(long long)r * kpad + k] = h;
+      lo[(long long)r * kpad + k] = v - h;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SIMT fallback/FFMA kernel: any shape, stride or alignment. Used for the
+// "FFMA" f32 mode and for operands TMA cannot describe (row pitch not a
+// multiple of 16 bytes). 64x64 output tile per 256-thread block, 4x4 per
+// thread, fp32 accumulate.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p) {
+  if constexpr (sizeof(T) == 2)
+    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(p));
+  else
+    return *p;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
+                                                        GemmArgs args) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < args.K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int kk = i / 64, mm = i % 64;
+      const int m = m0 + mm, k = k0 + kk;
+      float va = 0.f, vb = 0.f;
+      if (m < args.M && k < args.K)
+        va = ldf(A + (args.transA ? (long long)k * args.lda + m : (long long)m * args.lda + k));
+      const int n = n0 + mm;
+      if (n < args.N && k < args.K)
+        vb = ldf(B + (args.transB ? (long long)n * args.ldb + k : (long long)k * args.ldb + n));
+      As[kk][mm] = va;
+      Bs[kk][mm] = vb;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= args.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n < args.N) gemm_store_one(args, m, n, acc[i][j]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static bool encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esz, uint64_t inner,
+                      uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = get_tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_pitch_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  (void)esz;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Operand descriptor: logical [rows(MN), K] operand, stored either K-major
+// (row r at base + r*ld, K contiguous) or MN-major (K row k at base + k*ld).
+template <bool TF32>
+static bool make_operand_map(CUtensorMap* map, const void* base, bool mn_major, int mn, int K, int ld,
+                             int box_mn) {
+  using Cfg = GemmCfg<TF32>;
+  const CUtensorMapDataType dt = TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t pitch = (uint64_t)ld * Cfg::ESZ;
+  if (mn_major) return encode_2d(map, base, dt, Cfg::ESZ, (uint64_t)mn, (uint64_t)K, pitch, Cfg::CHUNK, Cfg::BK);
+  return encode_2d(map, base, dt, Cfg::ESZ, (uint64_t)K, (uint64_t)mn, pitch, Cfg::BK, box_mn);
+}
+
+int gemm_tc_supported(const GemmArgs& a, int esz, const void* A, const void* B) {
+  // TMA wants 16-byte aligned bases and row pitches that are multiples of 16 bytes.
+  if (((uintptr_t)A & 15) || ((uintptr_t)B & 15)) return 0;
+  if (((long long)a.lda * esz) % 16 || ((long long)a.ldb * esz) % 16) return 0;
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+  return 1;
+}
+
+template <bool TF32, bool A_MN, bool B_MN>
+static cudaError_t launch_tc(const GemmArgs& args, const void* A, const void* B, const void* A2, const void* B2,
+                             cudaStream_t stream) {
+  using Cfg = GemmCfg<TF32>;
+  CUtensorMap ma{}, mb{}, ma2{}, mb2{};
+  if (!make_operand_map<TF32>(&ma, A, A_MN, args.M, args.K, args.lda, Cfg::BM)) return cudaErrorInvalidValue;
+  if (!make_operand_map<TF32>(&mb, B, B_MN, args.N, args.K, args.ldb, Cfg::BN)) return cudaErrorInvalidValue;
+  if (TF32) {
+    if (!make_operand_map<TF32>(&ma2, A2, A_MN, args.M, args.K, args.lda, Cfg::BM)) return cudaErrorInvalidValue;
+    if (!make_operand_map<TF32>(&mb2, B2, B_MN, args.N, args.K, args.ldb, Cfg::BN)) return cudaErrorInvalidValue;
+  } else {
+    ma2 = ma;
+    mb2 = mb;
+  }
+  GemmArgs a = args;
+  a.tiles_m = (args.M + Cfg::BM - 1) / Cfg::BM;
+  a.tiles_n = (args.N + Cfg::BN - 1) / Cfg::BN;
+  a.group_m = 16;
+  auto kern = gemm_tc_kernel<TF32, A_MN, B_MN>;
+  static bool attr_done = false;  // per template instantiation
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, a);
+  return cudaGetLastError();
+}
+
+template <bool TF32>
+static cudaError_t dispatch_tc(const GemmArgs& args, const void* A, const void* B, const void* A2, const void* B2,
+                               cudaStream_t s) {
+  // A is MN-major when stored transposed ([K,M]); B is MN-major when stored
+  // as [K,N] (the plain row-major right operand of `@`).
+  const bool a_mn = args.transA != 0, b_mn = args.transB == 0;
+  if (!a_mn && !b_mn) return launch_tc<TF32, false, false>(args, A, B, A2, B2, s);
+  if (!a_mn && b_mn) return launch_tc<TF32, false, true>(args, A, B, A2, B2, s);
+  if (a_mn && !b_mn) return launch_tc<TF32, true, false>(args, A, B, A2, B2, s);
+  return launch_tc<TF32, true, true>(args, A, B, A2, B2, s);
+}
+
+cudaError_t gemm_bf16_tc(const GemmArgs& args, const void* A, const void* B, cudaStream_t s) {
+  return dispatch_tc<false>(args, A, B, nullptr, nullptr, s);
+}
+
+static int kpad4(int K) { return (K + 3) & ~3; }
+
+size_t gemm_f32_scratch_floats(const GemmArgs& a) {
+  const size_t kp = (size_t)kpad4(a.K);
+  return 2 * ((size_t)a.M * kp + (size_t)a.N * kp);
+}
+
+cudaError_t gemm_f32_3xtf32(const GemmArgs& args, const float* A, const float* B, float* scratch,
+                            cudaStream_t s) {
+  const int kp = kpad4(args.K);
+  float* a_hi = scratch;
+  float* a_lo = a_hi + (size_t)args.M * kp;
+  float* b_hi = a_lo + (size_t)args.M * kp;
+  float* b_lo = b_hi + (size_t)args.N * kp;
+  dim3 ga((kp + 31) / 32, (args.M + 31) / 32), gb((kp + 31) / 32, (args.N + 31) / 32);
+  split_tf32_kernel<<<ga, 256, 0, s>>>(A, args.M, args.K, args.lda, args.transA, a_hi, a_lo, kp);
+  split_tf32_kernel<<<gb, 256, 0, s>>>(B, args.N, args.K, args.ldb, !args.transB, b_hi, b_lo, kp);
+  GemmArgs a = args;
+  a.K = kp;  // zero-filled tail contributes nothing
+  a.lda = kp;
+  a.ldb = kp;
+  a.transA = 0;
+  a.transB = 1;
+  return launch_tc<true, false, false>(a, a_hi, b_hi, a_lo, b_lo, s);
+}
+
+cudaError_t gemm_simt(const GemmArgs& args, const void* A, const void* B, int bf16_in, cudaStream_t s) {
+  dim3 grid((args.N + 63) / 64, (args.M + 63) / 64);
+  if (bf16_in)
+    gemm_simt_kernel<uint16_t><<<grid, 256, 0, s>>>((const uint16_t*)A, (const uint16_t*)B, args);
+  else
+    gemm_simt_kernel<float><<<grid, 256, 0, s>>>((const float*)A, (const float*)B, args);
+  return cudaGetLastError();
+}
+
+}  // namespace dgx

@@ -1,0 +1,108 @@
+// Internal interface of the GEMM kernels (not part of the public C ABI).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "common.h"
+#include "sm100.cuh"
+
+namespace dgx {
+
+struct GemmArgs {
+  int M, N, K;
+  int lda, ldb, ldc;
+  int transA, transB;      // A stored [K,M] / B stored [N,K]
+  void* C;
+  int c_bf16;              // output element type: 0 fp32, 1 bf16
+  const float* bias;       // [N] or null
+  int relu;
+  float beta;              // C = beta*C + op(A).op(B) (+bias)
+  uint32_t* err;           // device error word
+  int tiles_m, tiles_n, group_m;  // filled by the launcher
+};
+
+__device__ __forceinline__ float gemm_finish(const GemmArgs& a, int n, float acc, float old) {
+  float v = acc;
+  if (a.beta != 0.f) v = fmaf(a.beta, old, v);
+  if (a.bias) v += a.bias[n];
+  if (a.relu) v = fmaxf(v, 0.f);
+  return v;
+}
+
+__device__ __forceinline__ void gemm_store_one(const GemmArgs& a, int m, int n, float acc) {
+  const long long off = (long long)m * a.ldc + n;
+  if (a.c_bf16) {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(a.C) + off;
+    const float old = a.beta != 0.f ? __bfloat162float(*c) : 0.f;
+    *c = __float2bfloat16_rn(gemm_finish(a, n, acc, old));
+  } else {
+    float* c = reinterpret_cast<float*>(a.C) + off;
+    const float old = a.beta != 0.f ? *c : 0.f;
+    *c = gemm_finish(a, n, acc, old);
+  }
+}
+
+// Store 32 consecutive accumulator columns [n0, n0+32) of row m.
+__device__ __forceinline__ void gemm_store_row32(const GemmArgs& a, int m, int n0, const float* v) {
+  const int nvalid = a.N - n0;
+  const long long off = (long long)m * a.ldc + n0;
+  if (!a.c_bf16) {
+    float* row = reinterpret_cast<float*>(a.C) + off;
+    if (nvalid >= 32 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.beta != 0.f) old = *reinterpret_cast<const float4*>(row + j);
+        float4 o;
+        o.x = gemm_finish(a, n0 + j + 0, v[j + 0], old.x);
+        o.y = gemm_finish(a, n0 + j + 1, v[j + 1], old.y);
+        o.z = gemm_finish(a, n0 + j + 2, v[j + 2], old.z);
+        o.w = gemm_finish(a, n0 + j + 3, v[j + 3], old.w);
+        *reinterpret_cast<float4*>(row + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) {
+          const float old = a.beta != 0.f ? row[j] : 0.f;
+          row[j] = gemm_finish(a, n0 + j, v[j], old);
+        }
+    }
+  } else {
+    __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(a.C) + off;
+    if (nvalid >= 32 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 oldv = make_uint4(0, 0, 0, 0);
+        if (a.beta != 0.f) oldv = *reinterpret_cast<const uint4*>(row + j);
+        const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&oldv);
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float x0 = gemm_finish(a, n0 + j + 2 * h, v[j + 2 * h], __bfloat162float(ob[2 * h]));
+          const float x1 = gemm_finish(a, n0 + j + 2 * h + 1, v[j + 2 * h + 1], __bfloat162float(ob[2 * h + 1]));
+          w[h] = pack_bf16x2(x0, x1);
+        }
+        *reinterpret_cast<uint4*>(row + j) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) {
+          const float old = a.beta != 0.f ? __bfloat162float(row[j]) : 0.f;
+          row[j] = __float2bfloat16_rn(gemm_finish(a, n0 + j, v[j], old));
+        }
+    }
+  }
+}
+
+int gemm_tc_supported(const GemmArgs& a, int esz, const void* A, const void* B);
+cudaError_t gemm_bf16_tc(const GemmArgs& args, const void* A, const void* B, cudaStream_t s);
+size_t gemm_f32_scratch_floats(const GemmArgs& a);
+cudaError_t gemm_f32_3xtf32(const GemmArgs& args, const float* A, const float* B, float* scratch,
+                            cudaStream_t s);
+cudaError_t gemm_simt(const GemmArgs& args, const void* A, const void* B, int bf16_in, cudaStream_t s);
+
+}  // namespace dgx

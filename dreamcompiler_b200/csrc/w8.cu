@@ -1,0 +1,220 @@
+// int8 weight-only dense layer on sm_100a.
+//
+// Replaces the export-only int8 path of the reference: the quantiser and the
+// emitted dense_q of export_c_header_int8 (runtime/nn/training.inc:3668-3752),
+// y[j] = b[j] + sum_k scale*w[j,k]*x[k] in fp32, generalised to a per-output-
+// channel scale and a batch of rows, and run on the device.
+//
+// At the batch sizes the int8 export serves (1..256 rows) the layer streams
+// a [N][K] int8 weight matrix once per call, so the kernel is laid out for
+// HBM: each warp owns two output channels and reads their weight rows with
+// 16-byte loads (16 int8 per lane per step, 512 B per warp per step), the
+// activations come through L1, and the batch is tiled 8 rows per block so a
+// weight byte is loaded once per 8 rows.
+//   mode 0 (W8A32): fp32 products and sums, then y = b + scale*acc.
+//   mode 1 (W8A8) : activations pre-quantised per row (dgx_quantize_rows_i8),
+//                   exact int32 dot products with dp4a, y = b + scale*sx*acc.
+#include "common.h"
+
+namespace dgx {
+
+namespace {
+constexpr int CPW = 2;       // output channels per warp
+constexpr int WARPS = 8;
+constexpr int BT = 8;        // batch rows per block
+constexpr int KSTEP = 512;   // K consumed by one warp step (32 lanes x 16)
+
+__device__ __forceinline__ float4 ld4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+template <int MODE>
+__global__ void __launch_bounds__(256) w8_kernel(const void* __restrict__ X, const int8_t* __restrict__ W,
+                                                 const float* __restrict__ scale, const float* __restrict__ bias,
+                                                 const float* __restrict__ sx, float* __restrict__ Y,
+                                                 int32_t* __restrict__ acc_out, int B, int N, int K) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = (blockIdx.x * WARPS + warp) * CPW;
+  const int b0 = blockIdx.y * BT;
+  const int nb = min(BT, B - b0);
+  if (n0 >= N) return;
+  float facc[CPW][BT];
+  int iacc[CPW][BT];
+#pragma unroll
+  for (int c = 0; c < CPW; ++c)
+#pragma unroll
+    for (int b = 0; b < BT; ++b) {
+      facc[c][b] = 0.f;
+      iacc[c][b] = 0;
+    }
+  const bool vec = (K % 16) == 0;
+  for (int k0 = 0; k0 < K; k0 += KSTEP) {
+    const int k = k0 + lane * 16;
+    if (k >= K) continue;
+    int4 w[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      if (n0 + c < N && vec) {
+        w[c] = __ldg(reinterpret_cast<const int4*>(W + (size_t)(n0 + c) * K + k));
+      } else {
+        int8_t t[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) t[u] = (n0 + c < N && k + u < K) ? W[(size_t)(n0 + c) * K + k + u] : 0;
+        w[c] = *reinterpret_cast<int4*>(t);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < BT; ++b) {
+      if (b >= nb) break;
+      if (MODE == 0) {
+        const float* xr = reinterpret_cast<const float*>(X) + (size_t)(b0 + b) * K + k;
+        float xv[16];
+        if (vec) {
+#pragma unroll
+          for (int u = 0; u < 16; u += 4) *reinterpret_cast<float4*>(&xv[u]) = ld4(xr + u);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 16; ++u) xv[u] = (k + u < K) ? xr[u] : 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) {
+          const int8_t* wb = reinterpret_cast<const int8_t*>(&w[c]);
+          float s = facc[c][b];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) s = fmaf((float)wb[u], xv[u], s);
+          facc[c][b] = s;
+        }
+      } else {
+        const int8_t* xr = reinterpret_cast<const int8_t*>(X) + (size_t)(b0 + b) * K + k;
+        int4 xv;
+        if (vec) {
+          xv = __ldg(reinterpret_cast<const int4*>(xr));
+        } else {
+          int8_t t[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) t[u] = (k + u < K) ? xr[u] : 0;
+          xv = *reinterpret_cast<int4*>(t);
+        }
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) {
+          int s = iacc[c][b];
+          s = __dp4a(w[c].x, xv.x, s);
+          s = __dp4a(w[c].y, xv.y, s);
+          s = __dp4a(w[c].z, xv.z, s);
+          s = __dp4a(w[c].w, xv.w, s);
+          iacc[c][b] = s;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < CPW; ++c) {
+    const int n = n0 + c;
+#pragma unroll
+    for (int b = 0; b < BT; ++b) {
+      if (MODE == 0) {
+        float v = facc[c][b];
+#pragma unroll
+        for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0 && n < N && b < nb) Y[(size_t)(b0 + b) * N + n] = (bias ? bias[n] : 0.f) + scale[n] * v;
+      } else {
+        int v = iacc[c][b];
+#pragma unroll
+        for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0 && n < N && b < nb) {
+          if (acc_out) acc_out[(size_t)(b0 + b) * N + n] = v;
+          if (Y) Y[(size_t)(b0 + b) * N + n] = (bias ? bias[n] : 0.f) + scale[n] * sx[b0 + b] * (float)v;
+        }
+      }
+    }
+  }
+}
+
+// Per-row symmetric quantisation: sx = max|x|/127, q = clamp(round(x/sx)).
+__global__ void quant_rows_kernel(const float* __restrict__ X, int8_t* __restrict__ Xq, float* __restrict__ sx,
+                                  int K) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const float* x = X + (size_t)b * K;
+  float m = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(x[k]));
+#pragma unroll
+  for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (threadIdx.x == 0) red[0] = m;
+  }
+  __syncthreads();
+  m = red[0];
+  const float s = m > 0.f ? m / 127.f : 1.f;
+  const float inv = 1.f / s;
+  if (threadIdx.x == 0) sx[b] = s;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    float v = roundf(x[k] * inv);
+    v = fminf(127.f, fmaxf(-127.f, v));
+    Xq[(size_t)b * K + k] = (int8_t)v;
+  }
+}
+}  // namespace
+
+cudaError_t w8_gemm(const void* X, const int8_t* W, const float* scale, const float* bias, const float* sx,
+                    float* Y, int32_t* acc, int B, int N, int K, int mode, cudaStream_t s) {
+  dim3 grid((N + WARPS * CPW - 1) / (WARPS * CPW), (B + BT - 1) / BT);
+  if (mode == 0)
+    w8_kernel<0><<<grid, 256, 0, s>>>(X, W, scale, bias, sx, Y, acc, B, N, K);
+  else
+    w8_kernel<1><<<grid, 256, 0, s>>>(X, W, scale, bias, sx, Y, acc, B, N, K);
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_rows(const float* X, int8_t* Xq, float* sx, int B, int K, cudaStream_t s) {
+  quant_rows_kernel<<<B, 256, 0, s>>>(X, Xq, sx, K);
+  return cudaGetLastError();
+}
+
+}  // namespace dgx
+
+using namespace dgx;
+
+extern "C" {
+
+dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, int K, void* stream) {
+  if (B < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_quantize_rows_i8: negative size");
+  if (B == 0) return DGX_OK;
+  if (!X || !Xq || !sx) return set_error(DGX_EINVAL, "dgx_quantize_rows_i8: null pointer");
+  return cuda_status(quantize_rows(X, Xq, sx, B, K, (cudaStream_t)stream), "dgx_quantize_rows_i8");
+}
+
+dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream) {
+  if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: negative size");
+  if (B == 0 || N == 0) return DGX_OK;
+  if (!Xq || !W || !acc) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: null pointer");
+  if (((uintptr_t)Xq | (uintptr_t)W) & 15) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: pointers must be 16-byte aligned");
+  return cuda_status(w8_gemm(Xq, W, nullptr, nullptr, nullptr, nullptr, acc, B, N, K, 1, (cudaStream_t)stream),
+                     "dgx_gemm_i8i32");
+}
+
+dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y, int B,
+                       int N, int K, int mode, void* stream) {
+  if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_w8: negative size");
+  if (mode != 0 && mode != 1) return set_error(DGX_EINVAL, "dgx_gemm_w8: mode %d", mode);
+  if (B == 0 || N == 0) return DGX_OK;
+  if (!X || !W || !scale || !Y) return set_error(DGX_EINVAL, "dgx_gemm_w8: null pointer");
+  if (((uintptr_t)X | (uintptr_t)W) & 15) return set_error(DGX_EINVAL, "dgx_gemm_w8: X and W must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (mode == 0)
+    return cuda_status(w8_gemm(X, W, scale, bias, nullptr, Y, nullptr, B, N, K, 0, s), "dgx_gemm_w8");
+  // W8A8: quantised activations + row scales in library scratch.
+  const size_t xq_bytes = ((size_t)B * K + 255) & ~size_t(255);
+  uint8_t* ws = (uint8_t*)library_scratch(xq_bytes + (size_t)B * sizeof(float), s);
+  if (!ws) return set_error(DGX_ENOMEM, "dgx_gemm_w8: scratch");
+  int8_t* xq = reinterpret_cast<int8_t*>(ws);
+  float* sx = reinterpret_cast<float*>(ws + xq_bytes);
+  cudaError_t e = quantize_rows(X, xq, sx, B, K, s);
+  if (e != cudaSuccess) return cuda_status(e, "dgx_gemm_w8 quantize");
+  return cuda_status(w8_gemm(xq, W, scale, bias, sx, Y, nullptr, B, N, K, 1, s), "dgx_gemm_w8");
+}
+
+}  // extern "C"

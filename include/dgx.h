@@ -1,0 +1,150 @@
+/*
+ * libdgx — the C ABI between the Dream tensor runtime and its B200 (sm_100a)
+ * kernels. Plain pointers, sizes and status codes only; no C++ or torch types.
+ *
+ * All tensors are row-major and live in device memory unless a function says
+ * otherwise. Every call is asynchronous on `stream` (a cudaStream_t, NULL for
+ * the legacy default stream) and returns a status; on failure
+ * dgx_last_error() holds a one-line message for the calling thread. No call
+ * throws, aborts or falls back to the CPU.
+ *
+ * Each entry point names the reference interface it replaces
+ * (heellowdsf/DreamCompiler, paths relative to the project root).
+ */
+#ifndef DGX_H_
+#define DGX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  DGX_OK = 0,
+  DGX_EINVAL = 1,        /* bad argument (null pointer, negative size, bad enum) */
+  DGX_ECUDA = 2,         /* a CUDA runtime call failed */
+  DGX_ENCCL = 3,         /* a collective or peer-memory step failed */
+  DGX_ETIMEOUT = 4,      /* a bounded device or host wait ran out */
+  DGX_EUNSUPPORTED = 5,  /* shape/type combination this build does not handle */
+  DGX_ENOMEM = 6,        /* workspace too small or allocation failed */
+} dgx_status;
+
+typedef enum { DGX_F32 = 0, DGX_BF16 = 1, DGX_I8 = 2 } dgx_dtype;
+
+enum { DGX_EPI_NONE = 0, DGX_EPI_BIAS = 1, DGX_EPI_BIAS_RELU = 2, DGX_EPI_RELU = 3 };
+enum { DGX_F32_3XTF32 = 0, DGX_F32_FFMA = 1 };
+
+/* Library identification and error reporting. */
+const char* dgx_version(void);
+const char* dgx_last_error(void);
+
+/* Select and initialise a device for the calling thread.
+ * Replaces initBackend() (runtime/backend/gpu.inc:313-361): no OpenCL/cuBLAS
+ * probing and no CPU/GPU threshold (gpu.inc:293-307); the device always runs. */
+dgx_status dgx_init(int device);
+
+/* Wait for `stream`, then read and clear the device error word that bounded
+ * waits in the kernels report into. DGX_ETIMEOUT if any wait ran out. */
+dgx_status dgx_sync_check(void* stream);
+
+/*
+ * C[M,N] = beta*C + op(A)[M,K] . op(B)[K,N] (+bias[N]) (ReLU)
+ *   A stored [M,K] (transA=0) or [K,M] (transA=1), row pitch lda elements
+ *   B stored [K,N] (transB=0) or [N,K] (transB=1), row pitch ldb elements
+ *   ab_type: DGX_BF16 (tcgen05 kind::f16) or DGX_F32 (f32_mode 3xTF32 on
+ *            tcgen05 kind::tf32, or FFMA); accumulation is always fp32
+ *   c_type : DGX_F32 or DGX_BF16
+ *   epilogue: DGX_EPI_* (bias is required for the BIAS forms)
+ *   workspace: device scratch for the 3xTF32 split planes, at least
+ *            dgx_gemm_workspace_size() bytes; NULL lets the library use its
+ *            own per-device buffer.
+ * Replaces: tensor_matmul (runtime/ops/elementwise.inc:971-1213) incl. the
+ * f32 mirror path dream_gemm_f32 (:689-738) and cuBLAS Sgemm/GemmEx (:1046-1090);
+ * the "matmul" backward dA = dY.B^T (transB=1, beta=1) and dB = A^T.dY
+ * (transA=1, beta=1) (runtime/ops/autograd.inc:91-125); dream_linear /
+ * dream_linear_relu Y = X.W^T + b (transB=1, epilogue BIAS[_RELU])
+ * (runtime/ops/elementwise.inc:1432-1521).
+ */
+dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb, int ldc,
+                    int transA, int transB, dgx_dtype ab_type, dgx_dtype c_type, int f32_mode, const float* bias,
+                    int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream);
+size_t dgx_gemm_workspace_size(int M, int N, int K, int transA, int transB, dgx_dtype ab_type, int f32_mode);
+
+/*
+ * Batched GEMM C_b = A_b . B_b over `batch` contiguous [M,K] x [K,N] blocks.
+ * Replaces dream_bmm (runtime/ops/elementwise.inc:1218-1252).
+ */
+dgx_status dgx_bmm(const void* A, const void* B, void* C, int batch, int M, int N, int K, dgx_dtype ab_type,
+                   dgx_dtype c_type, void* stream);
+
+/*
+ * FlashAttention forward. Q, K, V, O: [BH][S][D] (heads folded into the batch,
+ * as dream_flash_attention's `(B, S*dk)` layout), dtype DGX_BF16.
+ * LSE [BH][S] fp32 receives the natural-log row log-sum-exp of scale*QK^T
+ * (may be NULL when no backward follows). causal=1 masks j > i.
+ * Replaces dream_flash_attention (runtime/nn/training.inc:284-401) and its
+ * OpenCL kernel flash_attention_v1 (:310-363).
+ */
+dgx_status dgx_flash_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int BH, int S, int D,
+                         float scale, int causal, dgx_dtype dtype, void* stream);
+
+/*
+ * FlashAttention backward: dQ, dK, dV ([BH][S][D], dtype) from Q, K, V, O, dO
+ * and the forward's LSE. workspace: at least dgx_flash_bwd_workspace_size()
+ * bytes of device scratch (fp32 dQ accumulator and the row terms
+ * D_i = dO_i . O_i); NULL lets the library use its own per-device buffer.
+ * Replaces the "flash_attention" backward branch
+ * (runtime/ops/autograd.inc:779-840), without its 3-pass recompute.
+ */
+dgx_status dgx_flash_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                         const float* LSE, void* dQ, void* dK, void* dV, int BH, int S, int D, float scale,
+                         int causal, dgx_dtype dtype, void* workspace, size_t workspace_bytes, void* stream);
+size_t dgx_flash_bwd_workspace_size(int BH, int S, int D);
+
+/*
+ * int8 weight-only dense layer, Y[B,N] = bias[N] + scale[n] * sum_k W[n,k] * X[b,k].
+ *   W int8 [N][K] (row n = output channel, the dense_q layout), scale [N] fp32
+ *   per output channel (a per-tensor scale is N copies of one value), bias [N]
+ *   or NULL, X [B][K] fp32, Y [B][N] fp32.
+ *   mode 0 (W8A32): fp32 products and accumulation, the arithmetic of the
+ *          exported dense_q (runtime/nn/training.inc:3738-3752).
+ *   mode 1 (W8A8): X quantised per row (sx = max|x|/127, round half away from
+ *          zero, clamp [-127,127]), exact int32 accumulation, then
+ *          Y = bias + scale[n]*sx[b]*acc.
+ * Replaces the export-only int8 path dense_q / export_c_header_int8
+ * (runtime/nn/training.inc:3492-3817) with an on-device kernel.
+ */
+dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y, int B,
+                       int N, int K, int mode, void* stream);
+/* Exact int32 accumulators acc[b,n] = sum_k Xq[b,k]*W[n,k] (the W8A8 core). */
+dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream);
+/* Per-row symmetric quantisation used by mode 1: Xq = clamp(round(X/sx)), sx = max|X_b|/127. */
+dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, int K, void* stream);
+
+/*
+ * Column-parallel tensor-parallel GEMM over `world` GPUs, one process per GPU.
+ * Each rank holds all of A [M,K] and its column shard of B ([K, n_r] with the
+ * reference's widths: base = N/world, the first N%world shards one wider).
+ * The GEMM epilogue writes every output tile straight into C_full [M,N] on
+ * every rank through NVLink peer stores, so the all-gather overlaps the GEMM
+ * tile by tile; the call returns after a bounded cross-rank completion flag.
+ * Replaces dream_tp_matmul_column (runtime/nn/training.inc:1604-1630), whose
+ * "all-gather" is a host copy into Y[:, col:col+ncol].
+ */
+/* Shard width and first column of `rank`, as dream_tp_matmul_column computes them. */
+void dgx_tp_shard(int N, int world, int rank, int* col0, int* ncol);
+/* Export this rank's C_full + flag buffers as an opaque handle (for exchange). */
+dgx_status dgx_tp_export(void* C_full, size_t c_bytes, void* handle_out, size_t handle_bytes);
+size_t dgx_tp_handle_size(void);
+/* Open all ranks' handles (handles: world * dgx_tp_handle_size() bytes). */
+dgx_status dgx_tp_open(int rank, int world, const void* handles);
+dgx_status dgx_tp_gemm_colsplit(const void* A, const void* B_shard, int M, int N, int K, dgx_dtype ab_type,
+                                dgx_dtype c_type, int timeout_ms, void* stream);
+dgx_status dgx_tp_close(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DGX_H_ */
