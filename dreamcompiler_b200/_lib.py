@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdgx.so")
 
 DGX_OK, DGX_EINVAL, DGX_ECUDA, DGX_ENCCL, DGX_ETIMEOUT, DGX_EUNSUPPORTED, DGX_ENOMEM = range(7)
-DGX_F32, DGX_BF16, DGX_I8 = 0, 1, 2
+DGX_F32, DGX_BF16, DGX_I8, DGX_F64 = 0, 1, 2, 3
 DGX_EPI_NONE, DGX_EPI_BIAS, DGX_EPI_BIAS_RELU, DGX_EPI_RELU = 0, 1, 2, 3
 DGX_F32_3XTF32, DGX_F32_FFMA = 0, 1
 
@@ -36,6 +36,7 @@ SIGNATURES = {
     "dgx_last_error": (C.c_char_p, []),
     "dgx_init": (_i, [_i]),
     "dgx_sync_check": (_i, [_vp]),
+    "dgx_convert": (_i, [_vp, _i, _vp, _i, _sz, _i, _vp]),
     "dgx_gemm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _f, _vp, _sz, _vp]),
     "dgx_gemm_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
     "dgx_bmm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),

@@ -69,19 +69,32 @@ def build_libdgx(verbose: bool = False, ptxas_verbose: bool = False) -> str:
     return LIBDGX
 
 
+# Flags `dream run` compiles the reference runtime with (src/main.cpp:994);
+# used for the runtime files that must reproduce its floating-point results
+# bit for bit (the seeded RNG), named *_fastmath.cpp.
+REF_FLAGS = ["-O3", "-ffast-math", "-mavx2", "-mfma", "-fno-math-errno"]
+
+
 def build_runtime(verbose: bool = False) -> str:
     srcs = sorted(glob.glob(os.path.join(RTSRC, "*.cpp")))
     if not srcs:
         return ""
     deps = srcs + sorted(glob.glob(os.path.join(RTSRC, "*.h")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
     if _newer(LIBRT, deps + [LIBDGX]):
-        cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-I" + os.path.join(ROOT, "include"),
-               "-I" + os.path.join(CUDA_HOME, "include")] + srcs + [
-            "-o", LIBRT, "-L" + HERE, "-ldgx", "-Wl,-rpath,$ORIGIN",
-            "-L" + os.path.join(CUDA_HOME, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA_HOME, "lib64")]
-        if verbose:
-            print(" ".join(cmd))
-        _run(cmd)
+        os.makedirs(BUILD, exist_ok=True)
+        objs = []
+        for s in srcs:
+            o = os.path.join(BUILD, os.path.basename(s) + ".o")
+            flags = REF_FLAGS if s.endswith("_fastmath.cpp") else ["-O2"]
+            cmd = ["g++", "-std=c++17", "-fPIC", "-Wall", "-I" + os.path.join(ROOT, "include"),
+                   "-I" + os.path.join(CUDA_HOME, "include")] + flags + ["-c", s, "-o", o]
+            if verbose:
+                print(" ".join(cmd))
+            _run(cmd)
+            objs.append(o)
+        _run(["g++", "-shared", "-o", LIBRT] + objs + [
+            "-L" + HERE, "-ldgx", "-Wl,-rpath,$ORIGIN",
+            "-L" + os.path.join(CUDA_HOME, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA_HOME, "lib64")])
     return LIBRT
 
 

@@ -157,7 +157,7 @@ dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, 
                     int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream) {
   if (M < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm: negative size %dx%dx%d", M, N, K);
   if (M == 0 || N == 0) return DGX_OK;
-  if (!A || !B || !C) return set_error(DGX_EINVAL, "dgx_gemm: null operand");
+  if (!C || (K > 0 && (!A || !B))) return set_error(DGX_EINVAL, "dgx_gemm: null operand");
   if (ab_type != DGX_F32 && ab_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gemm: ab_type %d", ab_type);
   if (c_type != DGX_F32 && c_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gemm: c_type %d", c_type);
   if (epilogue < DGX_EPI_NONE || epilogue > DGX_EPI_RELU) return set_error(DGX_EINVAL, "dgx_gemm: epilogue");

@@ -29,14 +29,16 @@ struct FlashBwdArgs {
   void* dK;
   void* dV;
   float* dq_acc;   // [BH*S*D] fp32 scratch
-  float* rowstat;  // [2][BH*S] scratch: D_i = dO_i.O_i, then LSE_i*log2(e)
+  float* rowstat;  // [2][BH][Spad] scratch: D_i = dO_i.O_i, then LSE_i*log2(e) (+inf past S)
   int BH, S, D;
+  int Spad;        // S rounded up to 128: every 128-row slice of rowstat is in bounds and aligned
   float scale;
   int causal;
   uint32_t* err;
 };
 
-// Scratch bytes the backward needs (dQ accumulator + row statistics).
+// Scratch bytes the backward needs (dQ accumulator + padded row statistics).
+inline int flash_spad(int S) { return (S + 127) / 128 * 128; }
 size_t flash_bwd_scratch_bytes(int BH, int S, int D);
 
 bool flash_tc_supported(int D, const void* const* ptrs, int n);

@@ -43,7 +43,7 @@ dgx_status dgx_flash_bwd(const void* Q, const void* K, const void* V, const void
   if (!ws) ws = library_scratch(need, s);
   if (!ws) return set_error(DGX_ENOMEM, "dgx_flash_bwd: cannot allocate %zu bytes of scratch", need);
   FlashBwdArgs a{Q, K, V, O, dO, LSE, dQ, dK, dV, (float*)ws, (float*)ws + (size_t)BH * S * D,
-                 BH, S, D, scale, causal ? 1 : 0, device_error_word()};
+                 BH, S, D, flash_spad(S), scale, causal ? 1 : 0, device_error_word()};
   const void* ptrs[9] = {Q, K, V, O, dO, dQ, dK, dV, LSE};
   if (flash_tc_supported(D, ptrs, 9)) return cuda_status(flash_bwd_tc(a, s), "dgx_flash_bwd");
   return cuda_status(flash_bwd_simt(a, s), "dgx_flash_bwd simt");

@@ -33,11 +33,15 @@ constexpr int BQ = 128;   // queries per step
 constexpr int DP = 64;
 constexpr int Q_STAGES = 2;
 constexpr int TILE = 128 * DP * 2;  // 16 KB
-constexpr int NUM_THREADS = 448;    // 8 compute + 4 dQ-drain + TMA + MMA warps
+constexpr int NUM_THREADS = 512;    // WG0-1 compute, WG2 dQ drain, WG3: TMA warp, MMA warp, 2 idle
+// setmaxnreg split (per thread): 2 x 184 + 96 + 40 = 504 <= 512 = 65536 / 128.
+constexpr uint32_t REG_COMPUTE = 184, REG_DRAIN = 96, REG_CTRL = 40;
 
 constexpr int SM_K = 0, SM_V = TILE, SM_Q = 2 * TILE, SM_DO = SM_Q + Q_STAGES * TILE;
 constexpr int SM_DS = SM_DO + Q_STAGES * TILE;  // 128 queries x 128 keys bf16, MN-major (2 x 16 KB)
-constexpr int SM_BAR = SM_DS + 2 * TILE;
+constexpr int SM_STAT = SM_DS + 2 * TILE;  // per stage: L2 stats [128] then D stats [128] (fp32)
+constexpr int STAT_BYTES = 2 * BQ * 4;
+constexpr int SM_BAR = SM_STAT + Q_STAGES * STAT_BYTES;
 constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
 
 constexpr uint32_t T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384;  // T_DQ: 2 x 64
@@ -80,8 +84,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int i0 = args.causal ? (j * BKV) / BQ : 0;
   const int n = nq - i0;  // Q tiles this CTA walks
   const size_t row0 = (size_t)bh * args.S;
-  const float* Dstat = args.rowstat;
-  const float* L2stat = args.rowstat + (size_t)args.BH * args.S;
+  const float* Dstat = args.rowstat + (size_t)bh * args.Spad;
+  const float* L2stat = args.rowstat + (size_t)args.BH * args.Spad + (size_t)bh * args.Spad;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
@@ -110,7 +114,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
 
-  if (warp == 12) {
+  // Each role's setmaxnreg sits inside its branch so that it dominates (and
+  // sets the register limit for) exactly that role's code.
+  if (warp >= 12) {
+   regs_dec<REG_CTRL>();
+   if (warp == 12) {
     // ---------------------------------------------------------------- TMA
     if (elect_one_lane()) {
       tma_prefetch_desc(&tmQ);
@@ -124,9 +132,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (; it < n; ++it) {
         const int s = it % Q_STAGES;
         if (!mbar_wait(&bars->q_empty[s], ((it / Q_STAGES) & 1) ^ 1, wc)) break;
-        mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE);
+        mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE + STAT_BYTES);
         tma_load_3d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, (i0 + it) * BQ, bh);
         tma_load_3d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, (i0 + it) * BQ, bh);
+        uint8_t* st = smem + SM_STAT + s * STAT_BYTES;
+        bulk_load(st, L2stat + (i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
+        bulk_load(st + BQ * 4, Dstat + (i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
       }
       mbar_drain(&bars->kv_full, 0);
       for (int f = max(0, it - Q_STAGES); f < it; ++f) mbar_drain(&bars->q_full[f % Q_STAGES], (f / Q_STAGES) & 1);
@@ -139,16 +150,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t id_dq = make_idesc(1, 1, 1, 128, DP);   // MN-major dS x MN-major K
       const uint32_t sK = smem_u32(smem + SM_K), sV = smem_u32(smem + SM_V);
       const uint32_t sQ = smem_u32(smem + SM_Q), sdO = smem_u32(smem + SM_DO), sdS = smem_u32(smem + SM_DS);
+      // Descriptors advance by adding (byte offset >> 4) to the start field.
       auto kmajor_pair = [&](uint32_t d, uint32_t a, uint32_t b) {  // d = a . b^T over D
-#pragma unroll
-        for (int kk = 0; kk < DP / 16; ++kk)
-          mma_f16_ss(d, sw128_desc(a + kk * 32, 16, 1024), sw128_desc(b + kk * 32, 16, 1024), id_s, kk > 0);
+        const uint64_t da = sw128_desc(a, 16, 1024), db = sw128_desc(b, 16, 1024);
+#pragma unroll 1
+        for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(d, da + 2 * kk, db + 2 * kk, id_s, kk > 0);
       };
       auto tmem_a_acc = [&](uint32_t d, uint32_t a_tmem, uint32_t b, bool first) {  // d += A(tmem) . B
-#pragma unroll
+        const uint64_t db = sw128_desc(b, DP * 128, 1024);
+#pragma unroll 1
         for (int kk = 0; kk < BQ / 16; ++kk)
-          mma_f16_ts(d, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), sw128_desc(b + kk * 2048, DP * 128, 1024), id_acc,
-                     (!first || kk > 0) ? 1u : 0u);
+          mma_f16_ts(d, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), db + 128 * kk, id_acc, (!first || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&bars->kv_full, 0, wc) && mbar_wait(&bars->q_full[0], 0, wc);
       if (ok) {
@@ -178,10 +190,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int b = it & 1;
         if (!(ok = mbar_wait(&bars->dq_empty[b], ((it >> 1) & 1) ^ 1, wc))) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)  // dQ_part = dS K
-          mma_f16_ss(tmem + T_DQ + 64 * b, sw128_desc(sdS + kk * 2048, BKV * 128, 1024),
-                     sw128_desc(sK + kk * 2048, DP * 128, 1024), id_dq, kk > 0);
+        {
+          const uint64_t da = sw128_desc(sdS, BKV * 128, 1024), dk = sw128_desc(sK, DP * 128, 1024);
+#pragma unroll 1
+          for (int kk = 0; kk < BKV / 16; ++kk)  // dQ_part = dS K
+            mma_f16_ss(tmem + T_DQ + 64 * b, da + 128 * kk, dk + 128 * kk, id_dq, kk > 0);
+        }
         tc_commit(&bars->dq_full[b]);
         tc_commit(&bars->q_empty[s]);
         if (next) {
@@ -192,7 +206,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (ok) tc_commit(&bars->acc_done);
     }
     __syncwarp();
+   }
   } else if (warp >= 8) {
+    regs_dec<REG_DRAIN>();
     // ---------------------------------------------------------------- dQ drain
     const int qw = warp & 3;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
@@ -223,17 +239,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
+    regs_inc<REG_COMPUTE>();
     // ---------------------------------------------------------------- compute (P, dS)
     const int qw = warp & 3, h = warp >> 2;
     const int kr = qw * 32 + lane;
     const int key = j * BKV + kr;
+    const bool kvalid = key < args.S;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const float sl2 = args.scale * 1.4426950408889634f;
     uint8_t* ds_tile = smem + SM_DS + h * TILE;  // queries [64h, 64h+64)
     for (int it = 0; it < n; ++it) {
-      const int qbase = (i0 + it) * BQ + 64 * h;
-      const bool need_mask = (args.causal && (i0 + it) * BQ < j * BKV + BKV - 1) || (qbase + 64 > args.S) ||
-                             (j * BKV + BKV > args.S);
+      const int qt0 = (i0 + it) * BQ;
+      // Causal mask only on the diagonal tile; rows past S carry L2 = +inf
+      // (P = 0) in the padded statistics, so they need no test here.
+      const bool diag = args.causal && qt0 < j * BKV + BKV - 1;
+      const float* st = reinterpret_cast<const float*>(smem + SM_STAT + (it % Q_STAGES) * STAT_BYTES);
+      const float* Ls = st + 64 * h;
+      const float* Ds = st + BQ + 64 * h;
       if (!mbar_wait(&bars->s_full, it & 1, wc)) break;
       tc_fence_after();
       float p[64];
@@ -244,11 +266,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const int q = qbase + cc + t;
-          const float l2 = q < args.S ? __ldg(L2stat + row0 + q) : 0.f;
-          float e = ex2(fmaf(__uint_as_float(sv[t]), sl2, -l2));
-          if (need_mask && (q >= args.S || key >= args.S || (args.causal && q < key))) e = 0.f;
-          p[cc + t] = e;
+          const float e = ex2(fmaf(__uint_as_float(sv[t]), sl2, -Ls[cc + t]));
+          const bool vis = kvalid && !(diag && qt0 + 64 * h + cc + t < key);
+          p[cc + t] = vis ? e : 0.f;
         }
         uint32_t pk[16];
 #pragma unroll
@@ -270,11 +290,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const int q = qbase + cc + t;
-          const float d0 = q < args.S ? __ldg(Dstat + row0 + q) : 0.f;
-          const float d1 = q + 1 < args.S ? __ldg(Dstat + row0 + q + 1) : 0.f;
-          const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - d0);
-          const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - d1);
+          const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - Ds[cc + t]);
+          const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - Ds[cc + t + 1]);
           pk[t / 2] = pack_bf16x2(ds0, ds1);
         }
         tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
@@ -331,24 +348,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-// D_i = dO_i . O_i (fp32), L2_i = LSE_i * log2(e); zero the dQ accumulator.
-// One warp per row.
+// D_i = dO_i . O_i (fp32), L2_i = LSE_i * log2(e) in the padded [BH][Spad]
+// layout (rows past S: D = 0, L2 = +inf so that exp2(s - L2) = 0); zero the
+// dQ accumulator. One warp per row.
 __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
-  const long long rows = (long long)a.BH * a.S;
+  const long long rows = (long long)a.BH * a.Spad;
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-    const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.O) + r * a.D;
-    const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.dO) + r * a.D;
+    const int bh = (int)(r / a.Spad), q = (int)(r % a.Spad);
+    if (q >= a.S) {
+      if (lane == 0) {
+        a.rowstat[r] = 0.f;
+        a.rowstat[rows + r] = INFINITY;
+      }
+      continue;
+    }
+    const long long src = (long long)bh * a.S + q;
+    const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.O) + src * a.D;
+    const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.dO) + src * a.D;
     float s = 0.f;
     for (int c = lane; c < a.D; c += 32) s = fmaf(__bfloat162float(o[c]), __bfloat162float(g[c]), s);
 #pragma unroll
     for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    float* dq = a.dq_acc + r * a.D;
+    float* dq = a.dq_acc + src * a.D;
     for (int c = lane; c < a.D; c += 32) dq[c] = 0.f;
     if (lane == 0) {
       a.rowstat[r] = s;
-      a.rowstat[rows + r] = a.lse[r] * 1.4426950408889634f;
+      a.rowstat[rows + r] = a.lse[src] * 1.4426950408889634f;
     }
   }
 }
@@ -377,7 +404,7 @@ bool make_map(CUtensorMap* map, const void* base, int BH, int S, int D) {
 }  // namespace
 
 size_t flash_bwd_scratch_bytes(int BH, int S, int D) {
-  return ((size_t)BH * S * D + 2 * (size_t)BH * S) * sizeof(float);
+  return ((size_t)BH * S * D + 2 * (size_t)BH * flash_spad(S)) * sizeof(float);
 }
 
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
@@ -440,7 +467,7 @@ __global__ void flash_bwd_simt_dq_kernel(FlashBwdArgs a) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= a.S) return;
   const size_t base = (size_t)bh * a.S * a.D, r = (size_t)bh * a.S + i;
-  const float lse = a.lse[r], Di = a.rowstat[r];
+  const float lse = a.lse[r], Di = a.rowstat[(size_t)bh * a.Spad + i];
   float acc[SIMT_DMAX];
   for (int d = 0; d < a.D; ++d) acc[d] = 0.f;
   const int jend = a.causal ? i : a.S - 1;
@@ -472,7 +499,7 @@ __global__ void flash_bwd_simt_dkdv_kernel(FlashBwdArgs a) {
       s = fmaf(bf(a.Q, base + (size_t)i * a.D + d), bf(a.K, base + (size_t)jj * a.D + d), s);
       dp = fmaf(bf(a.dO, base + (size_t)i * a.D + d), bf(a.V, base + (size_t)jj * a.D + d), dp);
     }
-    const float p = __expf(s * a.scale - a.lse[r]), ds = p * (dp - a.rowstat[r]);
+    const float p = __expf(s * a.scale - a.lse[r]), ds = p * (dp - a.rowstat[(size_t)bh * a.Spad + i]);
     for (int d = 0; d < a.D; ++d) {
       dv[d] = fmaf(p, bf(a.dO, base + (size_t)i * a.D + d), dv[d]);
       dk[d] = fmaf(ds, bf(a.Q, base + (size_t)i * a.D + d), dk[d]);

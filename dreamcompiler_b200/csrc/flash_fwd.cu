@@ -32,7 +32,9 @@ constexpr int BLOCK_N = 128;   // keys per K/V tile
 constexpr int DP = 64;         // head dim held in shared memory / TMEM (D <= 64 zero-padded)
 constexpr int KV_STAGES = 3;
 constexpr int TILE_BYTES = BLOCK_M * DP * 2;  // 16 KB for every Q/K/V tile
-constexpr int NUM_THREADS = 320;
+constexpr int NUM_THREADS = 384;  // WG0: softmax A, WG1: softmax B, WG2: TMA warp, MMA warp, 2 idle
+// setmaxnreg split (per thread): 2 x 224 + 56 = 504 <= 3 x 168 (65536 / 384 rounded down to 8).
+constexpr uint32_t REG_SOFTMAX = 224, REG_CTRL = 56;
 constexpr float RESCALE_LOG2 = 8.0f;
 
 // shared memory map (offsets from a 1024-aligned base)
@@ -108,7 +110,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = bars->tmem_slot;
   const int row_base = bh * args.S;  // row of the [BH*S, D] view
 
-  if (warp == 8) {
+  // Each role's setmaxnreg sits inside its branch so that it dominates (and
+  // sets the register limit for) exactly that role's code.
+  if (warp >= 8) {
+   regs_dec<REG_CTRL>();
+   if (warp == 8) {
     // ---------------------------------------------------------------- TMA
     if (elect_one_lane()) {
       tma_prefetch_desc(&tmQ);
@@ -138,20 +144,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_s = make_idesc(1, 0, 0, BLOCK_M, BLOCK_N);  // Q.K^T, both K-major
       constexpr uint32_t idesc_o = make_idesc(1, 0, 1, BLOCK_M, DP);       // P.V, V MN-major
       const uint32_t sq = smem_u32(smem + SM_Q), sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V);
+      // Descriptors advance by adding (byte offset >> 4) to the start field.
       auto issue_s = [&](int x, int j) {
-        const uint32_t qa = sq + x * TILE_BYTES, ka = sk + (j % KV_STAGES) * TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < DP / 16; ++kk)
-          mma_f16_ss(tmem + (x ? T_S1 : T_S0), sw128_desc(qa + kk * 32, 16, 1024), sw128_desc(ka + kk * 32, 16, 1024),
-                     idesc_s, kk > 0 ? 1u : 0u);
+        const uint64_t dq = sw128_desc(sq + x * TILE_BYTES, 16, 1024);
+        const uint64_t dk = sw128_desc(sk + (j % KV_STAGES) * TILE_BYTES, 16, 1024);
+        const uint32_t d = tmem + (x ? T_S1 : T_S0);
+#pragma unroll 1
+        for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(d, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
         tc_commit(&bars->s_full[x]);
       };
       auto issue_pv = [&](int x, int j) {
-        const uint32_t va = sv + (j % KV_STAGES) * TILE_BYTES;
-#pragma unroll
+        const uint64_t dv = sw128_desc(sv + (j % KV_STAGES) * TILE_BYTES, DP * 128, 1024);
+        const uint32_t d = tmem + (x ? T_O1 : T_O0), a = tmem + (x ? T_S1 : T_S0);
+#pragma unroll 1
         for (int kk = 0; kk < BLOCK_N / 16; ++kk)
-          mma_f16_ts(tmem + (x ? T_O1 : T_O0), tmem + (x ? T_S1 : T_S0) + kk * 8,
-                     sw128_desc(va + kk * 16 * 128, DP * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_f16_ts(d, a + kk * 8, dv + 128 * kk, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&bars->q_full, 0, wc) && mbar_wait(&bars->k_full[0], 0, wc);
       if (ok) {
@@ -183,7 +190,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     __syncwarp();
+   }
   } else {
+    regs_inc<REG_SOFTMAX>();
     // ---------------------------------------------------------------- softmax (warps 0-3: A, 4-7: B)
     const int x = warp >> 2;
     const int q = warp & 3;

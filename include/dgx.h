@@ -31,7 +31,7 @@ typedef enum {
   DGX_ENOMEM = 6,        /* workspace too small or allocation failed */
 } dgx_status;
 
-typedef enum { DGX_F32 = 0, DGX_BF16 = 1, DGX_I8 = 2 } dgx_dtype;
+typedef enum { DGX_F32 = 0, DGX_BF16 = 1, DGX_I8 = 2, DGX_F64 = 3 } dgx_dtype;  /* F64: dgx_convert only */
 
 enum { DGX_EPI_NONE = 0, DGX_EPI_BIAS = 1, DGX_EPI_BIAS_RELU = 2, DGX_EPI_RELU = 3 };
 enum { DGX_F32_3XTF32 = 0, DGX_F32_FFMA = 1 };
@@ -48,6 +48,18 @@ dgx_status dgx_init(int device);
 /* Wait for `stream`, then read and clear the device error word that bounded
  * waits in the kernels report into. DGX_ETIMEOUT if any wait ran out. */
 dgx_status dgx_sync_check(void* stream);
+
+/*
+ * Device-side element conversion dst[i] = (dst_type) src[i] for n elements
+ * (f64/f32 -> bf16 round to nearest even, as dream_to_bf16,
+ * runtime/nn/training.inc:1969-1976; f64 -> f32 round to nearest). With
+ * accumulate=1 the converted value is ADDED to dst (f64/f32 dst only), which
+ * is how autograd's `grad +=` (runtime/ops/autograd.inc:112,123) lands.
+ * Lets a caller whose tensors are f64 (the Dream runtime's `data`/`grad`)
+ * move them to the device at 8 B/element and convert there.
+ */
+dgx_status dgx_convert(const void* src, dgx_dtype src_type, void* dst, dgx_dtype dst_type, size_t n, int accumulate,
+                       void* stream);
 
 /*
  * C[M,N] = beta*C + op(A)[M,K] . op(B)[K,N] (+bias[N]) (ReLU)

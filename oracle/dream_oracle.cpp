@@ -23,25 +23,6 @@
 
 extern "C" {
 
-// ---------------------------------------------------------------- RNG
-// The reference seeds one global std::mt19937 (set_seed, runtime/ops/
-// elementwise.inc:30-41) and draws std::normal_distribution<double>(0,1)
-// element by element for randn (:48-55). A fresh distribution object is
-// built per randn call, so no cached second normal carries across calls.
-static std::mt19937& rng() {
-  static std::mt19937 r(42);
-  return r;
-}
-void orc_set_seed(unsigned seed) { rng().seed(seed); }
-void orc_randn(double* out, long n) {
-  std::normal_distribution<double> dist(0.0, 1.0);
-  for (long i = 0; i < n; ++i) out[i] = dist(rng());
-}
-void orc_rand_uniform(double* out, long n, double lo, double hi) {
-  std::uniform_real_distribution<double> dist(lo, hi);
-  for (long i = 0; i < n; ++i) out[i] = dist(rng());
-}
-
 // ---------------------------------------------------------------- bf16
 // fp32 -> bf16 -> fp32 with round-to-nearest-even on the raw bits, as
 // dream_to_bf16 (runtime/nn/training.inc:1969-1976).

@@ -1,0 +1,126 @@
+"""Generate the golden vectors in tests/golden/ from the reference runtime.
+
+Runs only where the reference sources exist (it loads
+oracle/_ref/libdream_ref.so, built by oracle/build_ref.sh from
+heellowdsf/DreamCompiler runtime/). Every input is drawn with the reference's
+own RNG (set_seed + randn, runtime/ops/elementwise.inc:30-55) and every
+output comes from the reference's own ops:
+
+  gemm.npz   tensor_matmul f64 and f32-mirror paths + "matmul" backward, on
+             the shapes of gemm_selftest (runtime/ops/elementwise.inc:893-896)
+  flash.npz  dream_flash_attention + its backward, dream_attention_causal,
+             on the flash_attention_selftest configs (runtime/nn/training.inc:411)
+             and the tests/26_flash_backward.dream case
+  linear.npz dream_linear / dream_linear_relu + backward
+  tp.npz     dream_tp_matmul_column for G in {2,3,4,5,7} (training.inc:1664-1706)
+
+Usage:  python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle import refrt as R  # noqa: E402
+
+# gemm_selftest's shapes up to 128x100x96 (its two largest are left out to keep the fixture small)
+GEMM_SHAPES = [(1, 1, 1), (1, 7, 1), (5, 1, 9), (3, 4, 5), (7, 13, 17), (31, 33, 37), (64, 64, 64), (65, 63, 66),
+               (128, 100, 96)]
+FLASH_CFGS = [(64, 16, 8), (64, 16, 16), (128, 32, 32), (100, 24, 16), (128, 64, 64), (160, 64, 32)]
+
+
+def seeded_backward(out, shape):
+    """backward(sum(out * G)) with G ~ randn: injects dOut = G (autograd.inc:26)."""
+    g = R.randn(*shape)
+    s = R.call("sum", R.call("tensor_mul", out, g))
+    R.call("backward", s)
+    return R.data(g)
+
+
+def gen_gemm():
+    out = {}
+    R.set_seed(42)
+    for (M, K, N) in GEMM_SHAPES:
+        A, B = R.randn(M, K), R.randn(K, N)
+        C = R.call("tensor_matmul", A, B)
+        G = seeded_backward(C, (M, N))
+        tag = f"{M}x{K}x{N}"
+        out[f"A_{tag}"], out[f"B_{tag}"], out[f"G_{tag}"] = R.data(A), R.data(B), G
+        out[f"C_{tag}"], out[f"dA_{tag}"], out[f"dB_{tag}"] = R.data(C), R.grad(A), R.grad(B)
+        # f32 mirror path: dream_set_precision(t, 1) then `@` (elementwise.inc:1000-1016)
+        A32, B32 = R.tensor(out[f"A_{tag}"]), R.tensor(out[f"B_{tag}"])
+        R.call("dream_set_precision", A32, 1)
+        R.call("dream_set_precision", B32, 1)
+        out[f"C32_{tag}"] = R.data(R.call("tensor_matmul", A32, B32))
+    np.savez_compressed(os.path.join(HERE, "gemm.npz"), **out)
+
+
+def gen_flash():
+    out = {}
+    R.set_seed(20260709)
+    for (S, dk, Bc) in FLASH_CFGS:
+        B = 2 if S * dk <= 4096 else 1
+        Q, K, V = R.randn(B, S * dk), R.randn(B, S * dk), R.randn(B, S * dk)
+        sc = [R.scalar(v) for v in (B, S, dk, Bc)]
+        O = R.call("dream_flash_attention", Q, K, V, *sc)
+        G = seeded_backward(O, (B, S * dk))
+        tag = f"{S}_{dk}_{Bc}"
+        for name, t in (("Q", Q), ("K", K), ("V", V)):
+            out[f"{name}_{tag}"] = R.data(t).reshape(B, S, dk)
+            out[f"d{name}_{tag}"] = R.grad(t).reshape(B, S, dk)
+        out[f"G_{tag}"] = G.reshape(B, S, dk)
+        out[f"O_{tag}"] = R.data(O).reshape(B, S, dk)
+        Oc = R.call("dream_attention_causal", Q, K, V, *sc[:3])
+        out[f"Ocausal_{tag}"] = R.data(Oc).reshape(B, S, dk)
+        On = R.call("dream_attention", Q, K, V, *sc[:3])
+        out[f"Ofull_{tag}"] = R.data(On).reshape(B, S, dk)
+    # tests/26_flash_backward.dream: set_seed(5); Q,K,V = randn(1,512); S=32, dk=16, block 8; backward(sum(o)).
+    R.set_seed(5)
+    Q, K, V = R.randn(1, 512), R.randn(1, 512), R.randn(1, 512)
+    O = R.call("dream_flash_attention", Q, K, V, R.scalar(1), R.scalar(32), R.scalar(16), R.scalar(8))
+    R.call("backward", R.call("sum", O))
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        out[f"t26_{name}"] = R.data(t).reshape(1, 32, 16)
+        out[f"t26_d{name}"] = R.grad(t).reshape(1, 32, 16)
+    out["t26_O"] = R.data(O).reshape(1, 32, 16)
+    np.savez_compressed(os.path.join(HERE, "flash.npz"), **out)
+
+
+def gen_linear():
+    out = {}
+    R.set_seed(11)
+    for relu in (0, 1):
+        for (N, din, dout) in [(8, 16, 12), (33, 65, 17)]:
+            X, W, b = R.randn(N, din), R.randn(dout, din), R.randn(1, dout)
+            Y = R.call("dream_linear_relu" if relu else "dream_linear", X, W, b)
+            G = seeded_backward(Y, (N, dout))
+            tag = f"{relu}_{N}_{din}_{dout}"
+            out[f"X_{tag}"], out[f"W_{tag}"], out[f"b_{tag}"], out[f"G_{tag}"] = R.data(X), R.data(W), R.data(b)[0], G
+            out[f"Y_{tag}"], out[f"dX_{tag}"], out[f"dW_{tag}"], out[f"db_{tag}"] = (
+                R.data(Y), R.grad(X), R.grad(W), R.grad(b)[0])
+    np.savez_compressed(os.path.join(HERE, "linear.npz"), **out)
+
+
+def gen_tp():
+    out = {}
+    R.set_seed(20260709)
+    for (M, K, N) in [(12, 16, 24), (9, 10, 23)]:
+        X, W = R.randn(M, K), R.randn(K, N)
+        out[f"X_{M}_{K}_{N}"], out[f"W_{M}_{K}_{N}"] = R.data(X), R.data(W)
+        for G in (1, 2, 3, 4, 5, 7):
+            out[f"Y_{M}_{K}_{N}_{G}"] = R.data(R.call("dream_tp_matmul_column", X, W, R.scalar(G)))
+    np.savez_compressed(os.path.join(HERE, "tp.npz"), **out)
+
+
+if __name__ == "__main__":
+    gen_gemm()
+    gen_flash()
+    gen_linear()
+    gen_tp()
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

@@ -1,0 +1,173 @@
+"""CPU: the oracle (oracle/dream_oracle.cpp) pinned against golden vectors
+produced by the reference runtime itself (tests/golden/make_golden.py), plus
+known-answer tests for the parts the reference does not export."""
+import numpy as np
+import pytest
+
+from conftest import normwise
+
+GEMM_SHAPES = [(1, 1, 1), (1, 7, 1), (5, 1, 9), (3, 4, 5), (7, 13, 17), (31, 33, 37), (64, 64, 64), (65, 63, 66),
+               (128, 100, 96)]
+FLASH_CFGS = [(64, 16, 8), (64, 16, 16), (128, 32, 32), (100, 24, 16), (128, 64, 64), (160, 64, 32)]
+
+
+def test_rng_replays_reference_stream(orc, golden):
+    """set_seed(42) + randn in the fixture's draw order (A, B, G per shape)
+    reproduces the reference's std::mt19937/normal_distribution stream bit
+    for bit (runtime/ops/elementwise.inc:30-55)."""
+    g = golden("gemm")
+    orc.set_seed(42)
+    for (M, K, N) in GEMM_SHAPES:
+        t = f"{M}x{K}x{N}"
+        for name, shape in (("A", (M, K)), ("B", (K, N)), ("G", (M, N))):
+            assert np.array_equal(orc.randn(*shape), g[f"{name}_{t}"]), (name, t)
+
+
+@pytest.mark.parametrize("shape", GEMM_SHAPES)
+def test_gemm_f64_and_backward(orc, golden, shape):
+    g = golden("gemm")
+    M, K, N = shape
+    t = f"{M}x{K}x{N}"
+    A, B, G = g[f"A_{t}"], g[f"B_{t}"], g[f"G_{t}"]
+    assert normwise(orc.gemm_f64(A, B), g[f"C_{t}"]) < 1e-13
+    dA, dB = orc.matmul_bwd(A, B, G)
+    assert normwise(dA, g[f"dA_{t}"]) < 1e-13
+    assert normwise(dB, g[f"dB_{t}"]) < 1e-13
+
+
+@pytest.mark.parametrize("shape", GEMM_SHAPES)
+def test_gemm_f32_mirror_path(orc, golden, shape):
+    """The f32 path accumulates in fp32 (dream_gemm_f32); same arithmetic
+    order per KC=256 block, so these short-K shapes agree to the last bits."""
+    g = golden("gemm")
+    M, K, N = shape
+    t = f"{M}x{K}x{N}"
+    C32 = orc.gemm_f32(g[f"A_{t}"].astype(np.float32), g[f"B_{t}"].astype(np.float32))
+    assert normwise(C32, g[f"C32_{t}"]) < 1e-6
+
+
+@pytest.mark.parametrize("cfg", FLASH_CFGS)
+def test_flash_fwd_bwd(orc, golden, cfg):
+    g = golden("flash")
+    S, dk, Bc = cfg
+    t = f"{S}_{dk}_{Bc}"
+    Q, K, V, G = g[f"Q_{t}"], g[f"K_{t}"], g[f"V_{t}"], g[f"G_{t}"]
+    O, lse = orc.flash_fwd(Q, K, V, Bc)
+    assert normwise(O, g[f"O_{t}"]) < 1e-12
+    # flash == materialised causal attention (flash_attention_selftest, rel < 1e-9)
+    assert normwise(O, g[f"Ocausal_{t}"]) < 1e-9
+    assert normwise(orc.attention(Q, K, V, causal=True), g[f"Ocausal_{t}"]) < 1e-12
+    assert normwise(orc.attention(Q, K, V, causal=False), g[f"Ofull_{t}"]) < 1e-12
+    dQ, dK, dV = orc.flash_bwd(Q, K, V, G)
+    for name, x in (("dQ", dQ), ("dK", dK), ("dV", dV)):
+        assert normwise(x, g[f"{name}_{t}"]) < 1e-11, name
+    # LSE is consistent with O: log sum_j exp(s_ij) >= max_j s_ij
+    s = np.einsum("bid,bjd->bij", Q, K) / np.sqrt(dk)
+    s = np.where(np.tril(np.ones((S, S), bool)), s, -np.inf)
+    ref_lse = np.log(np.exp(s - s.max(-1, keepdims=True)).sum(-1)) + s.max(-1)
+    assert np.abs(lse - ref_lse).max() < 1e-10
+
+
+def test_flash_backward_reference_test26(orc, golden):
+    """tests/26_flash_backward.dream: set_seed(5), S=32, dk=16, block 8,
+    backward(sum(o)) -> dO = 1."""
+    g = golden("flash")
+    Q, K, V = g["t26_Q"], g["t26_K"], g["t26_V"]
+    O, _ = orc.flash_fwd(Q, K, V, 8)
+    assert normwise(O, g["t26_O"]) < 1e-12
+    dQ, dK, dV = orc.flash_bwd(Q, K, V, np.ones_like(O))
+    assert normwise(dQ, g["t26_dQ"]) < 1e-11
+    assert normwise(dK, g["t26_dK"]) < 1e-11
+    assert normwise(dV, g["t26_dV"]) < 1e-11
+    # the reference test's own pass condition, against materialised attention
+    assert abs(np.abs(dQ).sum() - np.abs(g["t26_dQ"]).sum()) < 1e-7
+
+
+@pytest.mark.parametrize("relu", [0, 1])
+@pytest.mark.parametrize("dims", [(8, 16, 12), (33, 65, 17)])
+def test_linear(orc, golden, relu, dims):
+    g = golden("linear")
+    t = f"{relu}_{dims[0]}_{dims[1]}_{dims[2]}"
+    X, W, b, G = g[f"X_{t}"], g[f"W_{t}"], g[f"b_{t}"], g[f"G_{t}"]
+    Y = orc.linear(X, W, b, relu=bool(relu))
+    assert normwise(Y, g[f"Y_{t}"]) < 1e-13
+    dX, dW, db = orc.linear_bwd(X, W, Y, G, relu=bool(relu))
+    assert normwise(dX, g[f"dX_{t}"]) < 1e-13
+    assert normwise(dW, g[f"dW_{t}"]) < 1e-13
+    assert normwise(db, g[f"db_{t}"]) < 1e-13
+
+
+@pytest.mark.parametrize("dims", [(12, 16, 24), (9, 10, 23)])
+@pytest.mark.parametrize("G", [1, 2, 3, 4, 5, 7])
+def test_tp_matmul_column(orc, golden, dims, G):
+    g = golden("tp")
+    M, K, N = dims
+    X, W = g[f"X_{M}_{K}_{N}"], g[f"W_{M}_{K}_{N}"]
+    Y = orc.tp_matmul_column(X, W, G)
+    # the reference self-test demands max_rel < 1e-12 against the un-split product
+    assert normwise(Y, g[f"Y_{M}_{K}_{N}_{G}"]) < 1e-13
+    widths = [orc.tp_shard(N, G, r)[1] for r in range(G)]
+    assert sum(widths) == N and max(widths) - min(widths) <= 1
+    assert widths == sorted(widths, reverse=True)  # the first N % G shards are the wide ones
+
+
+def test_bf16_round_known_answers(orc):
+    """dream_to_bf16 (runtime/nn/training.inc:1969-1976): round to nearest even."""
+    ulp = 2.0 ** -7
+    cases = {
+        1.0: 1.0,
+        1.0 + ulp / 2: 1.0,                 # tie -> even (1.0)
+        1.0 + 1.5 * ulp: 1.0 + 2 * ulp,     # tie -> even mantissa
+        1.0 + 0.75 * ulp: 1.0 + ulp,        # above half -> up
+        -3.0 - ulp: -3.0,                   # below half ulp (ulp of 3 is 2^-6) -> down
+        65504.0: 65536.0,
+        0.0: 0.0,
+        float("inf"): float("inf"),
+    }
+    x = np.array(list(cases.keys()), np.float32)
+    out = orc.round_bf16(x)
+    assert np.array_equal(out, np.array(list(cases.values()), np.float32))
+    assert np.isnan(orc.round_bf16(np.array([np.nan], np.float32))[0])
+
+
+def test_bf16_round_matches_torch(orc):
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(200_000) * np.exp(rng.uniform(-20, 20, 200_000))).astype(np.float32)
+    ours = orc.bf16_bits(x)
+    t = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(ours, t)
+
+
+def test_int8_quantizer_known_answers(orc):
+    """export_c_header_int8's per-tensor quantiser (training.inc:3668-3692)."""
+    w = np.array([0.0, 1.27, -1.27, 0.005, 0.015, -0.635, 0.6350001], np.float64)
+    q, scale = orc.quantize_per_tensor(w)
+    assert scale == pytest.approx(0.01)
+    assert q.tolist() == [0, 127, -127, 1, 2, -64, 64]   # lround: 0.5 -> 1, -63.5 -> -64 (half away from zero)
+    q0, s0 = orc.quantize_per_tensor(np.zeros(5))
+    assert s0 == 1.0 and not q0.any()
+
+
+def test_dense_q_and_int_core(orc):
+    rng = np.random.default_rng(1)
+    B, N, K = 3, 17, 40
+    X = rng.standard_normal((B, K)).astype(np.float32)
+    W = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    sc = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    Y = orc.dense_q(X, W, sc, b)
+    ref = b.astype(np.float64) + sc.astype(np.float64) * (X.astype(np.float64) @ W.astype(np.float64).T)
+    assert normwise(Y, ref) < 1e-5
+    Xq, sx = orc.quantize_rows(X)
+    assert np.abs(Xq).max() <= 127
+    assert np.allclose(sx, np.abs(X).max(1) / 127, rtol=1e-6)
+    acc = orc.i8_gemm(Xq, W)
+    assert np.array_equal(acc, Xq.astype(np.int64) @ W.astype(np.int64).T)
+
+
+def test_gemm_rows_sampling(orc):
+    rng = np.random.default_rng(2)
+    A, B = rng.standard_normal((50, 30)), rng.standard_normal((30, 20))
+    rows = np.array([0, 7, 49, 13], np.int32)
+    assert normwise(orc.gemm_rows_f64(A, B, rows), (A @ B)[rows]) < 1e-14
