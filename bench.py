@@ -1,0 +1,360 @@
+"""Benchmark: GEMM & FlashAttention fwd+bwd TFLOPS on B200 vs the host CPU.
+
+Default workload = BASELINE configs[1]: causal FlashAttention forward +
+backward, batch 8 x 16 heads, seq 2048, head dim 64, bf16 Q/K/V/dO ~ N(0,1),
+scale 1/8, fp32 softmax statistics. One step = dgx_flash_fwd + dgx_flash_bwd
+over one batch resident in HBM. Multi-GPU: one process per GPU, each rank
+runs its own batch (attention shards by batch x head with no communication,
+so scaling is weak); time = max over ranks of CUDA-event time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Prints ONE JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GEMM & FlashAttn fwd+bwd TFLOPS (% tensor peak) at 1/2/4/8 B200 vs host CPU"
+B, H, S, D = 8, 16, 2048, 64
+BH = B * H
+FWD_FLOP = 4.0 * BH * S * S * D / 2   # causal: half the S^2 pairs
+BWD_FLOP = 10.0 * BH * S * S * D / 2
+HEAD_FLOP = (FWD_FLOP + BWD_FLOP) / BH
+NOMINAL_DENSE_BF16 = 2250.0
+CONFIG = {"workload": "FlashAttention fwd+bwd, causal (BASELINE configs[1])", "batch": B, "heads": H,
+          "seq_len": S, "head_dim": D, "causal": True, "scale": 1.0 / 8,
+          "parallelism": "batch x head across ranks, no communication (weak: each rank a full batch)",
+          "l2": "two rotating input sets (256 MiB of inputs > 126 MB L2)"}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p["bf16_tflops_sustained"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 1400.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------- CPU side
+def _cpu_worker(args):
+    kind, seed = args
+    from oracle import cpu_bench
+    return cpu_bench.flash_head(kind, seed, S, D)
+
+
+def cpu_flash_sample(workers: int, kind: str, seed0: int = 0):
+    """`workers` heads in parallel, one per process (the reference's
+    FlashAttention is single-threaded). Returns (TFLOPS, wall seconds)."""
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers) as pool:
+        pool.map(_cpu_worker, [(kind, 1)] * workers)  # load the library in every worker
+        times = pool.map(_cpu_worker, [(kind, seed0 + i) for i in range(workers)])
+    t = max(times)
+    return workers * HEAD_FLOP / t / 1e12, t
+
+
+def cpu_workers() -> int:
+    n = os.cpu_count() or 1
+    try:
+        n = len(os.sched_getaffinity(0))
+    except Exception:
+        pass
+    return max(1, min(n, 32))
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls NVML (SM clock, throttle reasons) in a thread during a region."""
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.stop_flag = [], set(), False
+        self.max_mhz, self.ok = None, False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            pass
+        self.names = {}
+        if self.ok:
+            nv = self.nv
+            for attr, name in (("nvmlClocksEventReasonHwSlowdown", "hw_slowdown"),
+                               ("nvmlClocksEventReasonHwThermalSlowdown", "hw_thermal_slowdown"),
+                               ("nvmlClocksEventReasonSwThermalSlowdown", "sw_thermal_slowdown"),
+                               ("nvmlClocksEventReasonSwPowerCap", "sw_power_cap"),
+                               ("nvmlClocksEventReasonHwPowerBrakeSlowdown", "hw_power_brake"),
+                               ("nvmlClocksEventReasonApplicationsClocksSetting", "applications_clocks_setting"),
+                               ("nvmlClocksEventReasonSyncBoost", "sync_boost")):
+                if hasattr(nv, attr):
+                    self.names[getattr(nv, attr)] = name
+
+    def _run(self):
+        while not self.stop_flag:
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.names.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.stop_flag = True
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0,
+                    "source": "nvml" if self.ok else "unavailable"}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml, 2 ms poll"}
+
+
+# ---------------------------------------------------------------- GPU side
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import dreamcompiler_b200 as dgx
+    from dreamcompiler_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    dgx.init(local_rank)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sets = [[torch.randn(BH, S, D, device=dev, generator=gen).bfloat16() for _ in range(4)] for _ in range(2)]
+    O = torch.empty(BH, S, D, device=dev, dtype=torch.bfloat16)
+    L = torch.empty(BH, S, device=dev, dtype=torch.float32)
+    dQ, dK, dV = (torch.empty_like(O) for _ in range(3))
+    ws = torch.empty(dgx.flash_bwd_workspace_size(BH, S, D) // 4 + 1, device=dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, timer=None):
+        q, k, v, do = sets[i & 1]
+        dgx.flash_fwd(q, k, v, out=O, lse=L)
+        if timer is not None:
+            lib.dgx_set_timer_events(timer[0].cuda_event, timer[1].cuda_event)
+        dgx.flash_bwd(q, k, v, O, do, L, dQ=dQ, dK=dK, dV=dV, workspace=ws)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        step(i)
+    dgx.sync_check()
+    K = args.steps
+    timers = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for a, b in timers:  # materialise the CUDA events
+        a.record(stream)
+        b.record(stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for i in range(K):
+            step(i, timers[i])
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    dgx.sync_check()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    bwd_kernel_s = sum(a.elapsed_time(b) for a, b in timers) / 1e3 / K
+
+    # ---- end to end: host bf16 buffers in pinned memory, H2D -> fwd -> bwd -> D2H,
+    # pipelined over head chunks on three streams.
+    host_in = [torch.empty(BH, S, D, dtype=torch.bfloat16, pin_memory=True) for _ in range(4)]
+    for h, d in zip(host_in, sets[0]):
+        h.copy_(d)
+    host_out = [torch.empty(BH, S, D, dtype=torch.bfloat16, pin_memory=True) for _ in range(4)]
+    CH = 16
+    nch = BH // CH
+    s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    ring = 3
+    dbuf = [[torch.empty(CH, S, D, device=dev, dtype=torch.bfloat16) for _ in range(8)] for _ in range(ring)]
+    dl = [torch.empty(CH, S, device=dev) for _ in range(ring)]
+    wsc = torch.empty(dgx.flash_bwd_workspace_size(CH, S, D) // 4 + 1, device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(ring)]
+    ev_cmp = [torch.cuda.Event() for _ in range(ring)]
+    ev_out = [torch.cuda.Event() for _ in range(ring)]
+
+    def e2e_step():
+        for c in range(nch):
+            r = c % ring
+            q, k, v, do, o, gq, gk, gv = dbuf[r]
+            sl = slice(c * CH, (c + 1) * CH)
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(ev_out[r])
+                for dst, src in zip((q, k, v, do), host_in):
+                    dst.copy_(src[sl], non_blocking=True)
+                ev_in[r].record(s_in)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(ev_in[r])
+                dgx.flash_fwd(q, k, v, out=o, lse=dl[r])
+                dgx.flash_bwd(q, k, v, o, do, dl[r], dQ=gq, dK=gk, dV=gv, workspace=wsc)
+                ev_cmp[r].record(s_cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_cmp[r])
+                for dst, src in zip(host_out, (o, gq, gk, gv)):
+                    dst[sl].copy_(src, non_blocking=True)
+                ev_out[r].record(s_out)
+
+    e2e_steps = max(3, min(K, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(s_in)
+    for _ in range(e2e_steps):
+        s_in.wait_stream(s_out)
+        e2e_step()
+    s_out.wait_stream(s_cmp)
+    t1.record(s_out)
+    torch.cuda.synchronize(dev)
+    barrier()
+    dgx.sync_check()
+    e2e_s = t0.elapsed_time(t1) / 1e3 / e2e_steps
+
+    t = torch.tensor([elapsed, e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t[0].item(), t[1].item(), bwd_kernel_s, clocks.summary()
+
+
+def traffic_per_launch():
+    """DRAM bytes per flash_bwd_kernel launch from the committed ncu summary
+    (profiles/flash_bwd_traffic.json), scaled to this workload's heads."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "flash_bwd_traffic.json")) as f:
+            p = json.load(f)
+        return p["dram_bytes_per_launch"] * BH / p["bh"]
+    except Exception:
+        return None
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    n = max(world, 1)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import cpu_bench
+        kind = cpu_bench.available_kind()
+        w = cpu_workers()
+        vals = []
+        per_step = None
+        steps_run = 0
+        for i in range(args.warmup + args.steps):
+            tf, wall = cpu_flash_sample(w, kind, seed0=i * w)
+            per_step = wall if per_step is None else per_step
+            if i >= args.warmup:
+                vals.append(tf)
+                steps_run += 1
+            # keep the whole reference run to a few minutes
+            if steps_run >= 1 and (i + 1) * max(per_step, 1.0) > 150:
+                break
+        v = statistics.median(vals) if vals else 0.0
+        ms = HEAD_FLOP * w / (v * 1e12) * 1e3 if v else None
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOPS", "n_gpus": n,
+            "steps": steps_run, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1), reference RNG",
+            "config": CONFIG,
+            "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": w, "kind": kind,
+                             "sample": f"{w} heads of config 2 (S=2048, dk=64) per step, one per process, "
+                                       "dream_flash_attention + backward (single-threaded per head)"},
+            "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    cpu = None
+    if n == 1 and not args.no_cpu_baseline:
+        # Before any CUDA work: worker processes are spawned, never forked.
+        from oracle import cpu_bench
+        kind = cpu_bench.available_kind()
+        w = cpu_workers()
+        tf, wall = cpu_flash_sample(w, kind)
+        cpu = {"value": tf, "unit": "TFLOPS", "cores": w, "kind": kind,
+               "sample": f"{w} heads of config 2 (S=2048, dk=64) fwd+bwd, one per process, {wall:.2f} s wall"}
+
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    elapsed, e2e_s, bwd_kernel_s, clocks = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    step_flop = FWD_FLOP + BWD_FLOP
+    value = n * step_flop * args.steps / elapsed / 1e12
+    sustained, burst, src = peaks()
+    achieved = BWD_FLOP / bwd_kernel_s / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: bf16 Q/K/V/dO ~ N(0,1), seeded, config 2 shapes", "config": CONFIG,
+        "pct_of_peak": {"per_gpu_tflops": value / n, "of_nominal_dense_bf16_2250": value / n / NOMINAL_DENSE_BF16,
+                        f"of_{src}_bf16_sustained": value / n / sustained},
+        "roofline": {"kernel": "flash_bwd_kernel", "bound": "tensor", "achieved": achieved, "peak": sustained,
+                     "peak_source": f"{src} bf16 sustained (kernel timed inside a long loop)",
+                     "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": traffic_per_launch(),
+                     "algorithmic": f"{BWD_FLOP:.4g} FLOP per launch = 10*BH*S^2*D/2 (causal)"},
+        "e2e": {"value": n * step_flop / e2e_s / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": 4 * BH * S * D * 2,
+                "d2h_bytes_per_step": 4 * BH * S * D * 2,
+                "path": "pinned host bf16 Q,K,V,dO -> dgx_flash_fwd/bwd -> O,dQ,dK,dV to host, 16-head chunks "
+                        "pipelined on 3 streams"},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -36,6 +36,7 @@ SIGNATURES = {
     "dgx_last_error": (C.c_char_p, []),
     "dgx_init": (_i, [_i]),
     "dgx_sync_check": (_i, [_vp]),
+    "dgx_set_timer_events": (None, [_vp, _vp]),
     "dgx_convert": (_i, [_vp, _i, _vp, _i, _sz, _i, _vp]),
     "dgx_gemm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _f, _vp, _sz, _vp]),
     "dgx_gemm_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i]),

@@ -98,6 +98,17 @@ void* library_scratch(size_t bytes, cudaStream_t s) {
   return st.scratch;
 }
 
+static thread_local cudaEvent_t g_timer_start = nullptr, g_timer_stop = nullptr;
+
+TimerScope::TimerScope(cudaStream_t st) : s(st), stop(g_timer_stop) {
+  if (g_timer_start && g_timer_stop) cudaEventRecord(g_timer_start, s);
+  else stop = nullptr;
+  g_timer_start = g_timer_stop = nullptr;
+}
+TimerScope::~TimerScope() {
+  if (stop) cudaEventRecord(stop, s);
+}
+
 }  // namespace dgx
 
 using namespace dgx;
@@ -107,6 +118,11 @@ extern "C" {
 const char* dgx_version(void) { return "libdgx 0.1 (sm_100a)"; }
 
 const char* dgx_last_error(void) { return g_err; }
+
+void dgx_set_timer_events(void* start, void* stop) {
+  g_timer_start = (cudaEvent_t)start;
+  g_timer_stop = (cudaEvent_t)stop;
+}
 
 dgx_status dgx_init(int device) {
   int n = 0;

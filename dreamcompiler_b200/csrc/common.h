@@ -29,4 +29,13 @@ dgx_status cuda_status(cudaError_t e, const char* what);
 // cudaMalloc, reused across calls on the same stream order).
 void* library_scratch(size_t bytes, cudaStream_t s);
 
+// Brackets one kernel launch with the events set by dgx_set_timer_events
+// (if any), then clears them. Construct right before the launch.
+struct TimerScope {
+  cudaStream_t s;
+  cudaEvent_t stop;
+  explicit TimerScope(cudaStream_t st);
+  ~TimerScope();
+};
+
 }  // namespace dgx

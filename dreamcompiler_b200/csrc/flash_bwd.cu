@@ -421,7 +421,10 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
   const int sms = num_sms();
   flash_bwd_pre_kernel<<<4 * sms, 256, 0, s>>>(a);
   const int nkv = (a.S + BKV - 1) / BKV;
-  flash_bwd_kernel<<<nkv * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+  {
+    TimerScope timer(s);
+    flash_bwd_kernel<<<nkv * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+  }
   flash_bwd_post_kernel<<<4 * sms, 256, 0, s>>>(a);
   return cudaGetLastError();
 }

@@ -338,7 +338,10 @@ cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s) {
     attr = true;
   }
   const int nqb = (a.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M);
-  flash_fwd_kernel<<<nqb * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, a);
+  {
+    TimerScope timer(s);
+    flash_fwd_kernel<<<nqb * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, a);
+  }
   return cudaGetLastError();
 }
 

@@ -408,7 +408,10 @@ static cudaError_t launch_tc(const GemmArgs& args, const void* A, const void* B,
   }
   const int tiles = a.tiles_m * a.tiles_n;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, a);
+  {
+    TimerScope timer(stream);
+    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, a);
+  }
   return cudaGetLastError();
 }
 

@@ -1,0 +1,50 @@
+"""Profiling entry point: run one small case of a hot-path kernel through the
+C ABI, sized for an `ncu` capture (a few hundred MB on the device at most,
+two launches of each kernel).
+
+    python -m dreamcompiler_b200.profile_case flash --bh 16      # S=2048, D=64
+    python -m dreamcompiler_b200.profile_case gemm --n 4096
+"""
+from __future__ import annotations
+
+import argparse
+
+
+def main() -> None:
+    import torch
+    import dreamcompiler_b200 as dgx
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kind", choices=["flash", "gemm", "w8"])
+    ap.add_argument("--bh", type=int, default=16)
+    ap.add_argument("--seq", type=int, default=2048)
+    ap.add_argument("--dim", type=int, default=64)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--reps", type=int, default=2)
+    a = ap.parse_args()
+    dgx.init(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    if a.kind == "flash":
+        Q, K, V, dO = (torch.randn(a.bh, a.seq, a.dim, device="cuda", generator=g).bfloat16() for _ in range(4))
+        O, L = dgx.flash_fwd(Q, K, V)
+        for _ in range(a.reps):
+            dgx.flash_fwd(Q, K, V, out=O, lse=L)
+            dgx.flash_bwd(Q, K, V, O, dO, L)
+    elif a.kind == "gemm":
+        A, B = (torch.randn(a.n, a.n, device="cuda", generator=g).bfloat16() for _ in range(2))
+        C = torch.empty(a.n, a.n, device="cuda", dtype=torch.bfloat16)
+        for _ in range(a.reps):
+            dgx.gemm(A, B, out=C)
+    else:
+        X = torch.randn(a.batch, a.n, device="cuda", generator=g)
+        W = torch.randint(-127, 128, (a.n, a.n), device="cuda", dtype=torch.int8, generator=g)
+        sc = torch.rand(a.n, device="cuda", generator=g) * 9e-3 + 1e-3
+        for _ in range(a.reps):
+            dgx.gemm_w8(X, W, sc, None, mode=0)
+    dgx.sync_check()
+    print("profile case ok")
+
+
+if __name__ == "__main__":
+    main()

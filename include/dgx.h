@@ -49,6 +49,15 @@ dgx_status dgx_init(int device);
  * waits in the kernels report into. DGX_ETIMEOUT if any wait ran out. */
 dgx_status dgx_sync_check(void* stream);
 
+/* Profiling hook: the next main kernel this thread launches (the tensor-core
+ * kernel behind dgx_gemm, dgx_flash_fwd or dgx_flash_bwd) is bracketed by
+ * cudaEventRecord(start) / cudaEventRecord(stop) on the stream it runs on,
+ * then the hook clears itself. start/stop are cudaEvent_t handles; NULL
+ * clears. Lets a benchmark time the dominant kernel live, inside its loop.
+ * (No reference counterpart: the reference only has host wall-clock
+ * regions, runtime/nn/training.inc:2223-2291.) */
+void dgx_set_timer_events(void* start, void* stop);
+
 /*
  * Device-side element conversion dst[i] = (dst_type) src[i] for n elements
  * (f64/f32 -> bf16 round to nearest even, as dream_to_bf16,
