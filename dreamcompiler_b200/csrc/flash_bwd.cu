@@ -17,12 +17,33 @@
 // in the order S(i) dP(i) | dV(i) S(i+1) | dK(i) dQ(i) dP(i+1) so the tensor
 // core overlaps the element-wise work of the 8 compute warps. dQ partials go
 // through two TMEM buffers to 4 drain warps that add them into an fp32
-// accumulator with vector atomics; a last kernel scales it and casts to bf16.
+// accumulator: each partial tile is staged in shared memory and added with one
+// TMA bulk reduce (cp.reduce.async.bulk.tensor .add) per tile; a last kernel
+// scales the accumulator and casts it to bf16.
 #include <math.h>
 
 #include "common.h"
 #include "flash.h"
 #include "sm100.cuh"
+#include "softmax_math.cuh"
+
+// Optional phase tracing for kernel tuning: built with -DDGX_TRACE, the CTA
+// of key tile 0, head 0 records clock64() at the marked points into
+// dgx_bwd_trace (read back with dgx_bwd_trace_read). Compiled out otherwise.
+#ifdef DGX_TRACE
+__device__ unsigned long long dgx_bwd_trace[16384];
+#define BWD_TRACE(slot) \
+  do {                  \
+    if (blockIdx.x == 0) dgx_bwd_trace[(slot)] = clock64(); \
+  } while (0)
+extern "C" int dgx_bwd_trace_read(void* dst) {
+  return (int)cudaMemcpyFromSymbol(dst, dgx_bwd_trace, sizeof(dgx_bwd_trace));
+}
+#else
+#define BWD_TRACE(slot) \
+  do {                  \
+  } while (0)
+#endif
 
 namespace dgx {
 
@@ -41,7 +62,9 @@ constexpr int SM_K = 0, SM_V = TILE, SM_Q = 2 * TILE, SM_DO = SM_Q + Q_STAGES * 
 constexpr int SM_DS = SM_DO + Q_STAGES * TILE;  // 128 queries x 128 keys bf16, MN-major (2 x 16 KB)
 constexpr int SM_STAT = SM_DS + 2 * TILE;  // per stage: L2 stats [128] then D stats [128] (fp32)
 constexpr int STAT_BYTES = 2 * BQ * 4;
-constexpr int SM_BAR = SM_STAT + Q_STAGES * STAT_BYTES;
+constexpr int SM_DQ = SM_STAT + Q_STAGES * STAT_BYTES;  // dQ staging: 2 boxes of 128 rows x 32 fp32 (SW128)
+constexpr int DQ_BOX = 128 * 128;
+constexpr int SM_BAR = SM_DQ + 2 * DQ_BOX;
 constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
 
 constexpr uint32_t T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384;  // T_DQ: 2 x 64
@@ -53,13 +76,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 struct BwdBars {
   uint64_t kv_full, q_full[Q_STAGES], q_empty[Q_STAGES];
@@ -71,7 +87,7 @@ struct BwdBars {
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                     FlashBwdArgs args) {
+                     const __grid_constant__ CUtensorMap tmdQacc, FlashBwdArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + SM_BAR);
@@ -175,7 +191,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t q_s = sQ + s * TILE, do_s = sdO + s * TILE;
         const bool next = it + 1 < n;
         const int s1 = (it + 1) % Q_STAGES;
+        BWD_TRACE(8192 + it * 8 + 0);
         if (!(ok = mbar_wait(&bars->p_ready, it & 1, wc))) break;
+        BWD_TRACE(8192 + it * 8 + 1);
         tc_fence_after();
         tmem_a_acc(tmem + T_DV, tmem + T_ST, do_s, it == 0);  // dV += P^T dO
         if (next) {
@@ -184,11 +202,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           kmajor_pair(tmem + T_ST, sK, sQ + s1 * TILE);  // S^T(i+1)
           tc_commit(&bars->s_full);
         }
+        BWD_TRACE(8192 + it * 8 + 2);
         if (!(ok = mbar_wait(&bars->ds_ready, it & 1, wc))) break;
+        BWD_TRACE(8192 + it * 8 + 3);
         tc_fence_after();
         tmem_a_acc(tmem + T_DK, tmem + T_DPT, q_s, it == 0);  // dK += dS^T Q
         const int b = it & 1;
         if (!(ok = mbar_wait(&bars->dq_empty[b], ((it >> 1) & 1) ^ 1, wc))) break;
+        BWD_TRACE(8192 + it * 8 + 4);
         tc_fence_after();
         {
           const uint64_t da = sw128_desc(sdS, BKV * 128, 1024), dk = sw128_desc(sK, DP * 128, 1024);
@@ -211,10 +232,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     regs_dec<REG_DRAIN>();
     // ---------------------------------------------------------------- dQ drain
     const int qw = warp & 3;
+    const int row = qw * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const bool issuer = warp == 8 && lane == 0;
+    uint8_t* stage = smem + SM_DQ;
+    if (issuer) tma_prefetch_desc(&tmdQacc);
     for (int it = 0; it < n; ++it) {
       const int b = it & 1;
+      if (issuer) BWD_TRACE(4096 + it * 8 + 0);
       if (!mbar_wait(&bars->dq_full[b], (it >> 1) & 1, wc)) break;
+      if (issuer) BWD_TRACE(4096 + it * 8 + 1);
       tc_fence_after();
       uint32_t v[DP];
       tmem_ld32(tmem + lane_off + T_DQ + 64 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
@@ -223,21 +250,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->dq_empty[b]);
-      const int q = (i0 + it) * BQ + qw * 32 + lane;
-      if (q < args.S) {
-        float* dst = args.dq_acc + (row0 + q) * args.D;
-        if (args.D == DP) {
+      // The previous tile's bulk reduce must have read the staging tile.
+      if (issuer) bulk_wait_read0();
+      named_bar_sync(1, 128);
+      // Row `row`, columns [32c, 32c+32) -> box c; 16-byte unit u at u ^ (row & 7).
 #pragma unroll
-          for (int c = 0; c < DP; c += 4)
-            red_add_v4(dst + c, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
-                       __uint_as_float(v[c + 3]));
-        } else {
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int c = 0; c < DP; ++c)
-            if (c < args.D) atomicAdd(dst + c, __uint_as_float(v[c]));
-        }
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(stage + c * DQ_BOX + row * 128 + ((u ^ (row & 7)) << 4)) =
+              make_uint4(v[32 * c + 4 * u], v[32 * c + 4 * u + 1], v[32 * c + 4 * u + 2], v[32 * c + 4 * u + 3]);
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
+      if (issuer) BWD_TRACE(4096 + it * 8 + 2);
+      if (issuer) {
+        const int q0 = (i0 + it) * BQ;
+        tma_reduce_add_3d(&tmdQacc, stage, 0, q0, bh);
+        if (args.D > 32) tma_reduce_add_3d(&tmdQacc, stage + DQ_BOX, 32, q0, bh);
+        bulk_commit();
       }
     }
+    if (issuer) bulk_wait0();
   } else {
     regs_inc<REG_COMPUTE>();
     // ---------------------------------------------------------------- compute (P, dS)
@@ -256,43 +289,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float* st = reinterpret_cast<const float*>(smem + SM_STAT + (it % Q_STAGES) * STAT_BYTES);
       const float* Ls = st + 64 * h;
       const float* Ds = st + BQ + 64 * h;
+      const bool trc = warp == 0 && lane == 0;
+      if (trc) BWD_TRACE(it * 8 + 0);
       if (!mbar_wait(&bars->s_full, it & 1, wc)) break;
+      if (trc) BWD_TRACE(it * 8 + 1);
       tc_fence_after();
       float p[64];
 #pragma unroll
       for (int cc = 0; cc < 64; cc += 32) {
         uint32_t sv[32];
         tmem_ld32(tmem + lane_off + T_ST + 64 * h + cc, sv);
-        tmem_ld_wait();
+        float lv[32];  // the 32 rows' L2 statistics (same for every lane: broadcast reads)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const float e = ex2(fmaf(__uint_as_float(sv[t]), sl2, -Ls[cc + t]));
+        for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
+        tmem_ld_wait();
+        static_for<0, 32, 1>([&](auto tt) {
+          constexpr int t = decltype(tt)::value;
+          const float e = ex2_col<t, DGX_EXP_EMU_BWD>(fmaf(__uint_as_float(sv[t]), sl2, -lv[t]));
           const bool vis = kvalid && !(diag && qt0 + 64 * h + cc + t < key);
           p[cc + t] = vis ? e : 0.f;
-        }
+        });
         uint32_t pk[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(p[cc + 2 * t], p[cc + 2 * t + 1]);
+        for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2_fast(p[cc + 2 * t], p[cc + 2 * t + 1]);
         tmem_st16(tmem + lane_off + T_ST + 64 * h + cc / 2, pk);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_ready);
-
+      if (trc) BWD_TRACE(it * 8 + 2);
       if (!mbar_wait(&bars->dp_full, it & 1, wc)) break;
+      if (trc) BWD_TRACE(it * 8 + 3);
       tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < 64; cc += 32) {
         uint32_t dv[32];
         tmem_ld32(tmem + lane_off + T_DPT + 64 * h + cc, dv);
+        float dd[32];
+#pragma unroll
+        for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&dd[t]) = *reinterpret_cast<const float4*>(Ds + cc + t);
         tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - Ds[cc + t]);
-          const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - Ds[cc + t + 1]);
-          pk[t / 2] = pack_bf16x2(ds0, ds1);
+          const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - dd[t]);
+          const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - dd[t + 1]);
+          pk[t / 2] = pack_bf16x2_fast(ds0, ds1);
         }
         tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
         // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
@@ -309,6 +352,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->ds_ready);
+      if (trc) BWD_TRACE(it * 8 + 4);
     }
     // ------------------------------------------------------------ epilogue: dV (h=0), dK (h=1)
     if (mbar_wait(&bars->acc_done, 0, wc)) {
@@ -349,43 +393,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // D_i = dO_i . O_i (fp32), L2_i = LSE_i * log2(e) in the padded [BH][Spad]
-// layout (rows past S: D = 0, L2 = +inf so that exp2(s - L2) = 0); zero the
-// dQ accumulator. One warp per row.
+// layout (rows past S: D = 0, L2 = +inf so that exp2(s - L2) = 0). Eight
+// lanes per row, 16-byte loads when D % 8 == 0.
 __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
   const long long rows = (long long)a.BH * a.Spad;
-  const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+  const int sub = threadIdx.x & 7;
+  const long long groups = (long long)gridDim.x * (blockDim.x >> 3);
+  const bool vec = (a.D % 8) == 0;
+  for (long long r = blockIdx.x * (long long)(blockDim.x >> 3) + (threadIdx.x >> 3); r < rows; r += groups) {
     const int bh = (int)(r / a.Spad), q = (int)(r % a.Spad);
-    if (q >= a.S) {
-      if (lane == 0) {
-        a.rowstat[r] = 0.f;
-        a.rowstat[rows + r] = INFINITY;
-      }
-      continue;
-    }
-    const long long src = (long long)bh * a.S + q;
-    const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.O) + src * a.D;
-    const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.dO) + src * a.D;
     float s = 0.f;
-    for (int c = lane; c < a.D; c += 32) s = fmaf(__bfloat162float(o[c]), __bfloat162float(g[c]), s);
+    if (q < a.S) {
+      const long long src = ((long long)bh * a.S + q) * a.D;
+      const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.O) + src;
+      const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.dO) + src;
+      if (vec) {
+        for (int c = sub * 8; c < a.D; c += 64) {
+          const uint4 ov = *reinterpret_cast<const uint4*>(o + c), gv = *reinterpret_cast<const uint4*>(g + c);
+          const __nv_bfloat162* op = reinterpret_cast<const __nv_bfloat162*>(&ov);
+          const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
 #pragma unroll
-    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    float* dq = a.dq_acc + src * a.D;
-    for (int c = lane; c < a.D; c += 32) dq[c] = 0.f;
-    if (lane == 0) {
-      a.rowstat[r] = s;
-      a.rowstat[rows + r] = a.lse[src] * 1.4426950408889634f;
+          for (int h = 0; h < 4; ++h) {
+            const float2 x = __bfloat1622float2(op[h]), y = __bfloat1622float2(gp[h]);
+            s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+          }
+        }
+      } else {
+        for (int c = sub; c < a.D; c += 8) s = fmaf(__bfloat162float(o[c]), __bfloat162float(g[c]), s);
+      }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (sub == 0) {
+      a.rowstat[r] = q < a.S ? s : 0.f;
+      a.rowstat[rows + r] = q < a.S ? a.lse[(long long)bh * a.S + q] * 1.4426950408889634f : INFINITY;
     }
   }
 }
 
-// dQ = bf16(scale * dQ_acc)
+// dQ = bf16(scale * dQ_acc), four elements per thread step.
 __global__ void flash_bwd_post_kernel(FlashBwdArgs a) {
   const long long total = (long long)a.BH * a.S * a.D;
+  const long long quads = total / 4;
   __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(a.dQ);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x)
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < quads; i += stride) {
+    const float4 v = reinterpret_cast<const float4*>(a.dq_acc)[i];
+    uint2 w;
+    w.x = pack_bf16x2(v.x * a.scale, v.y * a.scale);
+    w.y = pack_bf16x2(v.z * a.scale, v.w * a.scale);
+    reinterpret_cast<uint2*>(dq)[i] = w;
+  }
+  for (long long i = quads * 4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride)
     dq[i] = __float2bfloat16_rn(a.dq_acc[i] * a.scale);
 }
 
@@ -418,12 +478,28 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  CUtensorMap mdq{};
+  {
+    // fp32 dQ accumulator [BH][S][D] for the bulk reduce: boxes of 128 rows x
+    // 32 columns (128 bytes, 128B swizzle); rows past S and columns past D clip.
+    auto enc = get_tensor_map_encoder();
+    cuuint64_t dims[3] = {(cuuint64_t)a.D, (cuuint64_t)a.S, (cuuint64_t)a.BH};
+    cuuint64_t strides[2] = {(cuuint64_t)a.D * 4, (cuuint64_t)a.S * a.D * 4};
+    cuuint32_t box[3] = {32, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (!enc || enc(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.dq_acc, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   const int sms = num_sms();
-  flash_bwd_pre_kernel<<<4 * sms, 256, 0, s>>>(a);
+  cudaError_t e = cudaMemsetAsync(a.dq_acc, 0, (size_t)a.BH * a.S * a.D * sizeof(float), s);
+  if (e != cudaSuccess) return e;
+  flash_bwd_pre_kernel<<<8 * sms, 256, 0, s>>>(a);
   const int nkv = (a.S + BKV - 1) / BKV;
   {
     TimerScope timer(s);
-    flash_bwd_kernel<<<nkv * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+    flash_bwd_kernel<<<nkv * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, mdq, a);
   }
   flash_bwd_post_kernel<<<4 * sms, 256, 0, s>>>(a);
   return cudaGetLastError();

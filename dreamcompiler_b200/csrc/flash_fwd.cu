@@ -7,11 +7,15 @@
 //
 // One CTA owns 256 query rows as two 128-row tiles (A, B) that share every
 // K/V tile load. Warps 0-3 run tile A's softmax, warps 4-7 tile B's, warp 8
-// issues TMA loads, warp 9 issues tcgen05.mma. TMEM holds S_A, S_B (128
-// fp32 columns each; P is written back over S as packed bf16 and read by the
-// P.V MMA straight from TMEM) and O_A, O_B (D fp32 columns each). The MMA
-// issue order  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)  lets the tensor core
-// work on one tile while the other tile's softmax runs.
+// issues TMA loads, warp 9 issues tcgen05.mma. TMEM holds S_A, S_B (128 fp32
+// columns each), O_A, O_B (D fp32 columns each) and P_A, P_B (128 bf16 = 64
+// columns each, the A operand of the P.V MMA read straight from TMEM). A
+// softmax warpgroup frees its S buffer as soon as S is in registers, so the
+// MMA warp computes S(j+1) = Q.K(j+1)^T while tile j's exponentials run.
+//
+// At head dim 64 the exponentials (MUFU, 16/clk/SM) cost more than the MMAs,
+// so the two warpgroups take turns on them (A_j, B_j, A_j+1, ...): each
+// group's TMEM traffic and waits overlap the other's exponential phase.
 //
 // O is rescaled lazily: a row keeps its stale max until the new max exceeds
 // it by more than 8 (log2 units), so P stays <= 256 and the TMEM read-modify-
@@ -22,6 +26,25 @@
 #include "common.h"
 #include "flash.h"
 #include "sm100.cuh"
+#include "softmax_math.cuh"
+
+// Optional phase tracing for kernel tuning: built with -DDGX_TRACE, CTA 0
+// records clock64() at the marked points into dgx_fwd_trace (read back with
+// dgx_fwd_trace_read). Compiled out otherwise.
+#ifdef DGX_TRACE
+__device__ unsigned long long dgx_fwd_trace[16384];
+#define FWD_TRACE(slot) \
+  do {                  \
+    if (blockIdx.x == 0) dgx_fwd_trace[(slot)] = clock64(); \
+  } while (0)
+extern "C" int dgx_fwd_trace_read(void* dst) {
+  return (int)cudaMemcpyFromSymbol(dst, dgx_fwd_trace, sizeof(dgx_fwd_trace));
+}
+#else
+#define FWD_TRACE(slot) \
+  do {                  \
+  } while (0)
+#endif
 
 namespace dgx {
 
@@ -45,7 +68,7 @@ constexpr int SM_BAR = SM_V + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
 
 // TMEM columns
-constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + DP;
+constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + DP, T_P0 = 384, T_P1 = 448;
 constexpr uint32_t TMEM_COLS = 512;
 
 __device__ __forceinline__ float ex2(float x) {
@@ -56,7 +79,7 @@ __device__ __forceinline__ float ex2(float x) {
 
 struct FwdBars {
   uint64_t q_full, k_full[KV_STAGES], v_full[KV_STAGES], kv_empty[KV_STAGES];
-  uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], turn[2];
   uint32_t tmem_slot;
   int abort;
 };
@@ -94,8 +117,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->s_full[x], 1);
+      mbar_init(&bars->s_free[x], 4);
       mbar_init(&bars->p_full[x], 4);
-      mbar_init(&bars->o_done[x], 1);
+      mbar_init(&bars->pv_done[x], 1);
+      mbar_init(&bars->turn[x], 4);
     }
     bars->abort = 0;
     fence_mbar_init();
@@ -142,7 +167,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------------------------------------------------------- MMA
     if (elect_one_lane()) {
       constexpr uint32_t idesc_s = make_idesc(1, 0, 0, BLOCK_M, BLOCK_N);  // Q.K^T, both K-major
-      constexpr uint32_t idesc_o = make_idesc(1, 0, 1, BLOCK_M, DP);       // P.V, V MN-major
+      constexpr uint32_t idesc_o = make_idesc(1, 0, 1, BLOCK_M, DP);       // P (TMEM) . V (MN-major)
       const uint32_t sq = smem_u32(smem + SM_Q), sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V);
       // Descriptors advance by adding (byte offset >> 4) to the start field.
       auto issue_s = [&](int x, int j) {
@@ -155,10 +180,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       };
       auto issue_pv = [&](int x, int j) {
         const uint64_t dv = sw128_desc(sv + (j % KV_STAGES) * TILE_BYTES, DP * 128, 1024);
-        const uint32_t d = tmem + (x ? T_O1 : T_O0), a = tmem + (x ? T_S1 : T_S0);
+        const uint32_t d = tmem + (x ? T_O1 : T_O0), a = tmem + (x ? T_P1 : T_P0);
 #pragma unroll 1
-        for (int kk = 0; kk < BLOCK_N / 16; ++kk)
+        for (int kk = 0; kk < BLOCK_N / 16; ++kk)  // 16 keys = 8 packed bf16 columns per step
           mma_f16_ts(d, a + kk * 8, dv + 128 * kk, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&bars->pv_done[x]);
       };
       bool ok = mbar_wait(&bars->q_full, 0, wc) && mbar_wait(&bars->k_full[0], 0, wc);
       if (ok) {
@@ -168,25 +194,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       for (int j = 0; ok && j < nB; ++j) {
         const int s = j % KV_STAGES;
+        FWD_TRACE(8192 + j * 8 + 0);
+        if (j + 1 < nB) {
+          if (!(ok = mbar_wait(&bars->k_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, wc))) break;
+          if (j + 1 < nA) {
+            if (!(ok = mbar_wait(&bars->s_free[0], j & 1, wc))) break;
+            tc_fence_after();
+            FWD_TRACE(8192 + j * 8 + 1);
+            issue_s(0, j + 1);
+          }
+          if (!(ok = mbar_wait(&bars->s_free[1], j & 1, wc))) break;
+          tc_fence_after();
+          FWD_TRACE(8192 + j * 8 + 2);
+          issue_s(1, j + 1);
+        }
         if (!(ok = mbar_wait(&bars->v_full[s], (j / KV_STAGES) & 1, wc))) break;
-        const bool next = j + 1 < nB;
         if (j < nA) {
           if (!(ok = mbar_wait(&bars->p_full[0], j & 1, wc))) break;
           tc_fence_after();
+          FWD_TRACE(8192 + j * 8 + 3);
           issue_pv(0, j);
-          if (j == nA - 1) tc_commit(&bars->o_done[0]);
-        }
-        if (next) {
-          if (!(ok = mbar_wait(&bars->k_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, wc))) break;
-          tc_fence_after();
-          if (j + 1 < nA) issue_s(0, j + 1);
         }
         if (!(ok = mbar_wait(&bars->p_full[1], j & 1, wc))) break;
         tc_fence_after();
+        FWD_TRACE(8192 + j * 8 + 4);
         issue_pv(1, j);
         tc_commit(&bars->kv_empty[s]);
-        if (j == nB - 1) tc_commit(&bars->o_done[1]);
-        if (next) issue_s(1, j + 1);
       }
     }
     __syncwarp();
@@ -203,70 +236,96 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t t_s = tmem + lane_off + (x ? T_S1 : T_S0);
     const uint32_t t_o = tmem + lane_off + (x ? T_O1 : T_O0);
     const float sl2 = args.scale * 1.4426950408889634f;  // scores -> log2 units
+    const uint32_t t_p = tmem + lane_off + (x ? T_P1 : T_P0);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
+      const bool trc = (warp & 3) == 0 && lane == 0;
+      const int tb = x * 4096 + j * 8;
+      if (trc) FWD_TRACE(tb + 0);
       if (!(ok = mbar_wait(&bars->s_full[x], j & 1, wc))) break;
+      if (trc) FWD_TRACE(tb + 1);
       tc_fence_after();
       float s[BLOCK_N];
 #pragma unroll
       for (int c = 0; c < BLOCK_N; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&s[c]));
       tmem_ld_wait();
+      // S is in registers: let the MMA warp compute the next S into this buffer.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->s_free[x]);
       const int k0 = j * BLOCK_N;
       const bool need_mask = (args.causal && k0 + BLOCK_N - 1 > q0 + x * BLOCK_M) || (k0 + BLOCK_N > args.S);
-      float mt = -INFINITY;
       if (need_mask) {
-        const int lim = args.causal ? min(qrow, args.S - 1) : args.S - 1;  // last visible key
+        const int lim = (args.causal ? min(qrow, args.S - 1) : args.S - 1) - k0;  // last visible column
 #pragma unroll
-        for (int c = 0; c < BLOCK_N; ++c) {
-          s[c] = (k0 + c <= lim) ? s[c] * sl2 : -INFINITY;
-          mt = fmaxf(mt, s[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < BLOCK_N; ++c) {
-          s[c] *= sl2;
-          mt = fmaxf(mt, s[c]);
-        }
+        for (int c = 0; c < BLOCK_N; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
       }
+      // Row max of the raw scores with 8 independent partial maxima (short
+      // dependency chains); scale > 0, so max(s)*sl2 = max(s*sl2).
+      float pm[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pm[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < BLOCK_N; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+      const float mt = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
       // lazy rescale
       float factor = 1.f;
       if (mt > m_run + RESCALE_LOG2 || m_run == -INFINITY) {
         factor = (m_run == -INFINITY) ? 0.f : ex2(m_run - mt);
         m_run = mt;
       }
-      const float mb = (m_run == -INFINITY) ? 0.f : m_run;
-      float rs = 0.f;
-      uint32_t p[BLOCK_N / 2];
-#pragma unroll
-      for (int c = 0; c < BLOCK_N; c += 2) {
-        const float e0 = ex2(s[c] - mb), e1 = ex2(s[c + 1] - mb);
-        rs += e0 + e1;
-        p[c / 2] = pack_bf16x2(e0, e1);
+      const float nmb = (m_run == -INFINITY) ? 0.f : -m_run;
+      // Exponential phase turn: A_j waits for B_(j-1), B_j waits for A_j.
+      if (x == 0 ? j > 0 : j < ntile[0]) {
+        if (!(ok = mbar_wait(&bars->turn[x], x == 0 ? (j - 1) & 1 : j & 1, wc))) break;
       }
+      if (trc) FWD_TRACE(tb + 2);
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t p[BLOCK_N / 2];
+      auto step = [&](auto cc) {
+        constexpr int c = decltype(cc)::value;
+        const float e0 = ex2_col<c, DGX_EXP_EMU_FWD>(fmaf(s[c], sl2, nmb)), e1 = ex2_col<c + 1, DGX_EXP_EMU_FWD>(fmaf(s[c + 1], sl2, nmb));
+        ps[(c >> 1) & 7] += e0 + e1;
+        p[c / 2] = pack_bf16x2_fast(e0, e1);
+      };
+      static_for<0, BLOCK_N, 2>(step);
+      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      if (trc) FWD_TRACE(tb + 3);
+      // Hand the turn to the other group (B only while A has tiles left).
+      __syncwarp();
+      if (lane == 0 && (x == 0 || j + 1 < ntile[0])) mbar_arrive(&bars->turn[x ^ 1]);
       l_run = l_run * factor + rs;
-      if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
-        // O_x is stable here: S_x(j) completing implies PV_x(j-1) completed.
-        uint32_t o[32];
+      if (j > 0) {
+        // PV(j-1) must be done: it reads the P buffer and accumulates O.
+        if (!(ok = mbar_wait(&bars->pv_done[x], (j - 1) & 1, wc))) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, factor != 1.f)) {
+          uint32_t o[32];
 #pragma unroll
-        for (int c = 0; c < DP; c += 32) {
-          tmem_ld32(t_o + c, o);
-          tmem_ld_wait();
+          for (int c = 0; c < DP; c += 32) {
+            tmem_ld32(t_o + c, o);
+            tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          tmem_st16(t_o + c, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-          tmem_st16(t_o + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+            tmem_st16(t_o + c, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+            tmem_st16(t_o + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+          }
+          tmem_st_wait();
         }
       }
+      if (trc) FWD_TRACE(tb + 4);
 #pragma unroll
-      for (int c = 0; c < BLOCK_N / 2; c += 16) tmem_st16(t_s + c, *reinterpret_cast<uint32_t(*)[16]>(&p[c]));
+      for (int c = 0; c < BLOCK_N / 2; c += 16) tmem_st16(t_p + c, *reinterpret_cast<uint32_t(*)[16]>(&p[c]));
       tmem_st_wait();
+      if (trc) FWD_TRACE(tb + 5);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[x]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && mbar_wait(&bars->o_done[x], 0, wc)) {
+    if (ok && n > 0 && mbar_wait(&bars->pv_done[x], (n - 1) & 1, wc)) {
       tc_fence_after();
       uint32_t o[DP];
 #pragma unroll

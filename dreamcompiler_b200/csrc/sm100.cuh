@@ -119,6 +119,27 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// TMA reduce-add of a shared-memory tile into global memory (fp32 add),
+// tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* smem_src, int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the shared-memory sources of all committed bulk groups have been read.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until all committed bulk groups have completed.
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -256,6 +277,21 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, uint32_t a_major
          | (fmt << 7)           // A format
          | (fmt << 10)          // B format
          | (a_major << 15) | (b_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- compile-time loops
+template <int V>
+struct IntC {
+  static constexpr int value = V;
+};
+// f(IntC<B>), f(IntC<B+S>), ... for indices < E, fully unrolled with the
+// index available as a constant expression.
+template <int B, int E, int S, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (B < E) {
+    f(IntC<B>{});
+    static_for<B + S, E, S>(f);
+  }
 }
 
 // ---------------------------------------------------------------- numerics
