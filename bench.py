@@ -260,6 +260,48 @@ def run_ours(args, rank, world, local_rank):
     return t[0].item(), t[1].item(), bwd_kernel_s, clocks.summary()
 
 
+TP_N = 16384
+
+
+def run_tp_gemm(args, rank, world, local_rank):
+    """BASELINE config 4 at its largest size: bf16 C = A.B, M=N=K=16384, B
+    column-sharded over the ranks (reference widths), the all-gather of C
+    fused into the GEMM epilogue (NVLink peer stores). Strong scaling: the
+    problem is fixed, each rank computes N/world columns. Returns the max over
+    ranks of the per-step time."""
+    import torch
+    import torch.distributed as dist
+    from dreamcompiler_b200 import tp
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    n = TP_N
+    gemm = tp.ColumnParallelGemm(n, n, n, rank, world, out_dtype=torch.bfloat16, device=dev)
+    A = (torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16()
+    B = (torch.randn(n, gemm.ncol, device=dev, generator=g) / n ** 0.5).bfloat16()
+    steps = max(3, min(args.steps, 20))
+    for _ in range(3):
+        gemm(A, B)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        gemm(A, B)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    import dreamcompiler_b200 as dgx
+    dgx.sync_check()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3 / steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    gemm.close()
+    del A, B, gemm
+    torch.cuda.empty_cache()
+    return t.item(), steps
+
+
 def traffic_per_launch():
     """DRAM bytes per flash_bwd_kernel launch from the committed ncu summary
     (profiles/flash_bwd_traffic.json), scaled to this workload's heads."""
@@ -324,6 +366,7 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     elapsed, e2e_s, bwd_kernel_s, clocks = run_ours(args, rank, world, local_rank)
+    tp_s, tp_steps = run_tp_gemm(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -348,6 +391,11 @@ def main():
                 "d2h_bytes_per_step": 4 * BH * S * D * 2,
                 "path": "pinned host bf16 Q,K,V,dO -> dgx_flash_fwd/bwd -> O,dQ,dK,dV to host, 16-head chunks "
                         "pipelined on 3 streams"},
+        "tp_gemm": {"config": f"bf16 C=A.B, M=N=K={TP_N} (BASELINE configs[3]), B column-sharded over {n} "
+                              "GPU(s), all-gather fused into the epilogue (NVLink peer stores)",
+                    "scaling": "strong", "value": 2.0 * TP_N ** 3 / tp_s / 1e12, "unit": "TFLOPS",
+                    "ms_per_step": tp_s * 1e3, "steps": tp_steps,
+                    "per_gpu_frac_of_measured_bf16": 2.0 * TP_N ** 3 / tp_s / 1e12 / n / burst},
         "gpu_launches": 4 * args.steps,
         "clocks": clocks,
     }

@@ -21,6 +21,11 @@ struct GemmArgs {
   float beta;              // C = beta*C + op(A).op(B) (+bias)
   uint32_t* err;           // device error word
   int tiles_m, tiles_n, group_m;  // filled by the launcher
+  // Extra destinations with C's layout (pitch ldc) that receive the same
+  // output, e.g. other GPUs' buffers through NVLink peer mappings (the
+  // tensor-parallel all-gather fused into the epilogue). beta must be 0.
+  void* C_extra[7];
+  int n_extra;
 };
 
 __device__ __forceinline__ float gemm_finish(const GemmArgs& a, int n, float acc, float old) {
@@ -37,14 +42,17 @@ __device__ __forceinline__ void gemm_store_one(const GemmArgs& a, int m, int n, 
     __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(a.C) + off;
     const float old = a.beta != 0.f ? __bfloat162float(*c) : 0.f;
     *c = __float2bfloat16_rn(gemm_finish(a, n, acc, old));
+    for (int e = 0; e < a.n_extra; ++e) reinterpret_cast<__nv_bfloat16*>(a.C_extra[e])[off] = *c;
   } else {
     float* c = reinterpret_cast<float*>(a.C) + off;
     const float old = a.beta != 0.f ? *c : 0.f;
     *c = gemm_finish(a, n, acc, old);
+    for (int e = 0; e < a.n_extra; ++e) reinterpret_cast<float*>(a.C_extra[e])[off] = *c;
   }
 }
 
-// Store 32 consecutive accumulator columns [n0, n0+32) of row m.
+// Store 32 consecutive accumulator columns [n0, n0+32) of row m (to C and
+// to every extra destination).
 __device__ __forceinline__ void gemm_store_row32(const GemmArgs& a, int m, int n0, const float* v) {
   const int nvalid = a.N - n0;
   const long long off = (long long)m * a.ldc + n0;
@@ -61,13 +69,17 @@ __device__ __forceinline__ void gemm_store_row32(const GemmArgs& a, int m, int n
         o.z = gemm_finish(a, n0 + j + 2, v[j + 2], old.z);
         o.w = gemm_finish(a, n0 + j + 3, v[j + 3], old.w);
         *reinterpret_cast<float4*>(row + j) = o;
+        for (int e = 0; e < a.n_extra; ++e)
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.C_extra[e]) + off + j) = o;
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (j < nvalid) {
           const float old = a.beta != 0.f ? row[j] : 0.f;
-          row[j] = gemm_finish(a, n0 + j, v[j], old);
+          const float o = gemm_finish(a, n0 + j, v[j], old);
+          row[j] = o;
+          for (int e = 0; e < a.n_extra; ++e) reinterpret_cast<float*>(a.C_extra[e])[off + j] = o;
         }
     }
   } else {
@@ -85,14 +97,19 @@ __device__ __forceinline__ void gemm_store_row32(const GemmArgs& a, int m, int n
           const float x1 = gemm_finish(a, n0 + j + 2 * h + 1, v[j + 2 * h + 1], __bfloat162float(ob[2 * h + 1]));
           w[h] = pack_bf16x2(x0, x1);
         }
-        *reinterpret_cast<uint4*>(row + j) = make_uint4(w[0], w[1], w[2], w[3]);
+        const uint4 o = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(row + j) = o;
+        for (int e = 0; e < a.n_extra; ++e)
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.C_extra[e]) + off + j) = o;
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (j < nvalid) {
           const float old = a.beta != 0.f ? __bfloat162float(row[j]) : 0.f;
-          row[j] = __float2bfloat16_rn(gemm_finish(a, n0 + j, v[j], old));
+          const __nv_bfloat16 o = __float2bfloat16_rn(gemm_finish(a, n0 + j, v[j], old));
+          row[j] = o;
+          for (int e = 0; e < a.n_extra; ++e) reinterpret_cast<__nv_bfloat16*>(a.C_extra[e])[off + j] = o;
         }
     }
   }

@@ -154,6 +154,11 @@ dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, in
  * Replaces dream_tp_matmul_column (runtime/nn/training.inc:1604-1630), whose
  * "all-gather" is a host copy into Y[:, col:col+ncol].
  */
+/* C_full is complete on every rank when the call's stream reaches the end of
+ * the call (the last step is a bounded cross-rank completion wait; a missing
+ * rank shows up as DGX_ETIMEOUT from dgx_sync_check). It stays valid until
+ * any rank's next dgx_tp_gemm_colsplit, whose stores may land in it: callers
+ * that keep a result while another call starts must synchronise or copy. */
 /* Shard width and first column of `rank`, as dream_tp_matmul_column computes them. */
 void dgx_tp_shard(int N, int world, int rank, int* col0, int* ncol);
 /* Export this rank's C_full + flag buffers as an opaque handle (for exchange). */
