@@ -14,6 +14,8 @@
 //   mode 0 (W8A32): fp32 products and sums, then y = b + scale*acc.
 //   mode 1 (W8A8) : activations pre-quantised per row (dgx_quantize_rows_i8),
 //                   exact int32 dot products with dp4a, y = b + scale*sx*acc.
+#include <mutex>
+
 #include "common.h"
 
 namespace dgx {
@@ -218,3 +220,73 @@ dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, cons
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// dgx_gemm_w8a8_noalloc: the W8A8 layer without any device allocation.
+//
+// The activations quantised per row (int8) and their row scales need
+// somewhere to live between the two kernels. dgx_gemm_w8 takes that space
+// from the library's own buffer, which it grows with cudaMalloc on first use.
+// Some callers cannot let a library allocate: a deployment that hands the
+// whole device memory budget to its own pool at start-up, or a serving loop
+// that must not call cudaMalloc once it runs (cudaMalloc can synchronise the
+// device and take unbounded time). For them the space is this fixed array in
+// the library's own device image, reserved when the library is loaded.
+// ---------------------------------------------------------------------------
+namespace {
+// Largest problem the fixed array serves: B*K quantised activations and B rows.
+constexpr size_t kNoAllocMaxActs = (size_t)4 << 20;  // 4,194,304 int8 values (4 MiB)
+constexpr int kNoAllocMaxRows = 4096;                // row scales (16 KiB)
+}  // namespace
+
+// Every GPU that loads libdgx holds this array (4 MiB + 16 KiB) until the
+// process exits. All calls share it and it keeps the last call's contents.
+static __device__ __align__(256) unsigned char g_w8a8_noalloc_scratch[kNoAllocMaxActs + kNoAllocMaxRows * sizeof(float)];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of the array, per device
+
+// In host code the array's name only stands for it; the kernels need its
+// device address, fetched once per device with that device current.
+dgx_status noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return dgx::cuda_status(e, "dgx_gemm_w8a8_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return dgx::set_error(DGX_EUNSUPPORTED, "dgx_gemm_w8a8_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_w8a8_noalloc_scratch);
+    if (e != cudaSuccess) return dgx::cuda_status(e, "dgx_gemm_w8a8_noalloc: cudaGetSymbolAddress");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = static_cast<unsigned char*>(g_noalloc_addr[dev]);
+  return DGX_OK;
+}
+}  // namespace
+
+extern "C" dgx_status dgx_gemm_w8a8_noalloc(const float* X, const int8_t* W, const float* scale, const float* bias,
+                                            float* Y, int B, int N, int K, void* stream) {
+  if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_w8a8_noalloc: negative size");
+  if (B > kNoAllocMaxRows || (size_t)B * (size_t)K > kNoAllocMaxActs)
+    return set_error(DGX_EINVAL,
+                     "dgx_gemm_w8a8_noalloc: B=%d, K=%d exceeds the fixed scratch (B <= %d and B*K <= %zu); "
+                     "use dgx_gemm_w8 for larger batches",
+                     B, K, kNoAllocMaxRows, kNoAllocMaxActs);
+  if (B == 0 || N == 0) return DGX_OK;
+  if (!X || !W || !scale || !Y) return set_error(DGX_EINVAL, "dgx_gemm_w8a8_noalloc: null pointer");
+  if (((uintptr_t)X | (uintptr_t)W) & 15)
+    return set_error(DGX_EINVAL, "dgx_gemm_w8a8_noalloc: X and W must be 16-byte aligned");
+  unsigned char* base = nullptr;
+  const dgx_status st = noalloc_scratch(&base);
+  if (st != DGX_OK) return st;
+  // Nothing here has to start at zero: the quantiser overwrites the B*K
+  // activations and B scales that the GEMM then reads.
+  int8_t* xq = reinterpret_cast<int8_t*>(base);
+  float* sx = reinterpret_cast<float*>(base + kNoAllocMaxActs);
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = quantize_rows(X, xq, sx, B, K, s);
+  if (e != cudaSuccess) return cuda_status(e, "dgx_gemm_w8a8_noalloc quantize");
+  return cuda_status(w8_gemm(xq, W, scale, bias, sx, Y, nullptr, B, N, K, 1, s), "dgx_gemm_w8a8_noalloc");
+}

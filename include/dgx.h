@@ -139,6 +139,25 @@ size_t dgx_flash_bwd_workspace_size(int BH, int S, int D);
  */
 dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y, int B,
                        int N, int K, int mode, void* stream);
+/*
+ * dgx_gemm_w8 mode 1 (W8A8) for callers that cannot let a library allocate
+ * device memory: a deployment that gives the whole device budget to its own
+ * pool at start-up, or a serving loop that must not call cudaMalloc once it
+ * runs (cudaMalloc can synchronise the device and take unbounded time). It has
+ * no counterpart in the reference.
+ *   Same arguments and result as dgx_gemm_w8(..., mode = 1), without `mode`.
+ *   The quantised activations and row scales live in a fixed array inside
+ *   libdgx's device image (4 MiB + 16 KiB, held on every GPU that loads the
+ *   library until the process exits), so the call allocates nothing.
+ *   Limits: B <= 4096 and B*K <= 4,194,304; larger problems return DGX_EINVAL.
+ *   The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   All calls share the array and it keeps the last call's contents: calls
+ *   that overlap on the GPU (other streams, other host threads) race on it,
+ *   so issue them in order on one stream.
+ */
+dgx_status dgx_gemm_w8a8_noalloc(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y,
+                                 int B, int N, int K, void* stream);
 /* Exact int32 accumulators acc[b,n] = sum_k Xq[b,k]*W[n,k] (the W8A8 core). */
 dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream);
 /* Per-row symmetric quantisation used by mode 1: Xq = clamp(round(X/sx)), sx = max|X_b|/127. */
