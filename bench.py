@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the other configs' numbers (N=1 only)")
     return ap.parse_args()
 
 
@@ -302,6 +303,83 @@ def run_tp_gemm(args, rank, world, local_rank):
     return t.item(), steps
 
 
+def run_secondary(local_rank):
+    """The other BASELINE configs on this GPU, each timed with CUDA events
+    after warm-up (rank 0 at N=1 only):
+      configs[0]  f32 GEMM 1024^3 + dA/dB backward (3xTF32 tcgen05)
+      configs[3]  bf16 GEMM 4096/8192/16384^3, single GPU
+      configs[4]  int8 weight-only dense 4096x4096, B in {1, 16, 256}, both modes
+    Operands that fit in L2 are cycled through enough copies to exceed it."""
+    import torch
+    import dreamcompiler_b200 as dgx
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(5)
+    res = {}
+
+    def timed(fn, iters):
+        for _ in range(3):
+            fn(0)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(iters):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        dgx.sync_check()
+        return e0.elapsed_time(e1) / 1e3 / iters
+
+    # configs[0]: f32 1024^3 forward + backward; 24 operand sets (288 MB) cycle past L2
+    n = 1024
+    sets = [[torch.randn(n, n, device=dev, generator=g) for _ in range(3)] for _ in range(24)]
+    C = torch.empty(n, n, device=dev)
+    dA = torch.empty(n, n, device=dev)
+    dB = torch.empty(n, n, device=dev)
+    ws = torch.empty(dgx.gemm_workspace_size(n, n, n) // 4 + 1, device=dev)
+
+    def f32_step(i):
+        A, B, dC = sets[i % len(sets)]
+        dgx.gemm(A, B, out=C, workspace=ws)
+        dgx.gemm(dC, B, transB=True, out=dA, workspace=ws)
+        dgx.gemm(A, dC, transA=True, out=dB, workspace=ws)
+    t = timed(f32_step, 50)
+    res["config1_f32_gemm_1024_fwd_bwd"] = {"ms_per_step": t * 1e3, "tflops": 6 * n ** 3 / t / 1e12,
+                                            "path": "3xTF32 on tcgen05 kind::tf32 (3 MMAs per K step)"}
+    del sets, C, dA, dB, ws
+
+    # configs[3]: bf16 GEMM sweep, C bf16
+    sweep = {}
+    for n in (4096, 8192, 16384):
+        copies = 4 if n == 4096 else 1   # 4 x 64 MiB of operands > L2 at 4096
+        A = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
+        B = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
+        Cb = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+        t = timed(lambda i: dgx.gemm(A[i % copies], B[i % copies], out=Cb), 20 if n < 16384 else 6)
+        sweep[str(n)] = {"ms": t * 1e3, "tflops": 2 * n ** 3 / t / 1e12}
+        del A, B, Cb
+        torch.cuda.empty_cache()
+    res["config4_bf16_gemm"] = sweep
+
+    # configs[4]: int8 weight-only 4096x4096; 16 weight copies (256 MB) cycle past L2
+    N = K = 4096
+    Ws = [torch.randint(-127, 128, (N, K), device=dev, dtype=torch.int8, generator=g) for _ in range(16)]
+    sc = torch.rand(N, device=dev, generator=g) * 9e-3 + 1e-3
+    bias = torch.randn(N, device=dev, generator=g)
+    w8 = {}
+    for Bn in (1, 16, 256):
+        X = torch.randn(Bn, K, device=dev, generator=g)
+        Y = torch.empty(Bn, N, device=dev)
+        for mode in (0, 1):
+            t = timed(lambda i: dgx.gemm_w8(X, Ws[i % 16], sc, bias, mode=mode, out=Y), 64)
+            byts = N * K + Bn * K * 4 + Bn * N * 4 + N * 8
+            w8[f"B{Bn}_{'w8a32' if mode == 0 else 'w8a8'}"] = {"us": t * 1e6, "gb_s": byts / t / 1e9,
+                                                               "tops": 2 * Bn * N * K / t / 1e12}
+    res["config5_int8_w8"] = w8
+    del Ws
+    torch.cuda.empty_cache()
+    return res
+
+
 def traffic_per_launch():
     """DRAM bytes per flash_bwd_kernel launch from the committed ncu summary
     (profiles/flash_bwd_traffic.json), scaled to this workload's heads."""
@@ -367,6 +445,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     elapsed, e2e_s, bwd_kernel_s, clocks = run_ours(args, rank, world, local_rank)
     tp_s, tp_steps = run_tp_gemm(args, rank, world, local_rank)
+    secondary = run_secondary(local_rank) if world == 1 and not args.no_secondary else None
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -401,6 +480,8 @@ def main():
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if secondary is not None:
+        line["other_configs"] = secondary
     print(json.dumps(line))
 
 
