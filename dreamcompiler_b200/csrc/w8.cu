@@ -5,18 +5,19 @@
 // y[j] = b[j] + sum_k scale*w[j,k]*x[k] in fp32, generalised to a per-output-
 // channel scale and a batch of rows, and run on the device.
 //
-// At the batch sizes the int8 export serves (1..256 rows) the layer streams
-// a [N][K] int8 weight matrix once per call, so the kernel is laid out for
-// HBM: each warp owns two output channels and reads their weight rows with
-// 16-byte loads (16 int8 per lane per step, 512 B per warp per step), the
-// activations come through L1, and the batch is tiled 8 rows per block so a
-// weight byte is loaded once per 8 rows.
-//   mode 0 (W8A32): fp32 products and sums, then y = b + scale*acc.
+// Both modes run on the tensor cores (w8_tc.cu) whenever the weight rows can
+// be fetched by TMA (K a multiple of 16):
+//   mode 0 (W8A32): fp32 activations split exactly into three int8 planes,
+//                   int32 sums combined exactly, y = b + scale*acc rounded once.
 //   mode 1 (W8A8) : activations pre-quantised per row (dgx_quantize_rows_i8),
-//                   exact int32 dot products with dp4a, y = b + scale*sx*acc.
+//                   exact int32 dot products, y = b + scale*sx*acc.
+// The SIMT kernel below serves the other shapes: each warp owns two output
+// channels and reads their weight rows with 16-byte loads, fp32 products and
+// sums in mode 0, dp4a in mode 1.
 #include <mutex>
 
 #include "common.h"
+#include "w8.h"
 
 namespace dgx {
 
@@ -131,8 +132,10 @@ __global__ void __launch_bounds__(256) w8_kernel(const void* __restrict__ X, con
 }
 
 // Per-row symmetric quantisation: sx = max|x|/127, q = clamp(round(x/sx)).
+// Generic form: two passes over the row (any K, any alignment).
 __global__ void quant_rows_kernel(const float* __restrict__ X, int8_t* __restrict__ Xq, float* __restrict__ sx,
                                   int K) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the GEMM may start streaming weights
   __shared__ float red[32];
   const int b = blockIdx.x;
   const float* x = X + (size_t)b * K;
@@ -159,9 +162,54 @@ __global__ void quant_rows_kernel(const float* __restrict__ X, int8_t* __restric
     Xq[(size_t)b * K + k] = (int8_t)v;
   }
 }
+
+// Same quantisation with the row held in registers: one read of the row,
+// every load issued before the first use (K <= 1024*NV, K % 4 == 0, X 16-byte
+// aligned). 256 threads, one CTA per row.
+template <int NV>
+__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const float* __restrict__ X, int8_t* __restrict__ Xq,
+                                                             float* __restrict__ sx, int K) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ float red[8];
+  const int b = blockIdx.x;
+  const float* x = X + (size_t)b * K;
+  float4 v[NV];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int k = (threadIdx.x + 256 * j) * 4;
+    v[j] = k < K ? __ldg(reinterpret_cast<const float4*>(x + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+#pragma unroll
+  for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+  const float s = m > 0.f ? m / 127.f : 1.f;
+  const float inv = 1.f / s;
+  if (threadIdx.x == 0) sx[b] = s;
+  auto q = [&](float f) { return (int8_t)fminf(127.f, fmaxf(-127.f, roundf(f * inv))); };
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int k = (threadIdx.x + 256 * j) * 4;
+    if (k < K) {
+      char4 c;
+      c.x = q(v[j].x);
+      c.y = q(v[j].y);
+      c.z = q(v[j].z);
+      c.w = q(v[j].w);
+      *reinterpret_cast<char4*>(Xq + (size_t)b * K + k) = c;
+    }
+  }
+}
 }  // namespace
 
-cudaError_t w8_gemm(const void* X, const int8_t* W, const float* scale, const float* bias, const float* sx,
+cudaError_t w8_simt(const void* X, const int8_t* W, const float* scale, const float* bias, const float* sx,
                     float* Y, int32_t* acc, int B, int N, int K, int mode, cudaStream_t s) {
   dim3 grid((N + WARPS * CPW - 1) / (WARPS * CPW), (B + BT - 1) / BT);
   if (mode == 0)
@@ -172,8 +220,27 @@ cudaError_t w8_gemm(const void* X, const int8_t* W, const float* scale, const fl
 }
 
 cudaError_t quantize_rows(const float* X, int8_t* Xq, float* sx, int B, int K, cudaStream_t s) {
-  quant_rows_kernel<<<B, 256, 0, s>>>(X, Xq, sx, K);
+  const bool vec = K % 4 == 0 && (((uintptr_t)X | (uintptr_t)Xq) & 15) == 0;
+  if (vec && K <= 1024)
+    quant_rows_reg_kernel<1><<<B, 256, 0, s>>>(X, Xq, sx, K);
+  else if (vec && K <= 2048)
+    quant_rows_reg_kernel<2><<<B, 256, 0, s>>>(X, Xq, sx, K);
+  else if (vec && K <= 4096)
+    quant_rows_reg_kernel<4><<<B, 256, 0, s>>>(X, Xq, sx, K);
+  else if (vec && K <= 8192)
+    quant_rows_reg_kernel<8><<<B, 256, 0, s>>>(X, Xq, sx, K);
+  else
+    quant_rows_kernel<<<B, 256, 0, s>>>(X, Xq, sx, K);
   return cudaGetLastError();
+}
+
+// W8A8 from already quantised activations: tensor cores when TMA can fetch
+// the rows, else the SIMT kernel.
+cudaError_t w8a8_from_q(const int8_t* xq, const int8_t* W, const float* scale, const float* bias, const float* sx,
+                        float* Y, int32_t* acc, int B, int N, int K, bool after_quant, cudaStream_t s) {
+  if (K % 16 == 0 && K <= kW8MaxK)
+    return w8_tc_gemm(xq, 1, W, scale, bias, sx, Y, acc, B, N, K, after_quant, s);
+  return w8_simt(xq, W, scale, bias, sx, Y, acc, B, N, K, 1, s);
 }
 
 }  // namespace dgx
@@ -194,7 +261,7 @@ dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B
   if (B == 0 || N == 0) return DGX_OK;
   if (!Xq || !W || !acc) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: null pointer");
   if (((uintptr_t)Xq | (uintptr_t)W) & 15) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: pointers must be 16-byte aligned");
-  return cuda_status(w8_gemm(Xq, W, nullptr, nullptr, nullptr, nullptr, acc, B, N, K, 1, (cudaStream_t)stream),
+  return cuda_status(w8a8_from_q(Xq, W, nullptr, nullptr, nullptr, nullptr, acc, B, N, K, false, (cudaStream_t)stream),
                      "dgx_gemm_i8i32");
 }
 
@@ -206,17 +273,24 @@ dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, cons
   if (!X || !W || !scale || !Y) return set_error(DGX_EINVAL, "dgx_gemm_w8: null pointer");
   if (((uintptr_t)X | (uintptr_t)W) & 15) return set_error(DGX_EINVAL, "dgx_gemm_w8: X and W must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
-  if (mode == 0)
-    return cuda_status(w8_gemm(X, W, scale, bias, nullptr, Y, nullptr, B, N, K, 0, s), "dgx_gemm_w8");
-  // W8A8: quantised activations + row scales in library scratch.
-  const size_t xq_bytes = ((size_t)B * K + 255) & ~size_t(255);
+  if (mode == 0 && (K % 16 != 0 || K > kW8MaxK))
+    return cuda_status(w8_simt(X, W, scale, bias, nullptr, Y, nullptr, B, N, K, 0, s), "dgx_gemm_w8");
+  // Library scratch: the int8 activation planes (3 for W8A32, 1 for W8A8)
+  // and one fp32 scale per row.
+  const int planes = mode == 0 ? 3 : 1;
+  const size_t xq_bytes = ((size_t)planes * B * K + 255) & ~size_t(255);
   uint8_t* ws = (uint8_t*)library_scratch(xq_bytes + (size_t)B * sizeof(float), s);
   if (!ws) return set_error(DGX_ENOMEM, "dgx_gemm_w8: scratch");
   int8_t* xq = reinterpret_cast<int8_t*>(ws);
-  float* sx = reinterpret_cast<float*>(ws + xq_bytes);
-  cudaError_t e = quantize_rows(X, xq, sx, B, K, s);
+  float* rs = reinterpret_cast<float*>(ws + xq_bytes);
+  if (mode == 0) {
+    cudaError_t e = w8_split_planes(X, xq, rs, B, K, s);
+    if (e != cudaSuccess) return cuda_status(e, "dgx_gemm_w8 split");
+    return cuda_status(w8_tc_gemm(xq, 3, W, scale, bias, rs, Y, nullptr, B, N, K, true, s), "dgx_gemm_w8");
+  }
+  cudaError_t e = quantize_rows(X, xq, rs, B, K, s);
   if (e != cudaSuccess) return cuda_status(e, "dgx_gemm_w8 quantize");
-  return cuda_status(w8_gemm(xq, W, scale, bias, sx, Y, nullptr, B, N, K, 1, s), "dgx_gemm_w8");
+  return cuda_status(w8a8_from_q(xq, W, scale, bias, rs, Y, nullptr, B, N, K, true, s), "dgx_gemm_w8");
 }
 
 }  // extern "C"
@@ -288,5 +362,5 @@ extern "C" dgx_status dgx_gemm_w8a8_noalloc(const float* X, const int8_t* W, con
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = quantize_rows(X, xq, sx, B, K, s);
   if (e != cudaSuccess) return cuda_status(e, "dgx_gemm_w8a8_noalloc quantize");
-  return cuda_status(w8_gemm(xq, W, scale, bias, sx, Y, nullptr, B, N, K, 1, s), "dgx_gemm_w8a8_noalloc");
+  return cuda_status(w8a8_from_q(xq, W, scale, bias, sx, Y, nullptr, B, N, K, true, s), "dgx_gemm_w8a8_noalloc");
 }

@@ -1,0 +1,31 @@
+// Internal interface between the int8 dense-layer translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dgx {
+
+// Largest K for which the exact int32 accumulators of the tensor-core path
+// cannot overflow: |w*q| <= 128*127 per product.
+constexpr int kW8MaxK = 131072;
+
+// Y[b,n] (and/or acc_out[b,n]) from int8 activation planes Xp[planes][B][K]
+// and int8 weights W[N][K] on the tensor cores (tcgen05 kind::i8).
+//   planes == 1: acc = sum_k Xp[0][b][k]*W[n][k] (exact int32);
+//                acc_out <- acc, Y <- bias + scale[n]*rowscale[b]*acc.
+//   planes == 3: the three int8 planes of an exact fixed-point split of fp32
+//                activations (x = rowscale[b]*(q0 + q1/2^7 + q2/2^14 + r));
+//                Y <- bias + scale[n]*rowscale[b]*(A0 + A1/2^7 + A2/2^14).
+// K % 16 == 0, Xp and W 16-byte aligned. `after_producer` launches the
+// kernel as a programmatic dependent of the kernel just issued on `s`: the
+// weight stream starts before that kernel (which writes Xp and rowscale)
+// has finished.
+cudaError_t w8_tc_gemm(const int8_t* Xp, int planes, const int8_t* W, const float* scale, const float* bias,
+                       const float* rowscale, float* Y, int32_t* acc_out, int B, int N, int K,
+                       bool after_producer, cudaStream_t s);
+
+// Split fp32 rows into the three int8 planes above (Xp[3][B][K]) and the
+// power-of-two row scales. K % 16 == 0.
+cudaError_t w8_split_planes(const float* X, int8_t* Xp, float* rowscale, int B, int K, cudaStream_t s);
+
+}  // namespace dgx

@@ -64,3 +64,57 @@ def test_per_tensor_export_semantics(dgx, orc):
     Y = dgx.gemm_w8(*(torch.from_numpy(a).cuda() for a in (X, q, sc, b)), mode=0)
     dgx.sync_check()
     assert normwise(Y.cpu().numpy(), orc.dense_q(X, q, sc, b)) < 1e-5
+
+
+@pytest.mark.parametrize("B,N,K", [
+    (3, 200, 48),       # one K block, ragged N, 3 plane rows padded to 16
+    (33, 130, 4112),    # K % 128 != 0 (zero-filled tail), 2 output tiles, cluster split-K
+    (100, 4096, 1024),  # W8A32: two activation chunks of 64 rows
+    (300, 257, 256),    # W8A8: two chunks of 160 rows; W8A32: four of 80
+    (17, 384, 8192),    # 8-way cluster split-K
+    (2, 128, 20480),    # K beyond the register-resident pre-passes (looping forms)
+    (40, 12804, 128),   # unsplit, TMA-stored output tiles, last tile 4 channels wide
+])
+def test_tensor_core_partitions(dgx, orc, B, N, K):
+    """Shapes that exercise each way the tensor-core path divides the work:
+    cluster split-K with the DSMEM reduction, activation chunks, tails."""
+    X, W, sc, b = inputs(orc, B, N, K, seed=B * 7 + N + K)
+    Xd, Wd, scd, bd = (torch.from_numpy(a).cuda() for a in (X, W, sc, b))
+    Y0 = dgx.gemm_w8(Xd, Wd, scd, bd, mode=0)
+    Y1 = dgx.gemm_w8(Xd, Wd, scd, bd, mode=1)
+    Xq, sx = dgx.quantize_rows_i8(Xd)
+    acc = dgx.gemm_i8i32(Xq, Wd)
+    dgx.sync_check()
+    assert normwise(Y0.cpu().numpy(), orc.dense_q(X, W, sc, b)) < 1e-5
+    rXq, rsx = orc.quantize_rows(X)
+    racc = orc.i8_gemm(rXq, W)
+    assert np.array_equal(acc.cpu().numpy(), racc)
+    ref1 = b.astype(np.float64) + sc.astype(np.float64) * rsx.astype(np.float64)[:, None] * racc
+    assert normwise(Y1.cpu().numpy(), ref1) < 1e-6
+
+
+def test_w8a32_extreme_rows(dgx, orc):
+    """Rows spanning the fp32 range (tiny, huge, all-zero, a single spike):
+    the power-of-two row scale keeps the plane split exact for each."""
+    B, N, K = 6, 256, 512
+    rng = np.random.default_rng(5)
+    X = rng.standard_normal((B, K)).astype(np.float32)
+    X[0] *= np.float32(1e-30)
+    X[1] *= np.float32(1e30)
+    X[2] = 0
+    X[3] = 0
+    X[3, 77] = -3.5
+    X[4, ::2] = 0
+    W = rng.integers(-128, 128, (N, K)).astype(np.int8)  # includes -128
+    sc = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    b = np.zeros(N, np.float32)  # no bias: a 1e-29 output must stay visible
+    Y = dgx.gemm_w8(*(torch.from_numpy(a).cuda() for a in (X, W, sc, b)), mode=0)
+    dgx.sync_check()
+    ref = sc.astype(np.float64) * (X.astype(np.float64) @ W.T.astype(np.float64))
+    Yh = Y.cpu().numpy().astype(np.float64)
+    for r in range(B):
+        nr = np.linalg.norm(ref[r])
+        if nr == 0:
+            assert not Yh[r].any(), r
+        else:
+            assert np.linalg.norm(Yh[r] - ref[r]) / nr < 1e-5, r
