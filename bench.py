@@ -316,18 +316,31 @@ def run_secondary(local_rank):
     g = torch.Generator(device=dev).manual_seed(5)
     res = {}
 
-    def timed(fn, iters):
-        for _ in range(3):
-            fn(0)
+    def timed(fn, iters, reps=5):
+        """Device time per call: `iters` calls captured in one CUDA graph
+        (so microsecond kernels are not measured as Python launch overhead),
+        replayed `reps` times between CUDA events after warm-up."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn(0)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(iters):
+                fn(i)
+        graph.replay()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for i in range(iters):
-            fn(i)
+        for _ in range(reps):
+            graph.replay()
         e1.record()
         torch.cuda.synchronize(dev)
         dgx.sync_check()
-        return e0.elapsed_time(e1) / 1e3 / iters
+        del graph
+        return e0.elapsed_time(e1) / 1e3 / (iters * reps)
 
     # configs[0]: f32 1024^3 forward + backward; 24 operand sets (288 MB) cycle past L2
     n = 1024

@@ -18,6 +18,8 @@
 // 3xTF32 split (a = a_hi + a_lo, C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi) on
 // kind::tf32, which keeps the error near fp32 level (<= 1e-4 normwise); the
 // hi/lo planes are produced by `split_tf32_kernel` into caller-visible scratch.
+#include <algorithm>
+
 #include "sm100.cuh"
 #include "gemm.h"
 
@@ -26,10 +28,12 @@ namespace dgx {
 // ---------------------------------------------------------------------------
 // Tile configuration
 // ---------------------------------------------------------------------------
-template <bool TF32>
+// BN_: the default output tile width (256 bf16 / 128 tf32), or half of it for
+// problems whose default tiles would leave SMs idle.
+template <bool TF32, int BN_ = (TF32 ? 128 : 256)>
 struct GemmCfg {
   static constexpr int BM = 128;
-  static constexpr int BN = TF32 ? 128 : 256;
+  static constexpr int BN = BN_;
   static constexpr int ESZ = TF32 ? 4 : 2;                 // bytes per element
   static constexpr int BK = 128 / ESZ;                       // one 128-byte swizzle row of K
   static constexpr int MMA_K = 32 / ESZ;                     // K per tcgen05.mma (32 bytes)
@@ -37,7 +41,7 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * ESZ;              // 32 KB (bf16) / 16 KB (tf32)
   static constexpr int PLANES = TF32 ? 2 : 1;                // hi (+ lo) planes per operand
   static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = TF32 ? 3 : 4;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;                   // double-buffered accumulator
   static constexpr int CHUNK = 128 / ESZ;                    // MN elements per 128-byte chunk
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
@@ -66,12 +70,12 @@ __device__ __forceinline__ uint32_t kstep_offset(int kk) {
   return MN ? (uint32_t)kk * (32 / ESZ) * 128 : (uint32_t)kk * 32;
 }
 
-template <bool TF32, bool A_MN, bool B_MN>
+template <bool TF32, bool A_MN, bool B_MN, int BN_>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    GemmArgs args) {
-  using Cfg = GemmCfg<TF32>;
+  using Cfg = GemmCfg<TF32, BN_>;
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -252,10 +256,22 @@ __global__ void __launch_bounds__(192, 1)
 // produce. `src_t` = the source is stored [K][rows] (transposed); a 32x32
 // shared-memory tile keeps both the read and the write coalesced.
 // ---------------------------------------------------------------------------
-__global__ void split_tf32_kernel(const float* __restrict__ x, int rows, int K, int ld, int src_t,
-                                  float* __restrict__ hi, float* __restrict__ lo, int kpad) {
+struct SplitJob {
+  const float* x;
+  int rows, ld, src_t;
+  float* hi;
+  float* lo;
+};
+// blockIdx.z selects the operand: both are split by one launch.
+__global__ void split_tf32_kernel(SplitJob ja, SplitJob jb, int K, int kpad) {
   __shared__ float tile[32][33];
+  const SplitJob& j = blockIdx.z == 0 ? ja : jb;
+  const float* __restrict__ x = j.x;
+  float* __restrict__ hi = j.hi;
+  float* __restrict__ lo = j.lo;
+  const int rows = j.rows, ld = j.ld, src_t = j.src_t;
   const int r0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
+  if (r0 >= rows) return;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
   for (int i = ty; i < 32; i += 8) {
     float v = 0.f;
@@ -366,7 +382,7 @@ static bool encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt
 template <bool TF32>
 static bool make_operand_map(CUtensorMap* map, const void* base, bool mn_major, int mn, int K, int ld,
                              int box_mn) {
-  using Cfg = GemmCfg<TF32>;
+  using Cfg = GemmCfg<TF32>;  // element size, BK and the MN chunk do not depend on the tile width
   const CUtensorMapDataType dt = TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint64_t pitch = (uint64_t)ld * Cfg::ESZ;
   if (mn_major) return encode_2d(map, base, dt, Cfg::ESZ, (uint64_t)mn, (uint64_t)K, pitch, Cfg::CHUNK, Cfg::BK);
@@ -381,10 +397,10 @@ int gemm_tc_supported(const GemmArgs& a, int esz, const void* A, const void* B) 
   return 1;
 }
 
-template <bool TF32, bool A_MN, bool B_MN>
-static cudaError_t launch_tc(const GemmArgs& args, const void* A, const void* B, const void* A2, const void* B2,
+template <bool TF32, bool A_MN, bool B_MN, int BN_>
+static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void* B, const void* A2, const void* B2,
                              cudaStream_t stream) {
-  using Cfg = GemmCfg<TF32>;
+  using Cfg = GemmCfg<TF32, BN_>;
   CUtensorMap ma{}, mb{}, ma2{}, mb2{};
   if (!make_operand_map<TF32>(&ma, A, A_MN, args.M, args.K, args.lda, Cfg::BM)) return cudaErrorInvalidValue;
   if (!make_operand_map<TF32>(&mb, B, B_MN, args.N, args.K, args.ldb, Cfg::BN)) return cudaErrorInvalidValue;
@@ -399,7 +415,7 @@ static cudaError_t launch_tc(const GemmArgs& args, const void* A, const void* B,
   a.tiles_m = (args.M + Cfg::BM - 1) / Cfg::BM;
   a.tiles_n = (args.N + Cfg::BN - 1) / Cfg::BN;
   a.group_m = 16;
-  auto kern = gemm_tc_kernel<TF32, A_MN, B_MN>;
+  auto kern = gemm_tc_kernel<TF32, A_MN, B_MN, BN_>;
   static bool attr_done = false;  // per template instantiation
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
@@ -413,6 +429,19 @@ static cudaError_t launch_tc(const GemmArgs& args, const void* A, const void* B,
     kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, a);
   }
   return cudaGetLastError();
+}
+
+// Full-width tiles, or half-width ones when the full-width tiles would leave
+// more than a quarter of the SMs idle (small problems such as the 1024^3
+// f32 GEMMs of the autograd step).
+template <bool TF32, bool A_MN, bool B_MN>
+static cudaError_t launch_tc(const GemmArgs& args, const void* A, const void* B, const void* A2, const void* B2,
+                             cudaStream_t stream) {
+  constexpr int BN_FULL = GemmCfg<TF32>::BN;
+  const long long tiles = (long long)((args.M + 127) / 128) * ((args.N + BN_FULL - 1) / BN_FULL);
+  if (tiles * 4 < (long long)num_sms() * 3)
+    return launch_tc_bn<TF32, A_MN, B_MN, BN_FULL / 2>(args, A, B, A2, B2, stream);
+  return launch_tc_bn<TF32, A_MN, B_MN, BN_FULL>(args, A, B, A2, B2, stream);
 }
 
 template <bool TF32>
@@ -445,9 +474,10 @@ cudaError_t gemm_f32_3xtf32(const GemmArgs& args, const float* A, const float* B
   float* a_lo = a_hi + (size_t)args.M * kp;
   float* b_hi = a_lo + (size_t)args.M * kp;
   float* b_lo = b_hi + (size_t)args.N * kp;
-  dim3 ga((kp + 31) / 32, (args.M + 31) / 32), gb((kp + 31) / 32, (args.N + 31) / 32);
-  split_tf32_kernel<<<ga, 256, 0, s>>>(A, args.M, args.K, args.lda, args.transA, a_hi, a_lo, kp);
-  split_tf32_kernel<<<gb, 256, 0, s>>>(B, args.N, args.K, args.ldb, !args.transB, b_hi, b_lo, kp);
+  const SplitJob ja{A, args.M, args.lda, args.transA, a_hi, a_lo};
+  const SplitJob jb{B, args.N, args.ldb, !args.transB, b_hi, b_lo};
+  dim3 grid((kp + 31) / 32, (std::max(args.M, args.N) + 31) / 32, 2);
+  split_tf32_kernel<<<grid, 256, 0, s>>>(ja, jb, args.K, kp);
   GemmArgs a = args;
   a.K = kp;  // zero-filled tail contributes nothing
   a.lda = kp;
