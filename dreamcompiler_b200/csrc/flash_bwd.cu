@@ -9,8 +9,11 @@
 //   P = exp(scale*QK^T - LSE),  dV = P^T dO,  dP = dO V^T,
 //   dS = P o (dP - D),  dQ = scale * dS K,  dK = scale * dS^T Q.
 //
-// One CTA keeps a 128-key K/V tile resident and walks the 128-row Q tiles
-// that can see it (causal: i >= j). Per Q tile the MMA warp issues
+// The kernel is persistent (one CTA per SM). Each work item is one 128-key
+// K/V tile of one head, kept resident in shared memory (two buffers, so the
+// next item's tile loads during the current one) while the CTA walks the
+// 128-row Q tiles that can see it (causal: i >= j). Per Q tile the MMA warp
+// issues
 //   S^T = K Q^T, dP^T = V dO^T           (TMEM, lanes = keys)
 //   dV += P^T dO, dK += dS^T Q           (P^T, dS^T read from TMEM)
 //   dQ_part = dS K                       (dS staged in shared memory)
@@ -58,7 +61,7 @@ constexpr int NUM_THREADS = 512;    // WG0-1 compute, WG2 dQ drain, WG3: TMA war
 // setmaxnreg split (per thread): 2 x 184 + 96 + 40 = 504 <= 512 = 65536 / 128.
 constexpr uint32_t REG_COMPUTE = 184, REG_DRAIN = 96, REG_CTRL = 40;
 
-constexpr int SM_K = 0, SM_V = TILE, SM_Q = 2 * TILE, SM_DO = SM_Q + Q_STAGES * TILE;
+constexpr int SM_K = 0, SM_V = 2 * TILE, SM_Q = 4 * TILE, SM_DO = SM_Q + Q_STAGES * TILE;  // K, V: 2 buffers
 constexpr int SM_DS = SM_DO + Q_STAGES * TILE;  // 128 queries x 128 keys bf16, MN-major (2 x 16 KB)
 constexpr int SM_STAT = SM_DS + 2 * TILE;  // per stage: L2 stats [128] then D stats [128] (fp32)
 constexpr int STAT_BYTES = 2 * BQ * 4;
@@ -78,7 +81,7 @@ __device__ __forceinline__ float ex2(float x) {
 
 
 struct BwdBars {
-  uint64_t kv_full, q_full[Q_STAGES], q_empty[Q_STAGES];
+  uint64_t kv_full[2], kv_empty[2], q_full[Q_STAGES], q_empty[Q_STAGES];
   uint64_t s_full, dp_full, p_ready, ds_ready, dq_full[2], dq_empty[2], acc_done;
   uint32_t tmem_slot;
   int abort;
@@ -94,17 +97,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WaitCtx wc{&bars->abort, args.err};
 
+  // Persistent: this CTA walks work items w = blockIdx.x, +gridDim.x, ...;
+  // item w is key tile j = w / BH of head bh = w % BH (heaviest first under
+  // causal). Barrier phases run on across items: `ic` counts this CTA's
+  // items, `gt` its Q tiles.
   const int nq = (args.S + BQ - 1) / BQ;
-  const int j = blockIdx.x / args.BH;  // key tile (heaviest first under causal)
-  const int bh = blockIdx.x % args.BH;
-  const int i0 = args.causal ? (j * BKV) / BQ : 0;
-  const int n = nq - i0;  // Q tiles this CTA walks
-  const size_t row0 = (size_t)bh * args.S;
-  const float* Dstat = args.rowstat + (size_t)bh * args.Spad;
-  const float* L2stat = args.rowstat + (size_t)args.BH * args.Spad + (size_t)bh * args.Spad;
+  const int nitems = ((args.S + BKV - 1) / BKV) * args.BH;
+  struct Item {
+    int j, bh, i0, n;
+  };
+  auto item = [&](int w) {
+    Item it;
+    it.j = w / args.BH;
+    it.bh = w % args.BH;
+    it.i0 = args.causal ? (it.j * BKV) / BQ : 0;
+    it.n = nq - it.i0;
+    return it;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->kv_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->kv_full[b], 1);
+      mbar_init(&bars->kv_empty[b], 1);
+    }
     for (int s = 0; s < Q_STAGES; ++s) {
       mbar_init(&bars->q_full[s], 1);
       mbar_init(&bars->q_empty[s], 1);
@@ -141,22 +156,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmdO);
-      mbar_arrive_expect_tx(&bars->kv_full, 2 * TILE);
-      tma_load_3d(smem + SM_K, &tmK, &bars->kv_full, 0, j * BKV, bh);
-      tma_load_3d(smem + SM_V, &tmV, &bars->kv_full, 0, j * BKV, bh);
-      int it = 0;
-      for (; it < n; ++it) {
-        const int s = it % Q_STAGES;
-        if (!mbar_wait(&bars->q_empty[s], ((it / Q_STAGES) & 1) ^ 1, wc)) break;
-        mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE + STAT_BYTES);
-        tma_load_3d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, (i0 + it) * BQ, bh);
-        tma_load_3d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, (i0 + it) * BQ, bh);
-        uint8_t* st = smem + SM_STAT + s * STAT_BYTES;
-        bulk_load(st, L2stat + (i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
-        bulk_load(st + BQ * 4, Dstat + (i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
+      int gt = 0, ic = 0;
+      bool ok = true;
+      uint32_t kv_filled = 0;  // items whose K/V load was issued
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+        const Item I = item(w);
+        const int kb = ic & 1;
+        if (!(ok = mbar_wait(&bars->kv_empty[kb], ((ic >> 1) & 1) ^ 1, wc))) break;
+        mbar_arrive_expect_tx(&bars->kv_full[kb], 2 * TILE);
+        tma_load_3d(smem + SM_K + kb * TILE, &tmK, &bars->kv_full[kb], 0, I.j * BKV, I.bh);
+        tma_load_3d(smem + SM_V + kb * TILE, &tmV, &bars->kv_full[kb], 0, I.j * BKV, I.bh);
+        ++kv_filled;
+        const float* Dstat = args.rowstat + (size_t)I.bh * args.Spad;
+        const float* L2stat = args.rowstat + (size_t)args.BH * args.Spad + (size_t)I.bh * args.Spad;
+        for (int it = 0; it < I.n; ++it, ++gt) {
+          const int s = gt % Q_STAGES;
+          if (!(ok = mbar_wait(&bars->q_empty[s], ((gt / Q_STAGES) & 1) ^ 1, wc))) break;
+          mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE + STAT_BYTES);
+          tma_load_3d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
+          tma_load_3d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
+          uint8_t* st = smem + SM_STAT + s * STAT_BYTES;
+          bulk_load(st, L2stat + (I.i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
+          bulk_load(st + BQ * 4, Dstat + (I.i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
+        }
       }
-      mbar_drain(&bars->kv_full, 0);
-      for (int f = max(0, it - Q_STAGES); f < it; ++f) mbar_drain(&bars->q_full[f % Q_STAGES], (f / Q_STAGES) & 1);
+      // Teardown: every copy issued must have landed before the CTA leaves.
+      for (uint32_t f = kv_filled > 2 ? kv_filled - 2 : 0; f < kv_filled; ++f) mbar_drain(&bars->kv_full[f & 1], (f >> 1) & 1);
+      for (int f = max(0, gt - Q_STAGES); f < gt; ++f) mbar_drain(&bars->q_full[f % Q_STAGES], (f / Q_STAGES) & 1);
     }
   } else if (warp == 13) {
     // ---------------------------------------------------------------- MMA
@@ -164,7 +190,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);   // K-major x K-major, N = 128 queries
       constexpr uint32_t id_acc = make_idesc(1, 0, 1, 128, DP);  // TMEM A x MN-major B, N = D
       constexpr uint32_t id_dq = make_idesc(1, 1, 1, 128, DP);   // MN-major dS x MN-major K
-      const uint32_t sK = smem_u32(smem + SM_K), sV = smem_u32(smem + SM_V);
       const uint32_t sQ = smem_u32(smem + SM_Q), sdO = smem_u32(smem + SM_DO), sdS = smem_u32(smem + SM_DS);
       // Descriptors advance by adding (byte offset >> 4) to the start field.
       auto kmajor_pair = [&](uint32_t d, uint32_t a, uint32_t b) {  // d = a . b^T over D
@@ -178,53 +203,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int kk = 0; kk < BQ / 16; ++kk)
           mma_f16_ts(d, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), db + 128 * kk, id_acc, (!first || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars->kv_full, 0, wc) && mbar_wait(&bars->q_full[0], 0, wc);
-      if (ok) {
+      int gt = 0, ic = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+        const Item I = item(w);
+        const int kb = ic & 1;
+        const uint32_t sK = smem_u32(smem + SM_K + kb * TILE), sV = smem_u32(smem + SM_V + kb * TILE);
+        // S^T and dP^T of the item's first tile: their TMEM was last read by
+        // the previous item's final dV / dK MMAs, issued before them.
+        if (!(ok = mbar_wait(&bars->kv_full[kb], (ic >> 1) & 1, wc) &&
+                   mbar_wait(&bars->q_full[gt % Q_STAGES], (gt / Q_STAGES) & 1, wc)))
+          break;
         tc_fence_after();
-        kmajor_pair(tmem + T_ST, sK, sQ);
+        kmajor_pair(tmem + T_ST, sK, sQ + (gt % Q_STAGES) * TILE);
         tc_commit(&bars->s_full);
-        kmajor_pair(tmem + T_DPT, sV, sdO);
+        kmajor_pair(tmem + T_DPT, sV, sdO + (gt % Q_STAGES) * TILE);
         tc_commit(&bars->dp_full);
-      }
-      for (int it = 0; ok && it < n; ++it) {
-        const int s = it % Q_STAGES;
-        const uint32_t q_s = sQ + s * TILE, do_s = sdO + s * TILE;
-        const bool next = it + 1 < n;
-        const int s1 = (it + 1) % Q_STAGES;
-        BWD_TRACE(8192 + it * 8 + 0);
-        if (!(ok = mbar_wait(&bars->p_ready, it & 1, wc))) break;
-        BWD_TRACE(8192 + it * 8 + 1);
-        tc_fence_after();
-        tmem_a_acc(tmem + T_DV, tmem + T_ST, do_s, it == 0);  // dV += P^T dO
-        if (next) {
-          if (!(ok = mbar_wait(&bars->q_full[s1], ((it + 1) / Q_STAGES) & 1, wc))) break;
+        for (int it = 0; it < I.n; ++it, ++gt) {
+          const int s = gt % Q_STAGES;
+          const uint32_t q_s = sQ + s * TILE, do_s = sdO + s * TILE;
+          const bool next = it + 1 < I.n;
+          const int s1 = (gt + 1) % Q_STAGES;
+          // p_ready of an item's first tile also means the compute warps have
+          // read out the previous item's dV / dK, so dV(0) may overwrite them.
+          if (!(ok = mbar_wait(&bars->p_ready, gt & 1, wc))) break;
           tc_fence_after();
-          kmajor_pair(tmem + T_ST, sK, sQ + s1 * TILE);  // S^T(i+1)
-          tc_commit(&bars->s_full);
-        }
-        BWD_TRACE(8192 + it * 8 + 2);
-        if (!(ok = mbar_wait(&bars->ds_ready, it & 1, wc))) break;
-        BWD_TRACE(8192 + it * 8 + 3);
-        tc_fence_after();
-        tmem_a_acc(tmem + T_DK, tmem + T_DPT, q_s, it == 0);  // dK += dS^T Q
-        const int b = it & 1;
-        if (!(ok = mbar_wait(&bars->dq_empty[b], ((it >> 1) & 1) ^ 1, wc))) break;
-        BWD_TRACE(8192 + it * 8 + 4);
-        tc_fence_after();
-        {
-          const uint64_t da = sw128_desc(sdS, BKV * 128, 1024), dk = sw128_desc(sK, DP * 128, 1024);
+          tmem_a_acc(tmem + T_DV, tmem + T_ST, do_s, it == 0);  // dV += P^T dO
+          if (next) {
+            if (!(ok = mbar_wait(&bars->q_full[s1], ((gt + 1) / Q_STAGES) & 1, wc))) break;
+            tc_fence_after();
+            kmajor_pair(tmem + T_ST, sK, sQ + s1 * TILE);  // S^T(i+1)
+            tc_commit(&bars->s_full);
+          }
+          if (!(ok = mbar_wait(&bars->ds_ready, gt & 1, wc))) break;
+          tc_fence_after();
+          tmem_a_acc(tmem + T_DK, tmem + T_DPT, q_s, it == 0);  // dK += dS^T Q
+          const int b = gt & 1;
+          if (!(ok = mbar_wait(&bars->dq_empty[b], ((gt >> 1) & 1) ^ 1, wc))) break;
+          tc_fence_after();
+          {
+            const uint64_t da = sw128_desc(sdS, BKV * 128, 1024), dk = sw128_desc(sK, DP * 128, 1024);
 #pragma unroll 1
-          for (int kk = 0; kk < BKV / 16; ++kk)  // dQ_part = dS K
-            mma_f16_ss(tmem + T_DQ + 64 * b, da + 128 * kk, dk + 128 * kk, id_dq, kk > 0);
+            for (int kk = 0; kk < BKV / 16; ++kk)  // dQ_part = dS K
+              mma_f16_ss(tmem + T_DQ + 64 * b, da + 128 * kk, dk + 128 * kk, id_dq, kk > 0);
+          }
+          tc_commit(&bars->dq_full[b]);
+          tc_commit(&bars->q_empty[s]);
+          if (next) {
+            kmajor_pair(tmem + T_DPT, sV, sdO + s1 * TILE);  // dP^T(i+1)
+            tc_commit(&bars->dp_full);
+          }
         }
-        tc_commit(&bars->dq_full[b]);
-        tc_commit(&bars->q_empty[s]);
-        if (next) {
-          kmajor_pair(tmem + T_DPT, sV, sdO + s1 * TILE);  // dP^T(i+1)
-          tc_commit(&bars->dp_full);
-        }
+        if (!ok) break;
+        tc_commit(&bars->acc_done);    // dV, dK of this item complete
+        tc_commit(&bars->kv_empty[kb]);  // K and V no longer read
       }
-      if (ok) tc_commit(&bars->acc_done);
     }
     __syncwarp();
    }
@@ -237,37 +270,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool issuer = warp == 8 && lane == 0;
     uint8_t* stage = smem + SM_DQ;
     if (issuer) tma_prefetch_desc(&tmdQacc);
-    for (int it = 0; it < n; ++it) {
-      const int b = it & 1;
-      if (issuer) BWD_TRACE(4096 + it * 8 + 0);
-      if (!mbar_wait(&bars->dq_full[b], (it >> 1) & 1, wc)) break;
-      if (issuer) BWD_TRACE(4096 + it * 8 + 1);
-      tc_fence_after();
-      uint32_t v[DP];
-      tmem_ld32(tmem + lane_off + T_DQ + 64 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32(tmem + lane_off + T_DQ + 64 * b + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->dq_empty[b]);
-      // The previous tile's bulk reduce must have read the staging tile.
-      if (issuer) bulk_wait_read0();
-      named_bar_sync(1, 128);
-      // Row `row`, columns [32c, 32c+32) -> box c; 16-byte unit u at u ^ (row & 7).
+    int gt = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+      const Item I = item(w);
+      for (int it = 0; it < I.n; ++it, ++gt) {
+        const int b = gt & 1;
+        if (!(ok = mbar_wait(&bars->dq_full[b], (gt >> 1) & 1, wc))) break;
+        tc_fence_after();
+        uint32_t v[DP];
+        tmem_ld32(tmem + lane_off + T_DQ + 64 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tmem + lane_off + T_DQ + 64 * b + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->dq_empty[b]);
+        // The previous tile's bulk reduce must have read the staging tile.
+        if (issuer) bulk_wait_read0();
+        named_bar_sync(1, 128);
+        // Row `row`, columns [32c, 32c+32) -> box c; 16-byte unit u at u ^ (row & 7).
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<uint4*>(stage + c * DQ_BOX + row * 128 + ((u ^ (row & 7)) << 4)) =
-              make_uint4(v[32 * c + 4 * u], v[32 * c + 4 * u + 1], v[32 * c + 4 * u + 2], v[32 * c + 4 * u + 3]);
-      fence_proxy_async_smem();
-      named_bar_sync(1, 128);
-      if (issuer) BWD_TRACE(4096 + it * 8 + 2);
-      if (issuer) {
-        const int q0 = (i0 + it) * BQ;
-        tma_reduce_add_3d(&tmdQacc, stage, 0, q0, bh);
-        if (args.D > 32) tma_reduce_add_3d(&tmdQacc, stage + DQ_BOX, 32, q0, bh);
-        bulk_commit();
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(stage + c * DQ_BOX + row * 128 + ((u ^ (row & 7)) << 4)) =
+                make_uint4(v[32 * c + 4 * u], v[32 * c + 4 * u + 1], v[32 * c + 4 * u + 2], v[32 * c + 4 * u + 3]);
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (issuer) {
+          const int q0 = (I.i0 + it) * BQ;
+          tma_reduce_add_3d(&tmdQacc, stage, 0, q0, I.bh);
+          if (args.D > 32) tma_reduce_add_3d(&tmdQacc, stage + DQ_BOX, 32, q0, I.bh);
+          bulk_commit();
+        }
       }
     }
     if (issuer) bulk_wait0();
@@ -276,104 +311,129 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------------------------------------------------------- compute (P, dS)
     const int qw = warp & 3, h = warp >> 2;
     const int kr = qw * 32 + lane;
-    const int key = j * BKV + kr;
-    const bool kvalid = key < args.S;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const float sl2 = args.scale * 1.4426950408889634f;
     uint8_t* ds_tile = smem + SM_DS + h * TILE;  // queries [64h, 64h+64)
-    for (int it = 0; it < n; ++it) {
-      const int qt0 = (i0 + it) * BQ;
-      // Causal mask only on the diagonal tile; rows past S carry L2 = +inf
-      // (P = 0) in the padded statistics, so they need no test here.
-      const bool diag = args.causal && qt0 < j * BKV + BKV - 1;
-      const float* st = reinterpret_cast<const float*>(smem + SM_STAT + (it % Q_STAGES) * STAT_BYTES);
-      const float* Ls = st + 64 * h;
-      const float* Ds = st + BQ + 64 * h;
-      const bool trc = warp == 0 && lane == 0;
-      if (trc) BWD_TRACE(it * 8 + 0);
-      if (!mbar_wait(&bars->s_full, it & 1, wc)) break;
-      if (trc) BWD_TRACE(it * 8 + 1);
-      tc_fence_after();
-      float p[64];
+    int gt = 0, ic = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+      const Item I = item(w);
+      const int key = I.j * BKV + kr;
+      const bool kvalid = key < args.S;
+      for (int it = 0; it < I.n; ++it, ++gt) {
+        const int qt0 = (I.i0 + it) * BQ;
+        // Causal mask only on the diagonal tile; rows past S carry L2 = +inf
+        // (P = 0) in the padded statistics, so they need no test here.
+        const bool diag = args.causal && qt0 < I.j * BKV + BKV - 1;
+        const float* st = reinterpret_cast<const float*>(smem + SM_STAT + (gt % Q_STAGES) * STAT_BYTES);
+        const float* Ls = st + 64 * h;
+        const float* Ds = st + BQ + 64 * h;
+        if (!(ok = mbar_wait(&bars->s_full, gt & 1, wc))) break;
+        tc_fence_after();
+        // Both 32-column loads in flight before one wait.
+        float p[64];
+        {
+          uint32_t sv[64];
+          tmem_ld32(tmem + lane_off + T_ST + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(tmem + lane_off + T_ST + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_ld_wait();
+          if (!diag) {
+            // Off the diagonal every query of the tile sees this key: no mask.
 #pragma unroll
-      for (int cc = 0; cc < 64; cc += 32) {
-        uint32_t sv[32];
-        tmem_ld32(tmem + lane_off + T_ST + 64 * h + cc, sv);
-        float lv[32];  // the 32 rows' L2 statistics (same for every lane: broadcast reads)
+            for (int cc = 0; cc < 64; cc += 32) {
+              float lv[32];
 #pragma unroll
-        for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
-        tmem_ld_wait();
-        static_for<0, 32, 1>([&](auto tt) {
-          constexpr int t = decltype(tt)::value;
-          const float e = ex2_col<t, DGX_EXP_EMU_BWD>(fmaf(__uint_as_float(sv[t]), sl2, -lv[t]));
-          const bool vis = kvalid && !(diag && qt0 + 64 * h + cc + t < key);
-          p[cc + t] = vis ? e : 0.f;
-        });
-        uint32_t pk[16];
+              for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
+              static_for<0, 32, 1>([&](auto tt) {
+                constexpr int t = decltype(tt)::value;
+                p[cc + t] = ex2_col<t, DGX_EXP_EMU_BWD>(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
+              });
+            }
+          } else {
 #pragma unroll
-        for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2_fast(p[cc + 2 * t], p[cc + 2 * t + 1]);
-        tmem_st16(tmem + lane_off + T_ST + 64 * h + cc / 2, pk);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_ready);
-      if (trc) BWD_TRACE(it * 8 + 2);
-      if (!mbar_wait(&bars->dp_full, it & 1, wc)) break;
-      if (trc) BWD_TRACE(it * 8 + 3);
-      tc_fence_after();
+            for (int cc = 0; cc < 64; cc += 32) {
+              float lv[32];
 #pragma unroll
-      for (int cc = 0; cc < 64; cc += 32) {
-        uint32_t dv[32];
-        tmem_ld32(tmem + lane_off + T_DPT + 64 * h + cc, dv);
-        float dd[32];
+              for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
+              static_for<0, 32, 1>([&](auto tt) {
+                constexpr int t = decltype(tt)::value;
+                const float e = ex2_col<t, DGX_EXP_EMU_BWD>(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
+                p[cc + t] = qt0 + 64 * h + cc + t < key ? 0.f : e;
+              });
+            }
+          }
+          if (!kvalid) {
 #pragma unroll
-        for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&dd[t]) = *reinterpret_cast<const float4*>(Ds + cc + t);
-        tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - dd[t]);
-          const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - dd[t + 1]);
-          pk[t / 2] = pack_bf16x2_fast(ds0, ds1);
+            for (int t = 0; t < 64; ++t) p[t] = 0.f;
+          }
         }
-        tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
-        // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
-        // [64h, 64h+64) of this half, 16-byte units XOR-swizzled by (kr & 7).
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int unit = cc / 8 + u;
-          uint4* dst = reinterpret_cast<uint4*>(ds_tile + kr * 128 + ((unit ^ (kr & 7)) << 4));
-          *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        for (int cc = 0; cc < 64; cc += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2_fast(p[cc + 2 * t], p[cc + 2 * t + 1]);
+          tmem_st16(tmem + lane_off + T_ST + 64 * h + cc / 2, pk);
         }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_ready);
+        if (!(ok = mbar_wait(&bars->dp_full, gt & 1, wc))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 64; cc += 32) {
+          uint32_t dv[32];
+          tmem_ld32(tmem + lane_off + T_DPT + 64 * h + cc, dv);
+          float dd[32];
+#pragma unroll
+          for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&dd[t]) = *reinterpret_cast<const float4*>(Ds + cc + t);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - dd[t]);
+            const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - dd[t + 1]);
+            pk[t / 2] = pack_bf16x2_fast(ds0, ds1);
+          }
+          tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
+          // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
+          // [64h, 64h+64) of this half, 16-byte units XOR-swizzled by (kr & 7).
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int unit = cc / 8 + u;
+            uint4* dst = reinterpret_cast<uint4*>(ds_tile + kr * 128 + ((unit ^ (kr & 7)) << 4));
+            *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          }
+        }
+        tmem_st_wait();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_ready);
       }
-      tmem_st_wait();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ds_ready);
-      if (trc) BWD_TRACE(it * 8 + 4);
-    }
-    // ------------------------------------------------------------ epilogue: dV (h=0), dK (h=1)
-    if (mbar_wait(&bars->acc_done, 0, wc)) {
+      if (!ok) break;
+      // ---------------------------------------------------------- item epilogue: dV (h=0), dK (h=1)
+      if (!(ok = mbar_wait(&bars->acc_done, ic & 1, wc))) break;
       tc_fence_after();
       uint32_t v[DP];
       const uint32_t col = h ? T_DK : T_DV;
       tmem_ld32(tmem + lane_off + col, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       tmem_ld32(tmem + lane_off + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       tmem_ld_wait();
+      tc_fence_before();  // the next item's first dV / dK MMAs follow this warp's next p_ready
       if (key < args.S) {
         const float mul = h ? args.scale : 1.f;
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) + (row0 + key) * args.D;
+        __nv_bfloat16* dst =
+            reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) + ((size_t)I.bh * args.S + key) * args.D;
         if (args.D == DP) {
 #pragma unroll
           for (int c = 0; c < DP; c += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(v[c + 0]) * mul, __uint_as_float(v[c + 1]) * mul);
-            w.y = pack_bf16x2(__uint_as_float(v[c + 2]) * mul, __uint_as_float(v[c + 3]) * mul);
-            w.z = pack_bf16x2(__uint_as_float(v[c + 4]) * mul, __uint_as_float(v[c + 5]) * mul);
-            w.w = pack_bf16x2(__uint_as_float(v[c + 6]) * mul, __uint_as_float(v[c + 7]) * mul);
-            *reinterpret_cast<uint4*>(dst + c) = w;
+            uint4 wv;
+            wv.x = pack_bf16x2(__uint_as_float(v[c + 0]) * mul, __uint_as_float(v[c + 1]) * mul);
+            wv.y = pack_bf16x2(__uint_as_float(v[c + 2]) * mul, __uint_as_float(v[c + 3]) * mul);
+            wv.z = pack_bf16x2(__uint_as_float(v[c + 4]) * mul, __uint_as_float(v[c + 5]) * mul);
+            wv.w = pack_bf16x2(__uint_as_float(v[c + 6]) * mul, __uint_as_float(v[c + 7]) * mul);
+            *reinterpret_cast<uint4*>(dst + c) = wv;
           }
         } else {
 #pragma unroll
@@ -499,7 +559,8 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
   const int nkv = (a.S + BKV - 1) / BKV;
   {
     TimerScope timer(s);
-    flash_bwd_kernel<<<nkv * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, mdq, a);
+    const int items = nkv * a.BH;
+    flash_bwd_kernel<<<items < sms ? items : sms, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, mdq, a);
   }
   flash_bwd_post_kernel<<<4 * sms, 256, 0, s>>>(a);
   return cudaGetLastError();
