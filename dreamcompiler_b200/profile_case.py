@@ -4,6 +4,7 @@ two launches of each kernel).
 
     python -m dreamcompiler_b200.profile_case flash --bh 16      # S=2048, D=64
     python -m dreamcompiler_b200.profile_case gemm --n 4096
+    python -m dreamcompiler_b200.profile_case w8 --batch 1 --mode 1   # int8 layer, N=K=4096
 """
 from __future__ import annotations
 
@@ -21,6 +22,7 @@ def main() -> None:
     ap.add_argument("--dim", type=int, default=64)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--mode", type=int, default=0, help="w8: 0 = W8A32, 1 = W8A8")
     ap.add_argument("--reps", type=int, default=2)
     a = ap.parse_args()
     dgx.init(0)
@@ -41,7 +43,7 @@ def main() -> None:
         W = torch.randint(-127, 128, (a.n, a.n), device="cuda", dtype=torch.int8, generator=g)
         sc = torch.rand(a.n, device="cuda", generator=g) * 9e-3 + 1e-3
         for _ in range(a.reps):
-            dgx.gemm_w8(X, W, sc, None, mode=0)
+            dgx.gemm_w8(X, W, sc, None, mode=a.mode)
     dgx.sync_check()
     print("profile case ok")
 
