@@ -48,6 +48,17 @@ SIGNATURES = {
     "dgx_gemm_w8a8_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "dgx_gemm_i8i32": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "dgx_quantize_rows_i8": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+    "dgx_layernorm_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "dgx_layernorm_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "dgx_gelu_fwd": (_i, [_vp, _vp, C.c_longlong, _vp]),
+    "dgx_gelu_bwd": (_i, [_vp, _vp, _vp, C.c_longlong, _vp]),
+    "dgx_embedding_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "dgx_embedding_bwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "dgx_softmax_nll": (_i, [_vp, _i, _i, _vp, _i, _vp, _vp, _i, _vp]),
+    "dgx_adamw": (_i, [_vp, _vp, _vp, _vp, C.c_longlong, _f, _f, _f, _f, _f, _i, _vp, _vp]),
+    "dgx_colsum": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
+    "dgx_rows_to_heads": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _i, _i, _vp]),
+    "dgx_heads_to_rows": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "dgx_tp_shard": (None, [_i, _i, _i, C.POINTER(_i), C.POINTER(_i)]),
     "dgx_tp_export": (_i, [_vp, _sz, _vp, _sz]),
     "dgx_tp_handle_size": (_sz, []),

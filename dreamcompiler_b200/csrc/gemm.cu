@@ -41,10 +41,12 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * ESZ;              // 32 KB (bf16) / 16 KB (tf32)
   static constexpr int PLANES = TF32 ? 2 : 1;                // hi (+ lo) planes per operand
   static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;                   // double-buffered accumulator
   static constexpr int CHUNK = 128 / ESZ;                    // MN elements per 128-byte chunk
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // Epilogue staging for the TMA-store path: 4 warps x 2 buffers x (32 rows x 128 B).
+  static constexpr int OUT_STAGE_BYTES = 4 * 2 * 4096;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t FMT = TF32 ? 2u : 1u;
 };
 
@@ -74,12 +76,13 @@ template <bool TF32, bool A_MN, bool B_MN, int BN_>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                   GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
   using Cfg = GemmCfg<TF32, BN_>;
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* out_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(out_stage + Cfg::OUT_STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* accf_bar = empty_bar + STAGES;  // [2]
   uint64_t* acce_bar = accf_bar + 2;        // [2]
@@ -217,6 +220,13 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     uint32_t use = 0;
+    // TMA-store path: each warp stages its 32 rows x 128 bytes (32 fp32 or 64
+    // bf16 columns) in one of two shared-memory buffers with the 128-byte
+    // swizzle (16-byte unit u of row r at u ^ (r & 7): conflict-free) and
+    // issues one TMA store / reduce-add per chunk.
+    uint8_t* my_stage = out_stage + (warp - 2) * 8192;
+    uint32_t issued = 0;  // stores issued by this warp: buffer = issued & 1
+    if (args.tma_out && lane == 0) tma_prefetch_desc(&tmC);
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++use) {
       const int buf = use & 1;
       if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
@@ -225,18 +235,80 @@ __global__ void __launch_bounds__(192, 1)
       sched.coords(t, tm, tn);
       const int m = tm * BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+      if (args.tma_out) {
+        constexpr int CW32 = 32;  // fp32 columns per 32-column TMEM load
+        const int cw = args.c_bf16 ? 64 : 32;  // columns per 128-byte staged row
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c, r);
-        tmem_ld_wait();
-        const int n0 = tn * BN + c;
-        if (m < args.M && n0 < args.N) gemm_store_row32(args, m, n0, reinterpret_cast<float*>(r));
+        for (int c = 0; c < BN; c += cw) {
+          uint32_t r[64];
+          tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          if (args.c_bf16) tmem_ld32(taddr + c + CW32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          tmem_ld_wait();
+          if (c + cw >= BN) {  // last loads of this accumulator: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce_bar[buf]);
+          }
+          const int n0 = tn * BN + c;
+          if (n0 >= args.N) continue;
+          uint8_t* st = my_stage + (issued & 1) * 4096;
+          if (lane == 0 && issued >= 2) bulk_wait_read1();  // the store issued from this buffer has read it
+          __syncwarp();
+          uint32_t w[32];
+          if (args.c_bf16) {
+#pragma unroll
+            for (int j = 0; j < 64; j += 2) {
+              float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
+              if (args.bias) {
+                v0 += n0 + j < args.N ? args.bias[n0 + j] : 0.f;
+                v1 += n0 + j + 1 < args.N ? args.bias[n0 + j + 1] : 0.f;
+              }
+              if (args.relu) {
+                v0 = fmaxf(v0, 0.f);
+                v1 = fmaxf(v1, 0.f);
+              }
+              w[j / 2] = pack_bf16x2(v0, v1);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float v = __uint_as_float(r[j]);
+              if (args.bias) v += n0 + j < args.N ? args.bias[n0 + j] : 0.f;
+              if (args.relu) v = fmaxf(v, 0.f);
+              w[j] = __float_as_uint(v);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(st + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (args.tma_out == 2)
+              tma_reduce_add_2d(&tmC, st, n0, tm * BM + q * 32);
+            else
+              tma_store_2d(&tmC, st, n0, tm * BM + q * 32);
+            bulk_commit();
+          }
+          ++issued;
+        }
+        (void)m;
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c, r);
+          tmem_ld_wait();
+          const int n0 = tn * BN + c;
+          if (m < args.M && n0 < args.N) gemm_store_row32(args, m, n0, reinterpret_cast<float*>(r));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce_bar[buf]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce_bar[buf]);
     }
+    if (args.tma_out && lane == 0) bulk_wait0();  // staged tiles read and stored before the CTA leaves
   }
 
   tc_fence_before();
@@ -415,6 +487,32 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   a.tiles_m = (args.M + Cfg::BM - 1) / Cfg::BM;
   a.tiles_n = (args.N + Cfg::BN - 1) / Cfg::BN;
   a.group_m = 16;
+  // Epilogue path (see GemmArgs::tma_out).
+  CUtensorMap mc{};
+  {
+    const int esz = a.c_bf16 ? 2 : 4;
+    const bool aligned = ((uintptr_t)a.C & 15) == 0 && ((long long)a.ldc * esz) % 16 == 0;
+    int mode = 0;
+    if (a.n_extra == 0 && aligned) {
+      if (a.beta == 0.f)
+        mode = 1;
+      else if (a.beta == 1.f && !a.c_bf16 && !a.relu)
+        mode = 2;
+    }
+    if (mode) {
+      auto enc = get_tensor_map_encoder();
+      const cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+      const cuuint64_t strides[1] = {(cuuint64_t)a.ldc * esz};
+      const cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32};
+      const cuuint32_t estr[2] = {1, 1};
+      if (!enc || enc(&mc, a.c_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.C, dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        mode = 0;
+    }
+    a.tma_out = mode;
+    if (!mode) mc = ma;  // unused
+  }
   auto kern = gemm_tc_kernel<TF32, A_MN, B_MN, BN_>;
   static bool attr_done = false;  // per template instantiation
   if (!attr_done) {
@@ -426,7 +524,7 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   const int grid = tiles < num_sms() ? tiles : num_sms();
   {
     TimerScope timer(stream);
-    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, a);
+    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, mc, a);
   }
   return cudaGetLastError();
 }

@@ -26,6 +26,10 @@ struct GemmArgs {
   // tensor-parallel all-gather fused into the epilogue). beta must be 0.
   void* C_extra[7];
   int n_extra;
+  // Output path of the epilogue: 0 per-thread stores (any layout, beta, extra
+  // destinations); 1 TMA tensor store of staged tiles (beta = 0); 2 TMA
+  // reduce-add of staged tiles (fp32 C, beta = 1, no ReLU).
+  int tma_out;
 };
 
 __device__ __forceinline__ float gemm_finish(const GemmArgs& a, int n, float acc, float old) {

@@ -1,0 +1,249 @@
+"""Device-resident GPT training step on libdgx.
+
+The model is the one a Dream program builds from the reference ops (see the
+restatement in oracle/gpt_oracle.py): token + position embedding, L pre-LN
+blocks of causal multi-head attention and a 4x GELU(tanh) MLP, a final
+layer_norm, a linear head, log_softmax + nll_loss, and AdamW. Every `linear`
+runs on dgx_gemm (bf16 operands, fp32 accumulate and bias epilogue), the
+attention on dgx_flash_fwd / dgx_flash_bwd, everything else on the libdgx
+device ops (dgx_layernorm_*, dgx_gelu_*, dgx_embedding_*, dgx_softmax_nll,
+dgx_colsum, dgx_adamw, the head layout permutes). Parameters, gradients and
+AdamW state are fp32; the GEMMs read bf16 copies of the weights refreshed
+after each update.
+
+All buffers are allocated up front, so one `step` can be captured in a CUDA
+graph and replayed (the AdamW step count lives on the device).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict
+
+import torch
+
+from . import _lib as L
+from .ops import _stream, flash_bwd, flash_bwd_workspace_size, flash_fwd, gemm
+
+
+@dataclass
+class GPTConfig:
+    n_layer: int = 6
+    d_model: int = 384
+    n_head: int = 6
+    seq_len: int = 256
+    batch: int = 64
+    vocab: int = 65
+    lr: float = 3e-4
+    betas: tuple = (0.9, 0.999)
+    eps: float = 1e-8
+    weight_decay: float = 0.01
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.n_head
+
+    @property
+    def vocab_pad(self) -> int:  # logits row pitch: 16-byte rows for the bf16 GEMM operand
+        return (self.vocab + 7) // 8 * 8
+
+    def n_params(self) -> int:
+        d, L_ = self.d_model, self.n_layer
+        return L_ * (12 * d * d + 9 * d) + (2 * self.vocab + self.seq_len) * d + self.vocab
+
+    def flops_per_step(self) -> float:
+        """Algorithmic FLOPs: 6 * (GEMM parameters) * tokens for the dense part
+        plus causal attention forward (4*S^2*D/2 per head) and backward (2.5x)."""
+        d, L_, S = self.d_model, self.n_layer, self.seq_len
+        tokens = self.batch * S
+        dense = 6 * (L_ * 12 * d * d + self.vocab * d) * tokens
+        attn = L_ * self.batch * self.n_head * 3.5 * 4 * S * S * self.head_dim / 2
+        return dense + attn
+
+
+def _c(name, *args):
+    L.call(name, *args)
+
+
+class GPT:
+    """Parameters, optimizer state and activations of one GPT on one GPU."""
+
+    def __init__(self, cfg: GPTConfig, device="cuda", params: Dict[str, torch.Tensor] = None, seed: int = 0):
+        self.cfg = c = cfg
+        dev = self.dev = torch.device(device)
+        d, H, hd, S, B, V, Vp = c.d_model, c.n_head, c.head_dim, c.seq_len, c.batch, c.vocab, c.vocab_pad
+        assert d % H == 0 and hd % 8 == 0 and hd <= 64, "head_dim must be a multiple of 8, at most 64"
+        R = self.R = B * S
+        f32, bf16 = torch.float32, torch.bfloat16
+
+        # ---- parameters: matrices (weight decay) and biases (none) in two flat buffers
+        mats = {"W_tok": (V, d), "P": (S, d)}
+        vecs = {}
+        for l in range(c.n_layer):
+            mats.update({f"Wqkv{l}": (3 * d, d), f"Wo{l}": (d, d), f"W1{l}": (4 * d, d), f"W2{l}": (d, 4 * d)})
+            vecs.update({f"bqkv{l}": (3 * d,), f"bo{l}": (d,), f"b1{l}": (4 * d,), f"b2{l}": (d,)})
+        mats["Wout"] = (Vp, d)
+        vecs["bout"] = (Vp,)
+        self.groups = {}
+        self.p, self.g, self.w16 = {}, {}, {}
+        for gname, spec in (("mat", mats), ("vec", vecs)):
+            n = sum(torch.Size(s).numel() for s in spec.values())
+            buf = {k: torch.zeros(n, device=dev, dtype=f32) for k in ("p", "g", "m", "v")}
+            self.groups[gname] = buf
+            if gname == "mat":
+                self.w16_flat = torch.zeros(n, device=dev, dtype=bf16)
+            off = 0
+            for name, shp in spec.items():
+                k = torch.Size(shp).numel()
+                self.p[name] = buf["p"][off:off + k].view(shp)
+                self.g[name] = buf["g"][off:off + k].view(shp)
+                if gname == "mat":
+                    self.w16[name] = self.w16_flat[off:off + k].view(shp)
+                off += k
+        self.step_dev = torch.zeros(1, device=dev, dtype=torch.int32)
+        self._init(params, seed)
+
+        # ---- activations kept for the backward
+        self.tok = torch.zeros(R, device=dev, dtype=torch.int32)
+        self.tgt = torch.zeros(R, device=dev, dtype=torch.int32)
+        self.x = [torch.empty(R, d, device=dev, dtype=f32) for _ in range(2 * c.n_layer + 1)]
+        self.h16 = [torch.empty(R, d, device=dev, dtype=bf16) for _ in range(2 * c.n_layer + 1)]
+        self.mu = [torch.empty(R, device=dev, dtype=f32) for _ in range(2 * c.n_layer + 1)]
+        self.rs = [torch.empty(R, device=dev, dtype=f32) for _ in range(2 * c.n_layer + 1)]
+        self.qkv32 = torch.empty(R, 3 * d, device=dev, dtype=f32)
+        heads = lambda: torch.empty(B * H, S, hd, device=dev, dtype=bf16)
+        self.q, self.k, self.v, self.o = ([heads() for _ in range(c.n_layer)] for _ in range(4))
+        self.lse = [torch.empty(B * H, S, device=dev, dtype=f32) for _ in range(c.n_layer)]
+        self.att16 = [torch.empty(R, d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
+        self.u32 = [torch.empty(R, 4 * d, device=dev, dtype=f32) for _ in range(c.n_layer)]
+        self.g16 = [torch.empty(R, 4 * d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
+        self.logits = torch.empty(R, Vp, device=dev, dtype=f32)
+        self.dlogits = torch.empty(R, Vp, device=dev, dtype=bf16)
+        self.loss = torch.zeros(1, device=dev, dtype=f32)
+        # ---- backward scratch
+        self.dx = torch.empty(R, d, device=dev, dtype=f32)
+        self.dx16 = torch.empty(R, d, device=dev, dtype=bf16)
+        self.dh = torch.empty(R, d, device=dev, dtype=f32)
+        self.dg = torch.empty(R, 4 * d, device=dev, dtype=f32)
+        self.du16 = torch.empty(R, 4 * d, device=dev, dtype=bf16)
+        self.dqkv16 = torch.empty(R, 3 * d, device=dev, dtype=bf16)
+        self.dO, self.dq, self.dk, self.dv = (heads() for _ in range(4))
+        self.fa_ws = torch.empty(flash_bwd_workspace_size(B * H, S, hd) // 4 + 1, device=dev, dtype=f32)
+
+    # ------------------------------------------------------------ setup
+    def _init(self, params, seed):
+        if params is None:
+            from_cpu = {}
+            gen = torch.Generator().manual_seed(seed)
+            for name, t in self.p.items():
+                std = 0.02 if name[0] in "WP" else 0.0
+                if name.startswith(("Wo", "W2")):
+                    std = 0.02 / (2 * self.cfg.n_layer) ** 0.5
+                from_cpu[name] = torch.randn(t.shape, generator=gen) * std
+            params = from_cpu
+        for name, t in self.p.items():
+            src = torch.as_tensor(params[name], dtype=torch.float32)
+            if name in ("Wout", "bout"):  # rows / entries past the vocabulary stay zero
+                t.zero_()
+                t[:src.shape[0]].copy_(src)
+            else:
+                t.copy_(src.reshape(t.shape))
+        self._refresh_w16()
+
+    def _refresh_w16(self):
+        s = _stream(self.w16_flat)
+        mat = self.groups["mat"]["p"]
+        _c("dgx_convert", mat.data_ptr(), L.DGX_F32, self.w16_flat.data_ptr(), L.DGX_BF16, mat.numel(), 0, s)
+
+    def set_batch(self, tok: torch.Tensor, tgt: torch.Tensor):
+        self.tok.copy_(tok.reshape(-1), non_blocking=True)
+        self.tgt.copy_(tgt.reshape(-1), non_blocking=True)
+
+    # ------------------------------------------------------------ step
+    def forward_backward(self):
+        c = self.cfg
+        d, H, hd, S, B, V, Vp, R = c.d_model, c.n_head, c.head_dim, c.seq_len, c.batch, c.vocab, c.vocab_pad, self.R
+        s = _stream(self.x[0])
+        p, g, w = self.p, self.g, self.w16
+        # ---- forward
+        _c("dgx_embedding_fwd", self.tok.data_ptr(), p["W_tok"].data_ptr(), p["P"].data_ptr(), self.x[0].data_ptr(),
+           R, S, d, V, s)
+        for l in range(c.n_layer):
+            x0, x1, x2 = self.x[2 * l], self.x[2 * l + 1], self.x[2 * l + 2]
+            h, h2 = self.h16[2 * l], self.h16[2 * l + 1]
+            _c("dgx_layernorm_fwd", x0.data_ptr(), h.data_ptr(), self.mu[2 * l].data_ptr(), self.rs[2 * l].data_ptr(),
+               R, d, s)
+            gemm(h, w[f"Wqkv{l}"], transB=True, out=self.qkv32, bias=p[f"bqkv{l}"])
+            for i, dst in enumerate((self.q[l], self.k[l], self.v[l])):
+                _c("dgx_rows_to_heads", self.qkv32.data_ptr(), L.DGX_F32, 3 * d, i * d, dst.data_ptr(), B, S, H, hd, s)
+            flash_fwd(self.q[l], self.k[l], self.v[l], out=self.o[l], lse=self.lse[l])
+            _c("dgx_heads_to_rows", self.o[l].data_ptr(), self.att16[l].data_ptr(), d, 0, B, S, H, hd, s)
+            x1.copy_(x0)
+            gemm(self.att16[l], w[f"Wo{l}"], transB=True, out=x1, bias=p[f"bo{l}"], beta=1.0)  # x1 = x0 + att Wo^T + bo
+            _c("dgx_layernorm_fwd", x1.data_ptr(), h2.data_ptr(), self.mu[2 * l + 1].data_ptr(),
+               self.rs[2 * l + 1].data_ptr(), R, d, s)
+            gemm(h2, w[f"W1{l}"], transB=True, out=self.u32[l], bias=p[f"b1{l}"])
+            _c("dgx_gelu_fwd", self.u32[l].data_ptr(), self.g16[l].data_ptr(), self.u32[l].numel(), s)
+            x2.copy_(x1)
+            gemm(self.g16[l], w[f"W2{l}"], transB=True, out=x2, bias=p[f"b2{l}"], beta=1.0)
+        xL, hf = self.x[2 * c.n_layer], self.h16[2 * c.n_layer]
+        _c("dgx_layernorm_fwd", xL.data_ptr(), hf.data_ptr(), self.mu[-1].data_ptr(), self.rs[-1].data_ptr(), R, d, s)
+        gemm(hf, w["Wout"], transB=True, out=self.logits, bias=p["bout"])
+        _c("dgx_softmax_nll", self.logits.data_ptr(), Vp, V, self.tgt.data_ptr(), R, self.loss.data_ptr(),
+           self.dlogits.data_ptr(), L.DGX_BF16, s)
+        # ---- backward
+        gemm(self.dlogits, w["Wout"], out=self.dh)                        # dhf = dlogits Wout
+        gemm(self.dlogits, hf, transA=True, out=g["Wout"])                # dWout = dlogits^T hf
+        _c("dgx_colsum", self.dlogits.data_ptr(), L.DGX_BF16, g["bout"].data_ptr(), R, Vp, 0, s)
+        _c("dgx_layernorm_bwd", xL.data_ptr(), self.mu[-1].data_ptr(), self.rs[-1].data_ptr(), self.dh.data_ptr(),
+           self.dx.data_ptr(), R, d, 0, s)
+        conv16 = lambda src, dst: _c("dgx_convert", src.data_ptr(), L.DGX_F32, dst.data_ptr(), L.DGX_BF16,
+                                     src.numel(), 0, s)
+        for l in reversed(range(c.n_layer)):
+            x0, x1 = self.x[2 * l], self.x[2 * l + 1]
+            h, h2 = self.h16[2 * l], self.h16[2 * l + 1]
+            # MLP: x2 = x1 + gelu(h2 W1^T + b1) W2^T + b2
+            conv16(self.dx, self.dx16)
+            gemm(self.dx16, w[f"W2{l}"], out=self.dg)                     # dg = dx W2
+            gemm(self.dx16, self.g16[l], transA=True, out=g[f"W2{l}"])     # dW2 = dx^T g
+            _c("dgx_colsum", self.dx.data_ptr(), L.DGX_F32, g[f"b2{l}"].data_ptr(), R, d, 0, s)
+            _c("dgx_gelu_bwd", self.u32[l].data_ptr(), self.dg.data_ptr(), self.du16.data_ptr(), self.du16.numel(), s)
+            gemm(self.du16, w[f"W1{l}"], out=self.dh)                     # dh2 = du W1
+            gemm(self.du16, h2, transA=True, out=g[f"W1{l}"])              # dW1 = du^T h2
+            _c("dgx_colsum", self.du16.data_ptr(), L.DGX_BF16, g[f"b1{l}"].data_ptr(), R, 4 * d, 0, s)
+            _c("dgx_layernorm_bwd", x1.data_ptr(), self.mu[2 * l + 1].data_ptr(), self.rs[2 * l + 1].data_ptr(),
+               self.dh.data_ptr(), self.dx.data_ptr(), R, d, 1, s)
+            # attention: x1 = x0 + merge(attn(split(h Wqkv^T + bqkv))) Wo^T + bo
+            conv16(self.dx, self.dx16)
+            gemm(self.dx16, w[f"Wo{l}"], out=self.dh)                     # datt = dx Wo
+            gemm(self.dx16, self.att16[l], transA=True, out=g[f"Wo{l}"])   # dWo = dx^T att
+            _c("dgx_colsum", self.dx.data_ptr(), L.DGX_F32, g[f"bo{l}"].data_ptr(), R, d, 0, s)
+            _c("dgx_rows_to_heads", self.dh.data_ptr(), L.DGX_F32, d, 0, self.dO.data_ptr(), B, S, H, hd, s)
+            flash_bwd(self.q[l], self.k[l], self.v[l], self.o[l], self.dO, self.lse[l], dQ=self.dq, dK=self.dk,
+                      dV=self.dv, workspace=self.fa_ws)
+            for i, src in enumerate((self.dq, self.dk, self.dv)):
+                _c("dgx_heads_to_rows", src.data_ptr(), self.dqkv16.data_ptr(), 3 * d, i * d, B, S, H, hd, s)
+            gemm(self.dqkv16, w[f"Wqkv{l}"], out=self.dh)                 # dh = dqkv Wqkv
+            gemm(self.dqkv16, h, transA=True, out=g[f"Wqkv{l}"])           # dWqkv = dqkv^T h
+            _c("dgx_colsum", self.dqkv16.data_ptr(), L.DGX_BF16, g[f"bqkv{l}"].data_ptr(), R, 3 * d, 0, s)
+            _c("dgx_layernorm_bwd", x0.data_ptr(), self.mu[2 * l].data_ptr(), self.rs[2 * l].data_ptr(),
+               self.dh.data_ptr(), self.dx.data_ptr(), R, d, 1, s)
+        g["W_tok"].zero_()
+        g["P"].zero_()
+        _c("dgx_embedding_bwd", self.tok.data_ptr(), self.dx.data_ptr(), g["W_tok"].data_ptr(), g["P"].data_ptr(),
+           R, S, d, V, s)
+        return self.loss
+
+    def optimizer_step(self):
+        c = self.cfg
+        s = _stream(self.step_dev)
+        self.step_dev.add_(1)
+        for gname, wd in (("mat", c.weight_decay), ("vec", 0.0)):
+            b = self.groups[gname]
+            _c("dgx_adamw", b["p"].data_ptr(), b["g"].data_ptr(), b["m"].data_ptr(), b["v"].data_ptr(), b["p"].numel(),
+               c.lr, c.betas[0], c.betas[1], c.eps, wd, 0, self.step_dev.data_ptr(), s)
+        self._refresh_w16()
+
+    def step(self):
+        loss = self.forward_backward()
+        self.optimizer_step()
+        return loss

@@ -164,6 +164,52 @@ dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B
 dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, int K, void* stream);
 
 /*
+ * Building blocks of the GPT training step: the device
+ * forms of the reference NN ops between the GEMMs and attention, so the step
+ * stays on the GPU. fp32 activations and master data; bf16 where the next
+ * consumer is a GEMM. Rows are contiguous ([R][C] row-major).
+ */
+/* y16 = bf16(layer_norm(x)) per row (no affine, eps 1e-5); mean/rstd [R] saved
+ * for the backward. Replaces dream_layer_norm (runtime/io/builtins.inc:167-197). */
+dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd, int R, int C, void* stream);
+/* dx (+)= rstd/C * (C*dy - sum(dy) - y*sum(dy*y)), y recomputed from x
+ * (runtime/ops/autograd.inc:453-470); accumulate = 1 adds into dx. */
+dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rstd, const float* dy, float* dx, int R,
+                             int C, int accumulate, void* stream);
+/* y16 = bf16(gelu(x)), tanh form (runtime/io/builtins.inc:548-560). */
+dgx_status dgx_gelu_fwd(const float* x, void* y16, long long n, void* stream);
+/* dx16 = bf16(gelu'(x) * dy) (runtime/ops/autograd.inc:293-303). */
+dgx_status dgx_gelu_bwd(const float* x, const float* dy, void* dx16, long long n, void* stream);
+/* x[i] = W[tok[i]] + P[i % S] (P may be NULL): dream_embedding
+ * (runtime/nn/training.inc:579-600) plus the broadcast position add. */
+dgx_status dgx_embedding_fwd(const int* tok, const float* W, const float* P, float* x, int n, int S, int d, int V,
+                             void* stream);
+/* dW[tok[i]] += dx[i] (fp32 atomics), dP[s] += sum over rows i % S == s
+ * (runtime/ops/autograd.inc:330-341). dP may be NULL. */
+dgx_status dgx_embedding_bwd(const int* tok, const float* dx, float* dW, float* dP, int n, int S, int d, int V,
+                             void* stream);
+/* loss = nll_loss(log_softmax(logits), target) over n rows of pitch ld (the
+ * first V columns valid), device scalar; dlogits (may be NULL; DGX_F32 or
+ * DGX_BF16, pitch ld) = (softmax - onehot(target)) / n, zero past V.
+ * runtime/ops/elementwise.inc:1550-1603, runtime/ops/autograd.inc:212-245. */
+dgx_status dgx_softmax_nll(const float* logits, int ld, int V, const int* target, int n, float* loss, void* dlogits,
+                           int dlogits_type, void* stream);
+/* One AdamW step, grad zeroed: dream_adamw_update
+ * (runtime/io/builtins.inc:578-617) with fp32 state. The 1-based step count
+ * is `step`, or *step_dev (device int) when step_dev is not NULL, so that a
+ * captured CUDA graph replays correct bias corrections. */
+dgx_status dgx_adamw(float* param, float* grad, float* m, float* v, long long n, float lr, float b1, float b2,
+                     float eps, float wd, int step, const int* step_dev, void* stream);
+/* db[j] (+)= sum_r dy[r][j] (bias gradients of dream_linear,
+ * runtime/ops/autograd.inc:156-211); dy DGX_F32 or DGX_BF16. Deterministic. */
+dgx_status dgx_colsum(const void* dy, int dy_type, float* db, int R, int N, int accumulate, void* stream);
+/* Head layouts for attention: rows [B*S][ld] with head h at columns
+ * col0 + h*D  <->  heads [B*H][S][D] (bf16, the dgx_flash_* layout). */
+dgx_status dgx_rows_to_heads(const void* src, int src_type, int ld, int col0, void* dst, int B, int S, int H, int D,
+                             void* stream);
+dgx_status dgx_heads_to_rows(const void* src, void* dst, int ld, int col0, int B, int S, int H, int D, void* stream);
+
+/*
  * Column-parallel tensor-parallel GEMM over `world` GPUs, one process per GPU.
  * Each rank holds all of A [M,K] and its column shard of B ([K, n_r] with the
  * reference's widths: base = N/world, the first N%world shards one wider).

@@ -49,6 +49,14 @@ _SIG = {
     "dream_linear_relu": [TP, TP, TP],
     "dream_bmm": [TP, TP, TP, TP, TP, TP],
     "tensor_decref": [TP],
+    "tensor_add": [TP, TP],
+    "dream_reshape_nd": [TP, TP, TP],
+    "dream_embedding": [TP, TP],
+    "dream_layer_norm": [TP],
+    "dream_gelu": [TP],
+    "dream_log_softmax": [TP],
+    "dream_nll_loss": [TP, TP],
+    "dream_adamw_update": [TP, TP, TP, TP, TP, TP],
     "zero_grad": [TP],
     "gemm_selftest": [],
     "flash_attention_selftest": [],

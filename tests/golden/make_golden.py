@@ -13,11 +13,18 @@ output comes from the reference's own ops:
              and the tests/26_flash_backward.dream case
   linear.npz dream_linear / dream_linear_relu + backward
   tp.npz     dream_tp_matmul_column for G in {2,3,4,5,7} (training.inc:1664-1706)
+  gpt.npz    one GPT training step (BASELINE config 3 architecture at a tiny
+             size) composed from the reference ops: embedding + broadcast
+             position add, layer_norm, per-head dream_linear and
+             dream_flash_attention, gelu, log_softmax + nll_loss, backward;
+             parameters from a seeded numpy generator (oracle/gpt_oracle.py)
+  adamw.npz  dream_adamw_update applied twice to one parameter
 
 Usage:  python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
+import ctypes as C
 import os
 import sys
 
@@ -116,11 +123,103 @@ def gen_tp():
     np.savez_compressed(os.path.join(HERE, "tp.npz"), **out)
 
 
+GPT_CFG = dict(L=1, d=64, H=2, B=2, S=64, V=65, seed=3)
+
+
+def gen_gpt():
+    from oracle import gpt_oracle as G
+
+    c = GPT_CFG
+    L, d, H, B, S, V = c["L"], c["d"], c["H"], c["B"], c["S"], c["V"]
+    hd, n = d // H, B * S
+    params = G.init_params(L, d, V, S, c["seed"])
+    rng = np.random.default_rng(c["seed"] + 1)
+    tok = rng.integers(0, V, n)
+    tgt = rng.integers(0, V, n)
+    sc = R.scalar
+    t = lambda a: R.tensor(np.asarray(a, np.float64).reshape(a.shape[0], -1) if a.ndim > 1 else
+                           np.asarray(a, np.float64).reshape(1, -1))
+    leaves = {}
+
+    def leaf(name, a):
+        leaves[name] = t(a)
+        return leaves[name]
+
+    e = R.call("dream_embedding", R.tensor(tok.astype(np.float64).reshape(n, 1)), leaf("W_tok", params["W_tok"]))
+    pos = R.call("dream_reshape_nd", leaf("P", params["P"]), sc(1), sc(S * d))
+    x = R.call("dream_reshape_nd", R.call("tensor_add", R.call("dream_reshape_nd", e, sc(B), sc(S * d)), pos),
+               sc(n), sc(d))
+    for l in range(L):
+        h = R.call("dream_layer_norm", x)
+        Wqkv, bqkv, Wo = params[f"Wqkv{l}"], params[f"bqkv{l}"], params[f"Wo{l}"]
+        z = None
+        for hh in range(H):
+            qkv = []
+            for i, nm in enumerate("qkv"):
+                rows = slice(i * d + hh * hd, i * d + (hh + 1) * hd)
+                y = R.call("dream_linear", h, leaf(f"W{nm}{l}_{hh}", Wqkv[rows]), leaf(f"b{nm}{l}_{hh}", bqkv[rows]))
+                qkv.append(R.call("dream_reshape_nd", y, sc(B), sc(S * hd)))
+            o = R.call("dream_flash_attention", *qkv, sc(B), sc(S), sc(hd), sc(64))
+            o = R.call("dream_reshape_nd", o, sc(n), sc(hd))
+            bias = params[f"bo{l}"] if hh == 0 else np.zeros(d, np.float32)
+            zz = R.call("dream_linear", o, leaf(f"Wo{l}_{hh}", Wo[:, hh * hd:(hh + 1) * hd]), leaf(f"bo{l}_{hh}", bias))
+            z = zz if z is None else R.call("tensor_add", z, zz)
+        x = R.call("tensor_add", x, z)
+        h2 = R.call("dream_layer_norm", x)
+        u = R.call("dream_linear", h2, leaf(f"W1{l}", params[f"W1{l}"]), leaf(f"b1{l}", params[f"b1{l}"]))
+        z2 = R.call("dream_linear", R.call("dream_gelu", u), leaf(f"W2{l}", params[f"W2{l}"]),
+                    leaf(f"b2{l}", params[f"b2{l}"]))
+        x = R.call("tensor_add", x, z2)
+    hf = R.call("dream_layer_norm", x)
+    logits = R.call("dream_linear", hf, leaf("Wout", params["Wout"]), leaf("bout", params["bout"]))
+    loss = R.call("dream_nll_loss", R.call("dream_log_softmax", logits), R.tensor(tgt.astype(np.float64).reshape(n, 1)))
+    R.call("backward", loss)
+
+    grads = {}
+    for name in ("W_tok", "P", "Wout", "bout"):
+        grads[name] = R.grad(leaves[name]).reshape(params[name].shape)
+    for l in range(L):
+        for name in ("W1", "b1", "W2", "b2"):
+            grads[f"{name}{l}"] = R.grad(leaves[f"{name}{l}"]).reshape(params[f"{name}{l}"].shape)
+        gW = np.zeros((3 * d, d))
+        gb = np.zeros(3 * d)
+        gWo = np.zeros((d, d))
+        for hh in range(H):
+            for i, nm in enumerate("qkv"):
+                rows = slice(i * d + hh * hd, i * d + (hh + 1) * hd)
+                gW[rows] = R.grad(leaves[f"W{nm}{l}_{hh}"]).reshape(hd, d)
+                gb[rows] = R.grad(leaves[f"b{nm}{l}_{hh}"]).reshape(hd)
+            gWo[:, hh * hd:(hh + 1) * hd] = R.grad(leaves[f"Wo{l}_{hh}"]).reshape(d, hd)
+        grads[f"Wqkv{l}"], grads[f"bqkv{l}"], grads[f"Wo{l}"] = gW, gb, gWo
+        grads[f"bo{l}"] = R.grad(leaves[f"bo{l}_0"]).reshape(d)
+    out = {"tok": tok.astype(np.int32), "tgt": tgt.astype(np.int32), "loss": np.float64(R.data(loss)[0, 0])}
+    for k, v in params.items():
+        out["p_" + k] = v
+        out["g_" + k] = grads[k].astype(np.float32)
+    out["cfg"] = np.array([c[k] for k in ("L", "d", "H", "B", "S", "V", "seed")], np.int64)
+    np.savez_compressed(os.path.join(HERE, "gpt.npz"), **out)
+
+
+def gen_adamw():
+    rng = np.random.default_rng(11)
+    p0 = rng.standard_normal((4, 50))
+    g1, g2 = rng.standard_normal((4, 50)), rng.standard_normal((4, 50)) * 0.1
+    p = R.tensor(p0)
+    out = {"p0": p0, "g1": g1, "g2": g2}
+    for k, g in enumerate((g1, g2), 1):
+        C.memmove(p.contents.grad, np.ascontiguousarray(g, np.float64).ctypes.data, g.nbytes)
+        R.call("dream_adamw_update", p, R.scalar(3e-4), R.scalar(0.9), R.scalar(0.999), R.scalar(1e-8), R.scalar(0.01))
+        out[f"p{k}"] = R.data(p)
+    np.savez_compressed(os.path.join(HERE, "adamw.npz"), **out)
+
+
 if __name__ == "__main__":
     gen_gemm()
     gen_flash()
     gen_linear()
     gen_tp()
+    gen_gpt()
+    gen_adamw()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

@@ -1,0 +1,111 @@
+"""GPU: the device-resident GPT training step (BASELINE config 3
+architecture) against the reference runtime's own step (golden vectors from
+tests/golden/make_golden.py) and the f64 oracle (oracle/gpt_oracle.py).
+
+The device step runs its GEMMs and attention on bf16 operands with fp32
+accumulation (fp32 master weights, activations and gradients elsewhere), the
+reference in f64: the loss must agree to 1e-3 relative and every parameter's
+gradient to 1e-2 normwise (the bf16 tolerance of the task; measured: 7e-6 and <5e-3)."""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+from oracle import gpt_oracle as G  # noqa: E402
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+LOSS_RTOL, GRAD_TOL = 1e-3, 1e-2
+
+
+def _grads(model, names):
+    V = model.cfg.vocab
+    out = {}
+    for k in names:
+        gk = model.g[k].float().cpu().numpy()
+        out[k] = gk[:V] if k in ("Wout", "bout") else gk
+    return out
+
+
+def _check(model, loss_ref, grads_ref, report=None):
+    loss = float(model.loss.item())
+    errs = {}
+    got = _grads(model, grads_ref)
+    for k, ref in grads_ref.items():
+        ref = np.asarray(ref, np.float64).reshape(got[k].shape)
+        errs[k] = np.linalg.norm(got[k] - ref) / np.linalg.norm(ref)
+    if report is not None:
+        report.update(errs)
+    assert abs(loss - loss_ref) <= LOSS_RTOL * abs(loss_ref), (loss, loss_ref)
+    bad = {k: e for k, e in errs.items() if not e <= GRAD_TOL}
+    assert not bad, bad
+
+
+def test_step_matches_reference_runtime_golden(dgx):
+    from dreamcompiler_b200.gpt import GPT, GPTConfig
+    z = np.load(os.path.join(GOLD, "gpt.npz"))
+    L, d, H, B, S, V, _ = (int(x) for x in z["cfg"])
+    params = {k[2:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("p_")}
+    m = GPT(GPTConfig(n_layer=L, d_model=d, n_head=H, seq_len=S, batch=B, vocab=V), params=params)
+    m.set_batch(torch.from_numpy(z["tok"]), torch.from_numpy(z["tgt"]))
+    m.forward_backward()
+    dgx.sync_check()
+    _check(m, float(z["loss"]), {k[2:]: z[k] for k in z.files if k.startswith("g_")})
+
+
+@pytest.mark.parametrize("L,d,H,B,S", [(2, 128, 2, 2, 128), (1, 192, 3, 3, 256)])
+def test_step_matches_oracle(dgx, L, d, H, B, S):
+    from dreamcompiler_b200.gpt import GPT, GPTConfig
+    V = 65
+    params = G.init_params(L, d, V, S, seed=L * 100 + d)
+    rng = np.random.default_rng(d)
+    tok, tgt = rng.integers(0, V, B * S), rng.integers(0, V, B * S)
+    loss_ref, grads_ref = G.step(params, tok, tgt, L, d, H, B, S, V)
+    m = GPT(GPTConfig(n_layer=L, d_model=d, n_head=H, seq_len=S, batch=B, vocab=V),
+            params={k: torch.from_numpy(v) for k, v in params.items()})
+    m.set_batch(torch.from_numpy(tok.astype(np.int32)), torch.from_numpy(tgt.astype(np.int32)))
+    m.forward_backward()
+    dgx.sync_check()
+    _check(m, loss_ref, grads_ref)
+
+
+def test_adamw_kernel_matches_oracle(dgx):
+    from dreamcompiler_b200 import _lib
+    rng = np.random.default_rng(4)
+    p0, g1, g2 = (rng.standard_normal(10000) for _ in range(3))
+    p = torch.from_numpy(p0.astype(np.float32)).cuda()
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    step_dev = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pr, mr, vr = p0.astype(np.float32).astype(np.float64), np.zeros(10000), np.zeros(10000)
+    s = torch.cuda.current_stream().cuda_stream
+    for k, g in enumerate((g1, g2), 1):
+        gd = torch.from_numpy(g.astype(np.float32)).cuda()
+        if k == 1:  # host step count
+            _lib.call("dgx_adamw", p.data_ptr(), gd.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), 3e-4, 0.9, 0.999,
+                      1e-8, 0.01, 1, None, s)
+        else:  # device step count
+            step_dev.fill_(2)
+            _lib.call("dgx_adamw", p.data_ptr(), gd.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), 3e-4, 0.9, 0.999,
+                      1e-8, 0.01, 0, step_dev.data_ptr(), s)
+        pr, mr, vr = G.adamw(pr, g.astype(np.float32).astype(np.float64), mr, vr, k, 3e-4)
+        assert not gd.any().item()  # gradient zeroed
+    dgx.sync_check()
+    np.testing.assert_allclose(p.cpu().numpy(), pr, rtol=0, atol=2e-6)
+
+
+def test_training_reduces_loss(dgx):
+    from dreamcompiler_b200.gpt import GPT, GPTConfig
+    cfg = GPTConfig(n_layer=2, d_model=128, n_head=2, seq_len=128, batch=4, vocab=65, lr=1e-3)
+    m = GPT(cfg, seed=1)
+    g = torch.Generator().manual_seed(2)
+    tok = torch.randint(0, 65, (cfg.batch * cfg.seq_len,), generator=g, dtype=torch.int32)
+    m.set_batch(tok, torch.roll(tok, -1))  # learnable: next token of a fixed sequence
+    first = None
+    for i in range(30):
+        loss = m.step()
+        if i == 0:
+            first = loss.item()
+    dgx.sync_check()
+    assert loss.item() < 0.8 * first, (first, loss.item())
