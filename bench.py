@@ -312,6 +312,7 @@ def run_secondary(local_rank):
       configs[0]  f32 GEMM 1024^3 + dA/dB backward (3xTF32 tcgen05)
       configs[3]  bf16 GEMM 4096/8192/16384^3, single GPU
       configs[4]  int8 weight-only dense 4096x4096, B in {1, 16, 256}, both modes
+      configs[2]  char-level GPT training step (fwd + bwd + AdamW), tokens/s
     Operands that fit in L2 are cycled through enough copies to exceed it."""
     import torch
     import dreamcompiler_b200 as dgx
@@ -392,6 +393,22 @@ def run_secondary(local_rank):
                                                                "tops": 2 * Bn * N * K / t / 1e12}
     res["config5_int8_w8"] = w8
     del Ws
+    torch.cuda.empty_cache()
+
+    # char-level GPT training step (6 layers, d 384, 6 heads, seq 256,
+    # batch 64, vocab 65): forward, backward and AdamW, synthetic uniform token ids
+    from dreamcompiler_b200.gpt import GPT, GPTConfig
+    cfg = GPTConfig()
+    model = GPT(cfg, device=dev, seed=0)
+    gtok = torch.Generator().manual_seed(3)
+    tok = torch.randint(0, cfg.vocab, (cfg.batch * cfg.seq_len,), generator=gtok, dtype=torch.int32)
+    model.set_batch(tok, torch.randint(0, cfg.vocab, tok.shape, generator=gtok, dtype=torch.int32))
+    t = timed(lambda i: model.step(), 4)
+    res["config3_gpt_train_step"] = {"ms_per_step": t * 1e3, "tokens_per_s": cfg.batch * cfg.seq_len / t,
+                                     "tflops": cfg.flops_per_step() / t / 1e12, "loss": float(model.loss.item()),
+                                     "params": cfg.n_params(), "algorithmic_flop_per_step": cfg.flops_per_step(),
+                                     "precision": "bf16 GEMM/attention operands, fp32 master weights, grads, AdamW"}
+    del model
     torch.cuda.empty_cache()
     return res
 

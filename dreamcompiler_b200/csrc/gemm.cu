@@ -123,18 +123,26 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const TileSched sched{args.tiles_m, args.tiles_n, args.group_m};
-  const int num_tiles = args.tiles_m * args.tiles_n;
-  const int nk = (args.K + BK - 1) / BK;
+  // Work units: (output tile, K slice); unit u -> tile u / splits, slice u % splits.
+  const int splits = args.splits;
+  const int num_tiles = args.tiles_m * args.tiles_n * splits;
+  const int nk_all = (args.K + BK - 1) / BK;
+  const int kper = (nk_all + splits - 1) / splits;
+  auto kslice = [&](int u, int& kb0, int& kb1) {
+    kb0 = (u % splits) * kper;
+    kb1 = min(nk_all, kb0 + kper);
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (elect_one_lane()) {
       uint32_t fill = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
-        int tm, tn;
-        sched.coords(t, tm, tn);
+        int tm, tn, kb0, kb1;
+        sched.coords(t / splits, tm, tn);
+        kslice(t, kb0, kb1);
         const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < nk; ++kb, ++fill) {
+        for (int kb = kb0; kb < kb1; ++kb, ++fill) {
           const int s = fill % STAGES;
           const uint32_t round = fill / STAGES;
           if (!mbar_wait(&empty_bar[s], (round & 1) ^ 1, wc)) break;
@@ -182,7 +190,9 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb, ++fill) {
+        int kb0, kb1;
+        kslice(t, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++fill) {
           const int s = fill % STAGES;
           if (!mbar_wait(&full_bar[s], (fill / STAGES) & 1, wc)) {
             ok = false;
@@ -196,7 +206,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t ao = kstep_offset<A_MN, Cfg::ESZ>(kk), bo = kstep_offset<B_MN, Cfg::ESZ>(kk);
             const uint64_t adesc = sw128_desc(sa + ao, a_lbo, 1024);
             const uint64_t bdesc = sw128_desc(sb + bo, b_lbo, 1024);
-            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
             if (TF32) {
               const uint64_t adesc_lo = sw128_desc(sa + Cfg::A_BYTES + ao, a_lbo, 1024);
               const uint64_t bdesc_lo = sw128_desc(sb + Cfg::B_BYTES + bo, b_lbo, 1024);
@@ -232,17 +242,17 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
       tc_fence_after();
       int tm, tn;
-      sched.coords(t, tm, tn);
+      sched.coords(t / splits, tm, tn);
       const int m = tm * BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       if (args.tma_out) {
         constexpr int CW32 = 32;  // fp32 columns per 32-column TMEM load
-        const int cw = args.c_bf16 ? 64 : 32;  // columns per 128-byte staged row
+        const int cw = (args.c_bf16 && args.tma_out != 3) ? 64 : 32;  // columns per 128-byte staged row
 #pragma unroll 1
         for (int c = 0; c < BN; c += cw) {
           uint32_t r[64];
           tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-          if (args.c_bf16) tmem_ld32(taddr + c + CW32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          if (cw == 64) tmem_ld32(taddr + c + CW32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
           tmem_ld_wait();
           if (c + cw >= BN) {  // last loads of this accumulator: hand it back to the MMA warp
             tc_fence_before();
@@ -255,7 +265,10 @@ __global__ void __launch_bounds__(192, 1)
           if (lane == 0 && issued >= 2) bulk_wait_read1();  // the store issued from this buffer has read it
           __syncwarp();
           uint32_t w[32];
-          if (args.c_bf16) {
+          if (args.tma_out == 3) {  // raw partial sums
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = r[j];
+          } else if (args.c_bf16) {
 #pragma unroll
             for (int j = 0; j < 64; j += 2) {
               float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
@@ -285,7 +298,9 @@ __global__ void __launch_bounds__(192, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (args.tma_out == 2)
+            if (args.tma_out == 3)
+              tma_store_3d(&tmC, st, n0, tm * BM + q * 32, t % splits);
+            else if (args.tma_out == 2)
               tma_reduce_add_2d(&tmC, st, n0, tm * BM + q * 32);
             else
               tma_store_2d(&tmC, st, n0, tm * BM + q * 32);
@@ -432,6 +447,31 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
 }
 
 // ---------------------------------------------------------------------------
+// Split-K reduction: C = epilogue(sum over slices of the fp32 partial tiles),
+// four columns per thread, slices added in order (deterministic).
+// ---------------------------------------------------------------------------
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int ldw, GemmArgs a) {
+  const int nq = (a.N + 3) / 4;
+  const long long total = (long long)a.M * nq;
+  const size_t slice = (size_t)a.M * ldw;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / nq), n = (int)(i % nq) * 4;
+    float4 acc = *reinterpret_cast<const float4*>(ws + (size_t)m * ldw + n);
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(ws + s * slice + (size_t)m * ldw + n);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const float r[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (n + j < a.N) gemm_store_one(a, m, n + j, r[j]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 static bool encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esz, uint64_t inner,
@@ -487,9 +527,35 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   a.tiles_m = (args.M + Cfg::BM - 1) / Cfg::BM;
   a.tiles_n = (args.N + Cfg::BN - 1) / Cfg::BN;
   a.group_m = 16;
+  // Split K over CTAs when the output tiles alone would leave most SMs idle
+  // (the weight-gradient GEMMs dW = dY^T X: small outputs, K = tokens).
+  a.splits = 1;
+  float* ws = nullptr;
+  int ldw = 0;
+  {
+    const int tiles = a.tiles_m * a.tiles_n;
+    const int nk_all = (args.K + Cfg::BK - 1) / Cfg::BK;
+    if (a.n_extra == 0 && tiles * 2 <= num_sms() && nk_all >= 16) {
+      const int sp = std::min(std::min(num_sms() / tiles, nk_all / 8), 16);
+      ldw = (a.N + 3) & ~3;
+      if (sp >= 2 && (ws = (float*)library_scratch((size_t)sp * a.M * ldw * sizeof(float), stream)) != nullptr)
+        a.splits = sp;
+    }
+  }
   // Epilogue path (see GemmArgs::tma_out).
   CUtensorMap mc{};
-  {
+  if (a.splits > 1) {
+    auto enc = get_tensor_map_encoder();
+    const cuuint64_t dims[3] = {(cuuint64_t)a.N, (cuuint64_t)a.M, (cuuint64_t)a.splits};
+    const cuuint64_t strides[2] = {(cuuint64_t)ldw * 4, (cuuint64_t)a.M * ldw * 4};
+    const cuuint32_t box[3] = {32, 32, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (!enc || enc(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ws, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    a.tma_out = 3;
+  } else {
     const int esz = a.c_bf16 ? 2 : 4;
     const bool aligned = ((uintptr_t)a.C & 15) == 0 && ((long long)a.ldc * esz) % 16 == 0;
     int mode = 0;
@@ -520,11 +586,16 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  const int tiles = a.tiles_m * a.tiles_n;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int units = a.tiles_m * a.tiles_n * a.splits;
+  const int grid = units < num_sms() ? units : num_sms();
   {
     TimerScope timer(stream);
     kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, mc, a);
+  }
+  if (a.splits > 1) {
+    const long long quads = (long long)a.M * ((a.N + 3) / 4);
+    const int rb = (int)std::min<long long>((quads + 255) / 256, (long long)num_sms() * 8);
+    splitk_reduce_kernel<<<rb, 256, 0, stream>>>(ws, a.splits, ldw, a);
   }
   return cudaGetLastError();
 }

@@ -28,8 +28,11 @@ struct GemmArgs {
   int n_extra;
   // Output path of the epilogue: 0 per-thread stores (any layout, beta, extra
   // destinations); 1 TMA tensor store of staged tiles (beta = 0); 2 TMA
-  // reduce-add of staged tiles (fp32 C, beta = 1, no ReLU).
+  // reduce-add of staged tiles (fp32 C, beta = 1, no ReLU); 3 raw fp32
+  // partial sums of K slice z into a split-K workspace [splits][M][N] (the
+  // bias / beta / ReLU epilogue then runs in the reduction kernel).
   int tma_out;
+  int splits;  // K slices per output tile (1: no split)
 };
 
 __device__ __forceinline__ float gemm_finish(const GemmArgs& a, int n, float acc, float old) {

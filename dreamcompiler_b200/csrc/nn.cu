@@ -85,9 +85,13 @@ __global__ void ln_bwd_kernel(const float* __restrict__ x, const float* __restri
 constexpr float kGeluK = 0.7978845608028654f;  // sqrt(2/pi)
 constexpr float kGeluC = 0.044715f;
 
-__global__ void gelu_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n) {
+__device__ __forceinline__ float ld_as_float(const float* p, long long i) { return p[i]; }
+__device__ __forceinline__ float ld_as_float(const __nv_bfloat16* p, long long i) { return __bfloat162float(p[i]); }
+
+template <typename TX>
+__global__ void gelu_fwd_kernel(const TX* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const float v = x[i];
+    const float v = ld_as_float(x, i);
     const float t = tanhf(kGeluK * fmaf(kGeluC * v, v * v, v));
     y[i] = __float2bfloat16_rn(0.5f * v * (1.f + t));
   }
@@ -95,14 +99,15 @@ __global__ void gelu_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* __re
 
 // dx = (0.5*(1+th) + 0.5*x*(1-th^2)*k*(1+3c x^2)) * dy, written as bf16 (the
 // next consumer is a GEMM).
-__global__ void gelu_bwd_kernel(const float* __restrict__ x, const float* __restrict__ dy,
-                                __nv_bfloat16* __restrict__ dx, long long n) {
+template <typename TX, typename TG>
+__global__ void gelu_bwd_kernel(const TX* __restrict__ x, const TG* __restrict__ dy, __nv_bfloat16* __restrict__ dx,
+                                long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const float v = x[i];
+    const float v = ld_as_float(x, i);
     const float th = tanhf(kGeluK * fmaf(kGeluC * v, v * v, v));
     const float dinner = kGeluK * fmaf(3.f * kGeluC * v, v, 1.f);
     const float g = 0.5f * (1.f + th) + 0.5f * v * (1.f - th * th) * dinner;
-    dx[i] = __float2bfloat16_rn(g * dy[i]);
+    dx[i] = __float2bfloat16_rn(g * ld_as_float(dy, i));
   }
 }
 
@@ -325,19 +330,37 @@ dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rst
   return cuda_status(cudaGetLastError(), "dgx_layernorm_bwd");
 }
 
-dgx_status dgx_gelu_fwd(const float* x, void* y16, long long n, void* stream) {
+dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream) {
   if (n < 0) return set_error(DGX_EINVAL, "dgx_gelu_fwd: n=%lld", n);
+  if (x_type != DGX_F32 && x_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gelu_fwd: type %d", x_type);
   if (n == 0) return DGX_OK;
   if (!x || !y16) return set_error(DGX_EINVAL, "dgx_gelu_fwd: null pointer");
-  gelu_fwd_kernel<<<ew_grid(n), 256, 0, (cudaStream_t)stream>>>(x, (__nv_bfloat16*)y16, n);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (x_type == DGX_F32)
+    gelu_fwd_kernel<float><<<ew_grid(n), 256, 0, s>>>((const float*)x, (__nv_bfloat16*)y16, n);
+  else
+    gelu_fwd_kernel<__nv_bfloat16><<<ew_grid(n), 256, 0, s>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)y16, n);
   return cuda_status(cudaGetLastError(), "dgx_gelu_fwd");
 }
 
-dgx_status dgx_gelu_bwd(const float* x, const float* dy, void* dx16, long long n, void* stream) {
+dgx_status dgx_gelu_bwd(const void* x, int x_type, const void* dy, int dy_type, void* dx16, long long n, void* stream) {
   if (n < 0) return set_error(DGX_EINVAL, "dgx_gelu_bwd: n=%lld", n);
+  const bool xt = x_type == DGX_F32 || x_type == DGX_BF16, gt = dy_type == DGX_F32 || dy_type == DGX_BF16;
+  if (!xt || !gt) return set_error(DGX_EINVAL, "dgx_gelu_bwd: types %d %d", x_type, dy_type);
   if (n == 0) return DGX_OK;
   if (!x || !dy || !dx16) return set_error(DGX_EINVAL, "dgx_gelu_bwd: null pointer");
-  gelu_bwd_kernel<<<ew_grid(n), 256, 0, (cudaStream_t)stream>>>(x, dy, (__nv_bfloat16*)dx16, n);
+  cudaStream_t s = (cudaStream_t)stream;
+  __nv_bfloat16* o = (__nv_bfloat16*)dx16;
+  const int g = ew_grid(n);
+  if (x_type == DGX_F32 && dy_type == DGX_F32)
+    gelu_bwd_kernel<float, float><<<g, 256, 0, s>>>((const float*)x, (const float*)dy, o, n);
+  else if (x_type == DGX_F32)
+    gelu_bwd_kernel<float, __nv_bfloat16><<<g, 256, 0, s>>>((const float*)x, (const __nv_bfloat16*)dy, o, n);
+  else if (dy_type == DGX_F32)
+    gelu_bwd_kernel<__nv_bfloat16, float><<<g, 256, 0, s>>>((const __nv_bfloat16*)x, (const float*)dy, o, n);
+  else
+    gelu_bwd_kernel<__nv_bfloat16, __nv_bfloat16><<<g, 256, 0, s>>>((const __nv_bfloat16*)x,
+                                                                    (const __nv_bfloat16*)dy, o, n);
   return cuda_status(cudaGetLastError(), "dgx_gelu_bwd");
 }
 

@@ -9,7 +9,9 @@ attention on dgx_flash_fwd / dgx_flash_bwd, everything else on the libdgx
 device ops (dgx_layernorm_*, dgx_gelu_*, dgx_embedding_*, dgx_softmax_nll,
 dgx_colsum, dgx_adamw, the head layout permutes). Parameters, gradients and
 AdamW state are fp32; the GEMMs read bf16 copies of the weights refreshed
-after each update.
+after each update. The residual stream and its gradient stay fp32; tensors
+whose only consumers read bf16 (the QKV projection, the MLP pre-activation
+and its gradient) are produced in bf16 by the GEMM epilogue.
 
 All buffers are allocated up front, so one `step` can be captured in a CUDA
 graph and replayed (the AdamW step count lives on the device).
@@ -109,12 +111,12 @@ class GPT:
         self.h16 = [torch.empty(R, d, device=dev, dtype=bf16) for _ in range(2 * c.n_layer + 1)]
         self.mu = [torch.empty(R, device=dev, dtype=f32) for _ in range(2 * c.n_layer + 1)]
         self.rs = [torch.empty(R, device=dev, dtype=f32) for _ in range(2 * c.n_layer + 1)]
-        self.qkv32 = torch.empty(R, 3 * d, device=dev, dtype=f32)
+        self.qkv16 = torch.empty(R, 3 * d, device=dev, dtype=bf16)
         heads = lambda: torch.empty(B * H, S, hd, device=dev, dtype=bf16)
         self.q, self.k, self.v, self.o = ([heads() for _ in range(c.n_layer)] for _ in range(4))
         self.lse = [torch.empty(B * H, S, device=dev, dtype=f32) for _ in range(c.n_layer)]
         self.att16 = [torch.empty(R, d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
-        self.u32 = [torch.empty(R, 4 * d, device=dev, dtype=f32) for _ in range(c.n_layer)]
+        self.u16 = [torch.empty(R, 4 * d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
         self.g16 = [torch.empty(R, 4 * d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
         self.logits = torch.empty(R, Vp, device=dev, dtype=f32)
         self.dlogits = torch.empty(R, Vp, device=dev, dtype=bf16)
@@ -123,7 +125,7 @@ class GPT:
         self.dx = torch.empty(R, d, device=dev, dtype=f32)
         self.dx16 = torch.empty(R, d, device=dev, dtype=bf16)
         self.dh = torch.empty(R, d, device=dev, dtype=f32)
-        self.dg = torch.empty(R, 4 * d, device=dev, dtype=f32)
+        self.dg16 = torch.empty(R, 4 * d, device=dev, dtype=bf16)
         self.du16 = torch.empty(R, 4 * d, device=dev, dtype=bf16)
         self.dqkv16 = torch.empty(R, 3 * d, device=dev, dtype=bf16)
         self.dO, self.dq, self.dk, self.dv = (heads() for _ in range(4))
@@ -172,17 +174,17 @@ class GPT:
             h, h2 = self.h16[2 * l], self.h16[2 * l + 1]
             _c("dgx_layernorm_fwd", x0.data_ptr(), h.data_ptr(), self.mu[2 * l].data_ptr(), self.rs[2 * l].data_ptr(),
                R, d, s)
-            gemm(h, w[f"Wqkv{l}"], transB=True, out=self.qkv32, bias=p[f"bqkv{l}"])
+            gemm(h, w[f"Wqkv{l}"], transB=True, out=self.qkv16, bias=p[f"bqkv{l}"])
             for i, dst in enumerate((self.q[l], self.k[l], self.v[l])):
-                _c("dgx_rows_to_heads", self.qkv32.data_ptr(), L.DGX_F32, 3 * d, i * d, dst.data_ptr(), B, S, H, hd, s)
+                _c("dgx_rows_to_heads", self.qkv16.data_ptr(), L.DGX_BF16, 3 * d, i * d, dst.data_ptr(), B, S, H, hd, s)
             flash_fwd(self.q[l], self.k[l], self.v[l], out=self.o[l], lse=self.lse[l])
             _c("dgx_heads_to_rows", self.o[l].data_ptr(), self.att16[l].data_ptr(), d, 0, B, S, H, hd, s)
             x1.copy_(x0)
             gemm(self.att16[l], w[f"Wo{l}"], transB=True, out=x1, bias=p[f"bo{l}"], beta=1.0)  # x1 = x0 + att Wo^T + bo
             _c("dgx_layernorm_fwd", x1.data_ptr(), h2.data_ptr(), self.mu[2 * l + 1].data_ptr(),
                self.rs[2 * l + 1].data_ptr(), R, d, s)
-            gemm(h2, w[f"W1{l}"], transB=True, out=self.u32[l], bias=p[f"b1{l}"])
-            _c("dgx_gelu_fwd", self.u32[l].data_ptr(), self.g16[l].data_ptr(), self.u32[l].numel(), s)
+            gemm(h2, w[f"W1{l}"], transB=True, out=self.u16[l], bias=p[f"b1{l}"])
+            _c("dgx_gelu_fwd", self.u16[l].data_ptr(), L.DGX_BF16, self.g16[l].data_ptr(), self.u16[l].numel(), s)
             x2.copy_(x1)
             gemm(self.g16[l], w[f"W2{l}"], transB=True, out=x2, bias=p[f"b2{l}"], beta=1.0)
         xL, hf = self.x[2 * c.n_layer], self.h16[2 * c.n_layer]
@@ -203,10 +205,11 @@ class GPT:
             h, h2 = self.h16[2 * l], self.h16[2 * l + 1]
             # MLP: x2 = x1 + gelu(h2 W1^T + b1) W2^T + b2
             conv16(self.dx, self.dx16)
-            gemm(self.dx16, w[f"W2{l}"], out=self.dg)                     # dg = dx W2
+            gemm(self.dx16, w[f"W2{l}"], out=self.dg16)                   # dg = dx W2
             gemm(self.dx16, self.g16[l], transA=True, out=g[f"W2{l}"])     # dW2 = dx^T g
             _c("dgx_colsum", self.dx.data_ptr(), L.DGX_F32, g[f"b2{l}"].data_ptr(), R, d, 0, s)
-            _c("dgx_gelu_bwd", self.u32[l].data_ptr(), self.dg.data_ptr(), self.du16.data_ptr(), self.du16.numel(), s)
+            _c("dgx_gelu_bwd", self.u16[l].data_ptr(), L.DGX_BF16, self.dg16.data_ptr(), L.DGX_BF16,
+               self.du16.data_ptr(), self.du16.numel(), s)
             gemm(self.du16, w[f"W1{l}"], out=self.dh)                     # dh2 = du W1
             gemm(self.du16, h2, transA=True, out=g[f"W1{l}"])              # dW1 = du^T h2
             _c("dgx_colsum", self.du16.data_ptr(), L.DGX_BF16, g[f"b1{l}"].data_ptr(), R, 4 * d, 0, s)

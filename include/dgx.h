@@ -176,10 +176,10 @@ dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd
  * (runtime/ops/autograd.inc:453-470); accumulate = 1 adds into dx. */
 dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rstd, const float* dy, float* dx, int R,
                              int C, int accumulate, void* stream);
-/* y16 = bf16(gelu(x)), tanh form (runtime/io/builtins.inc:548-560). */
-dgx_status dgx_gelu_fwd(const float* x, void* y16, long long n, void* stream);
-/* dx16 = bf16(gelu'(x) * dy) (runtime/ops/autograd.inc:293-303). */
-dgx_status dgx_gelu_bwd(const float* x, const float* dy, void* dx16, long long n, void* stream);
+/* y16 = bf16(gelu(x)), tanh form (runtime/io/builtins.inc:548-560); x DGX_F32 or DGX_BF16. */
+dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream);
+/* dx16 = bf16(gelu'(x) * dy) (runtime/ops/autograd.inc:293-303); x, dy DGX_F32 or DGX_BF16. */
+dgx_status dgx_gelu_bwd(const void* x, int x_type, const void* dy, int dy_type, void* dx16, long long n, void* stream);
 /* x[i] = W[tok[i]] + P[i % S] (P may be NULL): dream_embedding
  * (runtime/nn/training.inc:579-600) plus the broadcast position add. */
 dgx_status dgx_embedding_fwd(const int* tok, const float* W, const float* P, float* x, int n, int S, int d, int V,

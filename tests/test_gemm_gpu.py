@@ -178,3 +178,35 @@ def test_config4_bf16_4096_full_and_16384_sampled(dgx, orc):
             ref = orc.gemm_rows_f64(Ab, Bb, idx)
             assert normwise(Cn[idx], ref) < BF16_TOL
         del A, B, Ab, Bb, C
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("shape,tA", [((384, 384, 16384), 1), ((200, 130, 8192), 0), ((72, 384, 4096), 1)])
+def test_split_k_small_outputs_long_k(dgx, orc, dtype, shape, tA):
+    """Small outputs over a long K (the weight-gradient GEMMs dW = dY^T X)
+    take the split-K path: K slices on separate CTAs, fp32 partial tiles
+    summed in a fixed order, then the bias / beta / ReLU epilogue."""
+    M, N, K = shape
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((K, M) if tA else (M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    td = torch.bfloat16 if dtype == "bf16" else torch.float32
+    Ad, Bd = cuda(A, td), cuda(B, td)
+    Ar = bf16_round(A) if dtype == "bf16" else A.astype(np.float64)
+    Br = bf16_round(B) if dtype == "bf16" else B.astype(np.float64)
+    ref = (Ar.T if tA else Ar) @ Br
+    tol = BF16_TOL if dtype == "bf16" else F32_TOL
+    C = dgx.gemm(Ad, Bd, transA=bool(tA))
+    Cb = cuda(C0)
+    dgx.gemm(Ad, Bd, transA=bool(tA), out=Cb, beta=1.0, bias=cuda(bias), relu=True)
+    C16 = dgx.gemm(Ad, Bd, transA=bool(tA), out_dtype=torch.bfloat16)
+    dgx.sync_check()
+    assert normwise(C.cpu().numpy(), ref) < tol
+    assert normwise(Cb.cpu().numpy(), np.maximum(ref + C0 + bias, 0)) < tol
+    assert normwise(C16.float().cpu().numpy(), ref) < max(tol, 1e-2)
+    # deterministic: the same call twice gives the same bits
+    C2 = dgx.gemm(Ad, Bd, transA=bool(tA))
+    dgx.sync_check()
+    assert torch.equal(C, C2)
