@@ -124,6 +124,12 @@ void dgx_set_timer_events(void* start, void* stop) {
   g_timer_stop = (cudaEvent_t)stop;
 }
 
+dgx_status dgx_gemm_set_algo(int algo) {
+  if (algo != 0 && algo != 1) return set_error(DGX_EINVAL, "dgx_gemm_set_algo: %d", algo);
+  gemm_set_algo(algo);
+  return DGX_OK;
+}
+
 dgx_status dgx_init(int device) {
   int n = 0;
   cudaError_t e = cudaGetDeviceCount(&n);

@@ -625,7 +625,12 @@ static cudaError_t dispatch_tc(const GemmArgs& args, const void* A, const void* 
   return launch_tc<TF32, true, true>(args, A, B, A2, B2, s);
 }
 
+// 0: single-CTA kernel only; 1 (default): the 2-SM kernel (gemm2.cu) where eligible.
+static int g_gemm_algo = 1;
+void gemm_set_algo(int algo) { g_gemm_algo = algo; }
+
 cudaError_t gemm_bf16_tc(const GemmArgs& args, const void* A, const void* B, cudaStream_t s) {
+  if (g_gemm_algo == 1 && gemm2_eligible(args, A, B)) return gemm2_launch(args, A, B, s);
   return dispatch_tc<false>(args, A, B, nullptr, nullptr, s);
 }
 

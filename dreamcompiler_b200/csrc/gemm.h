@@ -35,6 +35,11 @@ struct GemmArgs {
   int splits;  // K slices per output tile (1: no split)
 };
 
+// 2-SM bf16 kernel (gemm2.cu) and the algorithm switch.
+bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B);
+cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cudaStream_t stream);
+void gemm_set_algo(int algo);
+
 __device__ __forceinline__ float gemm_finish(const GemmArgs& a, int n, float acc, float old) {
   float v = acc;
   if (a.beta != 0.f) v = fmaf(a.beta, old, v);

@@ -92,6 +92,11 @@ dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, 
                     int transA, int transB, dgx_dtype ab_type, dgx_dtype c_type, int f32_mode, const float* bias,
                     int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream);
 size_t dgx_gemm_workspace_size(int M, int N, int K, int transA, int transB, dgx_dtype ab_type, int f32_mode);
+/* bf16 GEMM kernel selection: 0 = single-CTA tiles (128 x 256) only;
+ * 1 (default) = 2-SM tiles (256 x 256 over a CTA pair, tcgen05 cta_group::2)
+ * wherever they apply (A not transposed, beta 0 or fp32 accumulate, K >= 1024,
+ * enough tiles), single-CTA tiles elsewhere. Process-wide. */
+dgx_status dgx_gemm_set_algo(int algo);
 
 /*
  * Batched GEMM C_b = A_b . B_b over `batch` contiguous [M,K] x [K,N] blocks.

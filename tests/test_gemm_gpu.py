@@ -210,3 +210,39 @@ def test_split_k_small_outputs_long_k(dgx, orc, dtype, shape, tA):
     C2 = dgx.gemm(Ad, Bd, transA=bool(tA))
     dgx.sync_check()
     assert torch.equal(C, C2)
+
+
+@pytest.mark.parametrize("algo", [0, 1])
+@pytest.mark.parametrize("shape,tB,cdt,beta,bias,relu", [
+    ((512, 768, 1024), True, "f32", 0.0, True, False),
+    ((1000, 600, 1100), False, "f32", 1.0, True, False),      # ragged M, N, K; fp32 accumulate
+    ((2048, 1152, 1536), True, "bf16", 0.0, True, True),
+    ((8448, 8192, 1024), False, "bf16", 0.0, False, False),  # many 256 x 256 pair tiles
+])
+def test_two_sm_and_single_cta_kernels_agree(dgx, algo, shape, tB, cdt, beta, bias, relu):
+    """The bf16 GEMM through the single-CTA kernel (algo 0) and through the
+    2-SM CTA-pair kernel (algo 1, tcgen05 cta_group::2) against the f64
+    product of the same bf16 inputs."""
+    from dreamcompiler_b200 import _lib
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + algo)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn((N, K) if tB else (K, N), device="cuda", generator=g).bfloat16()
+    td = torch.float32 if cdt == "f32" else torch.bfloat16
+    C0 = torch.randn(M, N, device="cuda", generator=g).to(td)
+    bb = torch.randn(N, device="cuda", generator=g) if bias else None
+    C = C0.clone()
+    try:
+        _lib.call("dgx_gemm_set_algo", algo)
+        dgx.gemm(A, B, transB=tB, out=C, beta=beta, bias=bb, relu=relu)
+        dgx.sync_check()
+    finally:
+        _lib.call("dgx_gemm_set_algo", 1)
+    ref = A.double() @ (B.double().t() if tB else B.double())
+    if beta:
+        ref += C0.double()
+    if bias:
+        ref += bb.double()
+    if relu:
+        ref = ref.clamp_min(0)
+    assert normwise(C.double().cpu().numpy(), ref.cpu().numpy()) < (1e-5 if cdt == "f32" else 1e-2)
