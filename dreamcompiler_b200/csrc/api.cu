@@ -59,8 +59,8 @@ int num_sms() {
 
 struct DeviceState {
   uint32_t* err_word = nullptr;
-  void* scratch = nullptr;
-  size_t scratch_bytes = 0;
+  void* scratch[kScratchSlots] = {};
+  size_t scratch_bytes[kScratchSlots] = {};
 };
 static std::mutex g_dev_mu;
 static DeviceState g_dev[64];
@@ -76,27 +76,30 @@ uint32_t* device_error_word() {
   return st.err_word;
 }
 
-void* library_scratch(size_t bytes, cudaStream_t s) {
+void* library_scratch_slot(int slot, size_t bytes, cudaStream_t s) {
+  if (slot < 0 || slot >= kScratchSlots) return nullptr;
   const int d = current_device();
   std::lock_guard<std::mutex> lk(g_dev_mu);
   DeviceState& st = g_dev[d & 63];
-  if (st.scratch_bytes < bytes) {
+  if (st.scratch_bytes[slot] < bytes) {
     // The old buffer may still be read by queued work on `s`.
-    if (st.scratch) {
+    if (st.scratch[slot]) {
       cudaStreamSynchronize(s);
-      cudaFree(st.scratch);
-      st.scratch = nullptr;
-      st.scratch_bytes = 0;
+      cudaFree(st.scratch[slot]);
+      st.scratch[slot] = nullptr;
+      st.scratch_bytes[slot] = 0;
     }
     size_t want = bytes < (64u << 20) ? (64u << 20) : bytes;
-    if (cudaMalloc(&st.scratch, want) != cudaSuccess) {
+    if (cudaMalloc(&st.scratch[slot], want) != cudaSuccess) {
       cudaGetLastError();
       return nullptr;
     }
-    st.scratch_bytes = want;
+    st.scratch_bytes[slot] = want;
   }
-  return st.scratch;
+  return st.scratch[slot];
 }
+
+void* library_scratch(size_t bytes, cudaStream_t s) { return library_scratch_slot(kScratchGeneral, bytes, s); }
 
 static thread_local cudaEvent_t g_timer_start = nullptr, g_timer_stop = nullptr;
 
@@ -204,7 +207,17 @@ dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, 
   a.relu = (epilogue == DGX_EPI_BIAS_RELU || epilogue == DGX_EPI_RELU);
   a.beta = beta;
   a.err = device_error_word();
-  if (K == 0) {
+  return gemm_run(a, A, B, ab_type, f32_mode, workspace, workspace_bytes, s);
+}
+
+}  // extern "C"
+
+namespace dgx {
+
+// Kernel choice for a validated GemmArgs (single or batched product).
+dgx_status gemm_run(const GemmArgs& a, const void* A, const void* B, dgx_dtype ab_type, int f32_mode,
+                    void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (a.K == 0) {
     // Degenerate contraction: C = beta*C (+bias)(relu); the SIMT kernel handles it.
     return cuda_status(gemm_simt(a, A, B, ab_type == DGX_BF16, s), "dgx_gemm simt");
   }
@@ -229,17 +242,60 @@ dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, 
   return cuda_status(gemm_simt(a, A, B, 0, s), "dgx_gemm f32 simt");
 }
 
-dgx_status dgx_bmm(const void* A, const void* B, void* C, int batch, int M, int N, int K, dgx_dtype ab_type,
-                   dgx_dtype c_type, void* stream) {
-  if (batch < 0) return set_error(DGX_EINVAL, "dgx_bmm: negative batch");
+}  // namespace dgx
+
+extern "C" {
+
+dgx_status dgx_gemm_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K, int lda,
+                            int ldb, int ldc, long long strideA, long long strideB, long long strideC, int transA,
+                            int transB, dgx_dtype ab_type, dgx_dtype c_type, float beta, void* stream) {
+  if (batch < 0 || M < 0 || N < 0 || K < 0)
+    return set_error(DGX_EINVAL, "dgx_gemm_batched: negative size %d x %dx%dx%d", batch, M, N, K);
+  if (batch == 0 || M == 0 || N == 0) return DGX_OK;
+  if (!C || (K > 0 && (!A || !B))) return set_error(DGX_EINVAL, "dgx_gemm_batched: null operand");
+  if (ab_type != DGX_F32 && ab_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gemm_batched: ab_type %d", ab_type);
+  if (c_type != DGX_F32 && c_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gemm_batched: c_type %d", c_type);
+  const int min_lda = transA ? M : K, min_ldb = transB ? K : N;
+  if (lda < min_lda || ldb < min_ldb || ldc < N)
+    return set_error(DGX_EINVAL, "dgx_gemm_batched: leading dimension too small (lda %d ldb %d ldc %d)", lda, ldb,
+                     ldc);
+  // Operands may overlap or repeat across batches (stride 0 broadcasts one
+  // operand); the outputs may not.
+  if (batch > 1 && (strideA < 0 || strideB < 0 || strideC < (long long)M * ldc))
+    return set_error(DGX_EINVAL, "dgx_gemm_batched: bad batch strides (%lld %lld %lld)", strideA, strideB, strideC);
   const size_t esz = ab_type == DGX_BF16 ? 2 : 4, csz = c_type == DGX_BF16 ? 2 : 4;
-  for (int b = 0; b < batch; ++b) {
-    dgx_status st = dgx_gemm((const char*)A + (size_t)b * M * K * esz, (const char*)B + (size_t)b * K * N * esz,
-                             (char*)C + (size_t)b * M * N * csz, M, N, K, K, N, N, 0, 0, ab_type, c_type,
-                             DGX_F32_3XTF32, nullptr, DGX_EPI_NONE, 0.f, nullptr, 0, stream);
+  // One launch per chunk of batches (the grid's z extent bounds the split and
+  // fallback kernels to 32767 batches a launch).
+  constexpr int kMaxBatch = 32767;
+  for (int b0 = 0; b0 < batch; b0 += kMaxBatch) {
+    GemmArgs a{};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.lda = lda;
+    a.ldb = ldb;
+    a.ldc = ldc;
+    a.transA = transA ? 1 : 0;
+    a.transB = transB ? 1 : 0;
+    a.C = (char*)C + (size_t)b0 * strideC * csz;
+    a.c_bf16 = c_type == DGX_BF16;
+    a.beta = beta;
+    a.err = device_error_word();
+    a.batch = batch - b0 < kMaxBatch ? batch - b0 : kMaxBatch;
+    a.sA = strideA;
+    a.sB = strideB;
+    a.sC = strideC;
+    dgx_status st = gemm_run(a, (const char*)A + (size_t)b0 * strideA * esz, (const char*)B + (size_t)b0 * strideB * esz,
+                             ab_type, DGX_F32_3XTF32, nullptr, 0, (cudaStream_t)stream);
     if (st != DGX_OK) return st;
   }
   return DGX_OK;
+}
+
+dgx_status dgx_bmm(const void* A, const void* B, void* C, int batch, int M, int N, int K, dgx_dtype ab_type,
+                   dgx_dtype c_type, void* stream) {
+  return dgx_gemm_batched(A, B, C, batch, M, N, K, K, N, N, (long long)M * K, (long long)K * N, (long long)M * N, 0,
+                          0, ab_type, c_type, 0.f, stream);
 }
 
 }  // extern "C"

@@ -25,9 +25,14 @@ uint32_t* device_error_word();  // per-device word in global memory
 dgx_status set_error(dgx_status st, const char* fmt, ...);
 dgx_status cuda_status(cudaError_t e, const char* what);
 
-// Per-device scratch buffer owned by the library (grown on demand with
-// cudaMalloc, reused across calls on the same stream order).
-void* library_scratch(size_t bytes, cudaStream_t s);
+// Per-device scratch buffers owned by the library (grown on demand with
+// cudaMalloc, reused across calls on the same stream order). Separate slots
+// for buffers that are live at the same time within one call: the GEMM's
+// split-K partial tiles (kScratchSplitK) while its operands may sit in the
+// general buffer (the 3xTF32 planes).
+constexpr int kScratchGeneral = 0, kScratchSplitK = 1, kScratchSlots = 2;
+void* library_scratch_slot(int slot, size_t bytes, cudaStream_t s);
+void* library_scratch(size_t bytes, cudaStream_t s);  // the general slot
 
 // Brackets one kernel launch with the events set by dgx_set_timer_events
 // (if any), then clears them. Construct right before the launch.

@@ -123,9 +123,11 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const TileSched sched{args.tiles_m, args.tiles_n, args.group_m};
-  // Work units: (output tile, K slice); unit u -> tile u / splits, slice u % splits.
+  // Work units: (batch, output tile, K slice); unit u -> batch u / per_batch,
+  // tile (u % per_batch) / splits, slice u % splits.
   const int splits = args.splits;
-  const int num_tiles = args.tiles_m * args.tiles_n * splits;
+  const int per_batch = args.tiles_m * args.tiles_n * splits;
+  const int num_tiles = per_batch * (args.batch > 1 ? args.batch : 1);
   const int nk_all = (args.K + BK - 1) / BK;
   const int kper = (nk_all + splits - 1) / splits;
   auto kslice = [&](int u, int& kb0, int& kb1) {
@@ -139,7 +141,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t fill = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int tm, tn, kb0, kb1;
-        sched.coords(t / splits, tm, tn);
+        const int bz = t / per_batch;
+        sched.coords((t - bz * per_batch) / splits, tm, tn);
         kslice(t, kb0, kb1);
         const int m0 = tm * BM, n0 = tn * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++fill) {
@@ -159,16 +162,16 @@ __global__ void __launch_bounds__(192, 1)
             if (A_MN) {
 #pragma unroll
               for (int c = 0; c < BM / Cfg::CHUNK; ++c)
-                tma_load_2d(pa + c * BK * 128, ma, &full_bar[s], m0 + c * Cfg::CHUNK, k0);
+                tma_load_3d(pa + c * BK * 128, ma, &full_bar[s], m0 + c * Cfg::CHUNK, k0, bz);
             } else {
-              tma_load_2d(pa, ma, &full_bar[s], k0, m0);
+              tma_load_3d(pa, ma, &full_bar[s], k0, m0, bz);
             }
             if (B_MN) {
 #pragma unroll
               for (int c = 0; c < BN / Cfg::CHUNK; ++c)
-                tma_load_2d(pb + c * BK * 128, mb, &full_bar[s], n0 + c * Cfg::CHUNK, k0);
+                tma_load_3d(pb + c * BK * 128, mb, &full_bar[s], n0 + c * Cfg::CHUNK, k0, bz);
             } else {
-              tma_load_2d(pb, mb, &full_bar[s], k0, n0);
+              tma_load_3d(pb, mb, &full_bar[s], k0, n0, bz);
             }
           }
         }
@@ -242,7 +245,8 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
       tc_fence_after();
       int tm, tn;
-      sched.coords(t / splits, tm, tn);
+      const int bz = t / per_batch;
+      sched.coords((t - bz * per_batch) / splits, tm, tn);
       const int m = tm * BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       if (args.tma_out) {
@@ -298,12 +302,13 @@ __global__ void __launch_bounds__(192, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
+            // z: the K slice for split-K partials (unbatched), else the batch.
             if (args.tma_out == 3)
               tma_store_3d(&tmC, st, n0, tm * BM + q * 32, t % splits);
             else if (args.tma_out == 2)
-              tma_reduce_add_2d(&tmC, st, n0, tm * BM + q * 32);
+              tma_reduce_add_3d(&tmC, st, n0, tm * BM + q * 32, bz);
             else
-              tma_store_2d(&tmC, st, n0, tm * BM + q * 32);
+              tma_store_3d(&tmC, st, n0, tm * BM + q * 32, bz);
             bulk_commit();
           }
           ++issued;
@@ -316,7 +321,8 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld32(taddr + c, r);
           tmem_ld_wait();
           const int n0 = tn * BN + c;
-          if (m < args.M && n0 < args.N) gemm_store_row32(args, m, n0, reinterpret_cast<float*>(r));
+          if (m < args.M && n0 < args.N)
+            gemm_store_row32(args, m, n0, reinterpret_cast<float*>(r), (long long)bz * args.sC);
         }
         tc_fence_before();
         __syncwarp();
@@ -348,14 +354,17 @@ struct SplitJob {
   int rows, ld, src_t;
   float* hi;
   float* lo;
+  long long sx;  // source batch stride (elements); the planes of batch b start at b * rows * kpad
 };
-// blockIdx.z selects the operand: both are split by one launch.
+// blockIdx.z = 2 * batch + operand: both operands of every batch are split by
+// one launch.
 __global__ void split_tf32_kernel(SplitJob ja, SplitJob jb, int K, int kpad) {
   __shared__ float tile[32][33];
-  const SplitJob& j = blockIdx.z == 0 ? ja : jb;
-  const float* __restrict__ x = j.x;
-  float* __restrict__ hi = j.hi;
-  float* __restrict__ lo = j.lo;
+  const SplitJob& j = (blockIdx.z & 1) == 0 ? ja : jb;
+  const long long bz = blockIdx.z >> 1;
+  const float* __restrict__ x = j.x + bz * j.sx;
+  float* __restrict__ hi = j.hi + bz * (long long)j.rows * kpad;
+  float* __restrict__ lo = j.lo + bz * (long long)j.rows * kpad;
   const int rows = j.rows, ld = j.ld, src_t = j.src_t;
   const int r0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
   if (r0 >= rows) return;
@@ -405,6 +414,9 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
   __shared__ float Bs[16][64 + 1];
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  A += blockIdx.z * args.sA;  // batch (gridDim.z = 1 for a single product)
+  B += blockIdx.z * args.sB;
+  const long long boff = blockIdx.z * args.sC;
   float acc[4][4] = {};
   for (int k0 = 0; k0 < args.K; k0 += 16) {
     for (int i = threadIdx.x; i < 16 * 64; i += 256) {
@@ -441,7 +453,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
-      if (n < args.N) gemm_store_one(args, m, n, acc[i][j]);
+      if (n < args.N) gemm_store_one(args, m, n, acc[i][j], boff);
     }
   }
 }
@@ -474,37 +486,47 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static bool encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esz, uint64_t inner,
-                      uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+// 3-D tiled map [batch][outer][inner]; a single product is batch 1.
+static bool encode_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                      uint64_t batch, uint64_t row_pitch_bytes, uint64_t batch_pitch_bytes, uint32_t box_inner,
+                      uint32_t box_outer, CUtensorMapL2promotion l2) {
   auto enc = get_tensor_map_encoder();
   if (!enc) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_pitch_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  (void)esz;
-  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (batch <= 1) {
+    batch = 1;
+    batch_pitch_bytes = (row_pitch_bytes * outer + 15) & ~uint64_t(15);
+  }
+  cuuint64_t dims[3] = {inner, outer, batch};
+  cuuint64_t strides[2] = {row_pitch_bytes, batch_pitch_bytes};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
 // Operand descriptor: logical [rows(MN), K] operand, stored either K-major
-// (row r at base + r*ld, K contiguous) or MN-major (K row k at base + k*ld).
+// (row r at base + r*ld, K contiguous) or MN-major (K row k at base + k*ld);
+// `batch` such operands `bstride` elements apart.
 template <bool TF32>
 static bool make_operand_map(CUtensorMap* map, const void* base, bool mn_major, int mn, int K, int ld,
-                             int box_mn) {
+                             int box_mn, int batch, long long bstride) {
   using Cfg = GemmCfg<TF32>;  // element size, BK and the MN chunk do not depend on the tile width
   const CUtensorMapDataType dt = TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const uint64_t pitch = (uint64_t)ld * Cfg::ESZ;
-  if (mn_major) return encode_2d(map, base, dt, Cfg::ESZ, (uint64_t)mn, (uint64_t)K, pitch, Cfg::CHUNK, Cfg::BK);
-  return encode_2d(map, base, dt, Cfg::ESZ, (uint64_t)K, (uint64_t)mn, pitch, Cfg::BK, box_mn);
+  const uint64_t pitch = (uint64_t)ld * Cfg::ESZ, bpitch = (uint64_t)bstride * Cfg::ESZ;
+  if (mn_major)
+    return encode_3d(map, base, dt, (uint64_t)mn, (uint64_t)K, batch, pitch, bpitch, Cfg::CHUNK, Cfg::BK,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  return encode_3d(map, base, dt, (uint64_t)K, (uint64_t)mn, batch, pitch, bpitch, Cfg::BK, box_mn,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
 int gemm_tc_supported(const GemmArgs& a, int esz, const void* A, const void* B) {
-  // TMA wants 16-byte aligned bases and row pitches that are multiples of 16 bytes.
+  // TMA wants 16-byte aligned bases and row / batch pitches that are multiples
+  // of 16 bytes (a broadcast operand, batch stride 0, takes the SIMT kernel).
   if (((uintptr_t)A & 15) || ((uintptr_t)B & 15)) return 0;
   if (((long long)a.lda * esz) % 16 || ((long long)a.ldb * esz) % 16) return 0;
+  if (a.batch > 1 && ((a.sA * esz) % 16 || (a.sB * esz) % 16 || a.sA <= 0 || a.sB <= 0)) return 0;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
   return 1;
 }
@@ -514,11 +536,16 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
                              cudaStream_t stream) {
   using Cfg = GemmCfg<TF32, BN_>;
   CUtensorMap ma{}, mb{}, ma2{}, mb2{};
-  if (!make_operand_map<TF32>(&ma, A, A_MN, args.M, args.K, args.lda, Cfg::BM)) return cudaErrorInvalidValue;
-  if (!make_operand_map<TF32>(&mb, B, B_MN, args.N, args.K, args.ldb, Cfg::BN)) return cudaErrorInvalidValue;
+  const int nb = args.batch > 1 ? args.batch : 1;
+  if (!make_operand_map<TF32>(&ma, A, A_MN, args.M, args.K, args.lda, Cfg::BM, nb, args.sA))
+    return cudaErrorInvalidValue;
+  if (!make_operand_map<TF32>(&mb, B, B_MN, args.N, args.K, args.ldb, Cfg::BN, nb, args.sB))
+    return cudaErrorInvalidValue;
   if (TF32) {
-    if (!make_operand_map<TF32>(&ma2, A2, A_MN, args.M, args.K, args.lda, Cfg::BM)) return cudaErrorInvalidValue;
-    if (!make_operand_map<TF32>(&mb2, B2, B_MN, args.N, args.K, args.ldb, Cfg::BN)) return cudaErrorInvalidValue;
+    if (!make_operand_map<TF32>(&ma2, A2, A_MN, args.M, args.K, args.lda, Cfg::BM, nb, args.sA))
+      return cudaErrorInvalidValue;
+    if (!make_operand_map<TF32>(&mb2, B2, B_MN, args.N, args.K, args.ldb, Cfg::BN, nb, args.sB))
+      return cudaErrorInvalidValue;
   } else {
     ma2 = ma;
     mb2 = mb;
@@ -535,10 +562,11 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   {
     const int tiles = a.tiles_m * a.tiles_n;
     const int nk_all = (args.K + Cfg::BK - 1) / Cfg::BK;
-    if (a.n_extra == 0 && tiles * 2 <= num_sms() && nk_all >= 16) {
+    if (a.n_extra == 0 && nb == 1 && tiles * 2 <= num_sms() && nk_all >= 16) {
       const int sp = std::min(std::min(num_sms() / tiles, nk_all / 8), 16);
       ldw = (a.N + 3) & ~3;
-      if (sp >= 2 && (ws = (float*)library_scratch((size_t)sp * a.M * ldw * sizeof(float), stream)) != nullptr)
+      if (sp >= 2 && (ws = (float*)library_scratch_slot(kScratchSplitK, (size_t)sp * a.M * ldw * sizeof(float), stream)) !=
+              nullptr)
         a.splits = sp;
     }
   }
@@ -557,7 +585,8 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
     a.tma_out = 3;
   } else {
     const int esz = a.c_bf16 ? 2 : 4;
-    const bool aligned = ((uintptr_t)a.C & 15) == 0 && ((long long)a.ldc * esz) % 16 == 0;
+    const bool aligned = ((uintptr_t)a.C & 15) == 0 && ((long long)a.ldc * esz) % 16 == 0 &&
+                         (nb == 1 || (a.sC * esz) % 16 == 0);
     int mode = 0;
     if (a.n_extra == 0 && aligned) {
       if (a.beta == 0.f)
@@ -565,17 +594,10 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
       else if (a.beta == 1.f && !a.c_bf16 && !a.relu)
         mode = 2;
     }
-    if (mode) {
-      auto enc = get_tensor_map_encoder();
-      const cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
-      const cuuint64_t strides[1] = {(cuuint64_t)a.ldc * esz};
-      const cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32};
-      const cuuint32_t estr[2] = {1, 1};
-      if (!enc || enc(&mc, a.c_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.C, dims,
-                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        mode = 0;
-    }
+    if (mode && !encode_3d(&mc, a.C, a.c_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                           (uint64_t)a.N, (uint64_t)a.M, nb, (uint64_t)a.ldc * esz, (uint64_t)a.sC * esz,
+                           128 / esz, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
+      mode = 0;
     a.tma_out = mode;
     if (!mode) mc = ma;  // unused
   }
@@ -586,8 +608,8 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  const int units = a.tiles_m * a.tiles_n * a.splits;
-  const int grid = units < num_sms() ? units : num_sms();
+  const long long units = (long long)a.tiles_m * a.tiles_n * a.splits * nb;
+  const int grid = units < num_sms() ? (int)units : num_sms();
   {
     TimerScope timer(stream);
     kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, mc, a);
@@ -607,7 +629,8 @@ template <bool TF32, bool A_MN, bool B_MN>
 static cudaError_t launch_tc(const GemmArgs& args, const void* A, const void* B, const void* A2, const void* B2,
                              cudaStream_t stream) {
   constexpr int BN_FULL = GemmCfg<TF32>::BN;
-  const long long tiles = (long long)((args.M + 127) / 128) * ((args.N + BN_FULL - 1) / BN_FULL);
+  const long long tiles = (long long)((args.M + 127) / 128) * ((args.N + BN_FULL - 1) / BN_FULL) *
+                          (args.batch > 1 ? args.batch : 1);
   if (tiles * 4 < (long long)num_sms() * 3)
     return launch_tc_bn<TF32, A_MN, B_MN, BN_FULL / 2>(args, A, B, A2, B2, stream);
   return launch_tc_bn<TF32, A_MN, B_MN, BN_FULL>(args, A, B, A2, B2, stream);
@@ -638,31 +661,35 @@ static int kpad4(int K) { return (K + 3) & ~3; }
 
 size_t gemm_f32_scratch_floats(const GemmArgs& a) {
   const size_t kp = (size_t)kpad4(a.K);
-  return 2 * ((size_t)a.M * kp + (size_t)a.N * kp);
+  return 2 * ((size_t)a.M * kp + (size_t)a.N * kp) * (size_t)(a.batch > 1 ? a.batch : 1);
 }
 
 cudaError_t gemm_f32_3xtf32(const GemmArgs& args, const float* A, const float* B, float* scratch,
                             cudaStream_t s) {
   const int kp = kpad4(args.K);
+  const int nb = args.batch > 1 ? args.batch : 1;
+  // Planes [batch][rows][kp], K-major.
   float* a_hi = scratch;
-  float* a_lo = a_hi + (size_t)args.M * kp;
-  float* b_hi = a_lo + (size_t)args.M * kp;
-  float* b_lo = b_hi + (size_t)args.N * kp;
-  const SplitJob ja{A, args.M, args.lda, args.transA, a_hi, a_lo};
-  const SplitJob jb{B, args.N, args.ldb, !args.transB, b_hi, b_lo};
-  dim3 grid((kp + 31) / 32, (std::max(args.M, args.N) + 31) / 32, 2);
+  float* a_lo = a_hi + (size_t)nb * args.M * kp;
+  float* b_hi = a_lo + (size_t)nb * args.M * kp;
+  float* b_lo = b_hi + (size_t)nb * args.N * kp;
+  const SplitJob ja{A, args.M, args.lda, args.transA, a_hi, a_lo, args.sA};
+  const SplitJob jb{B, args.N, args.ldb, !args.transB, b_hi, b_lo, args.sB};
+  dim3 grid((kp + 31) / 32, (std::max(args.M, args.N) + 31) / 32, 2 * nb);
   split_tf32_kernel<<<grid, 256, 0, s>>>(ja, jb, args.K, kp);
   GemmArgs a = args;
   a.K = kp;  // zero-filled tail contributes nothing
   a.lda = kp;
   a.ldb = kp;
+  a.sA = (long long)args.M * kp;
+  a.sB = (long long)args.N * kp;
   a.transA = 0;
   a.transB = 1;
   return launch_tc<true, false, false>(a, a_hi, b_hi, a_lo, b_lo, s);
 }
 
 cudaError_t gemm_simt(const GemmArgs& args, const void* A, const void* B, int bf16_in, cudaStream_t s) {
-  dim3 grid((args.N + 63) / 64, (args.M + 63) / 64);
+  dim3 grid((args.N + 63) / 64, (args.M + 63) / 64, args.batch > 1 ? args.batch : 1);
   if (bf16_in)
     gemm_simt_kernel<uint16_t><<<grid, 256, 0, s>>>((const uint16_t*)A, (const uint16_t*)B, args);
   else

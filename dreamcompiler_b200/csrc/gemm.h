@@ -33,6 +33,11 @@ struct GemmArgs {
   // bias / beta / ReLU epilogue then runs in the reduction kernel).
   int tma_out;
   int splits;  // K slices per output tile (1: no split)
+  // Batched GEMM (dream_bmm): `batch` independent products in one launch,
+  // operand / output b at A + b*sA, B + b*sB, C + b*sC (elements). 0 or 1:
+  // a single product.
+  int batch;
+  long long sA, sB, sC;
 };
 
 // 2-SM bf16 kernel (gemm2.cu) and the algorithm switch.
@@ -48,8 +53,8 @@ __device__ __forceinline__ float gemm_finish(const GemmArgs& a, int n, float acc
   return v;
 }
 
-__device__ __forceinline__ void gemm_store_one(const GemmArgs& a, int m, int n, float acc) {
-  const long long off = (long long)m * a.ldc + n;
+__device__ __forceinline__ void gemm_store_one(const GemmArgs& a, int m, int n, float acc, long long boff = 0) {
+  const long long off = boff + (long long)m * a.ldc + n;
   if (a.c_bf16) {
     __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(a.C) + off;
     const float old = a.beta != 0.f ? __bfloat162float(*c) : 0.f;
@@ -64,10 +69,11 @@ __device__ __forceinline__ void gemm_store_one(const GemmArgs& a, int m, int n, 
 }
 
 // Store 32 consecutive accumulator columns [n0, n0+32) of row m (to C and
-// to every extra destination).
-__device__ __forceinline__ void gemm_store_row32(const GemmArgs& a, int m, int n0, const float* v) {
+// to every extra destination); `boff` = the batch's element offset in C.
+__device__ __forceinline__ void gemm_store_row32(const GemmArgs& a, int m, int n0, const float* v,
+                                                 long long boff = 0) {
   const int nvalid = a.N - n0;
-  const long long off = (long long)m * a.ldc + n0;
+  const long long off = boff + (long long)m * a.ldc + n0;
   if (!a.c_bf16) {
     float* row = reinterpret_cast<float*>(a.C) + off;
     if (nvalid >= 32 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
@@ -128,6 +134,9 @@ __device__ __forceinline__ void gemm_store_row32(const GemmArgs& a, int m, int n
 }
 
 int gemm_tc_supported(const GemmArgs& a, int esz, const void* A, const void* B);
+// Runs a validated GemmArgs on the best kernel for it (api.cu).
+dgx_status gemm_run(const GemmArgs& a, const void* A, const void* B, dgx_dtype ab_type, int f32_mode,
+                    void* workspace, size_t workspace_bytes, cudaStream_t s);
 cudaError_t gemm_bf16_tc(const GemmArgs& args, const void* A, const void* B, cudaStream_t s);
 size_t gemm_f32_scratch_floats(const GemmArgs& a);
 cudaError_t gemm_f32_3xtf32(const GemmArgs& args, const float* A, const float* B, float* scratch,

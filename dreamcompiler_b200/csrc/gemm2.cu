@@ -335,7 +335,7 @@ bool encode_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
 // that the single-CTA 128 x 256 tiles measured faster on this GPU: more tiles
 // for the short main loops).
 bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B) {
-  if (a.transA || a.n_extra) return false;
+  if (a.transA || a.n_extra || a.batch > 1) return false;
   const int esz = a.c_bf16 ? 2 : 4;
   if ((((uintptr_t)a.C | (uintptr_t)A | (uintptr_t)B) & 15) || ((long long)a.ldc * esz) % 16) return false;
   if (((long long)a.lda * 2) % 16 || ((long long)a.ldb * 2) % 16) return false;

@@ -79,6 +79,26 @@ def bmm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float32
     return out
 
 
+def gemm_batched(A: torch.Tensor, B: torch.Tensor, *, transA: bool = False, transB: bool = False,
+                 out: Optional[torch.Tensor] = None, beta: float = 0.0,
+                 out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """C[b] = op(A[b]) . op(B[b]) (+ beta*C[b]) for 3-D tensors whose last dim
+    is contiguous (any batch and row strides); one launch for all batches."""
+    assert A.dim() == 3 and B.dim() == 3 and A.dtype == B.dtype
+    assert A.stride(2) == 1 and B.stride(2) == 1
+    batch = A.shape[0]
+    M, K = (A.shape[2], A.shape[1]) if transA else (A.shape[1], A.shape[2])
+    N = B.shape[1] if transB else B.shape[2]
+    assert B.shape[0] == batch and (B.shape[2] if transB else B.shape[1]) == K
+    if out is None:
+        out = torch.empty(batch, M, N, device=A.device, dtype=out_dtype)
+    assert out.shape == (batch, M, N) and out.stride(2) == 1
+    L.call("dgx_gemm_batched", A.data_ptr(), B.data_ptr(), out.data_ptr(), batch, M, N, K, A.stride(1),
+           B.stride(1), out.stride(1), A.stride(0), B.stride(0), out.stride(0), int(transA), int(transB),
+           _DT[A.dtype], _DT[out.dtype], float(beta), _stream(A))
+    return out
+
+
 def flash_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, causal: bool = True,
               scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
               lse: Optional[torch.Tensor] = None, want_lse: bool = True):

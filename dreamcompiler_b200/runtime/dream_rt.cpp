@@ -318,15 +318,23 @@ Tensor* dream_bmm(Tensor* a_, Tensor* b_, Tensor* batch_t, Tensor* m_t, Tensor* 
   return pub(c);
 }
 
-Tensor* dream_flash_attention(Tensor* Q_, Tensor* K_, Tensor* V_, Tensor* batch_t, Tensor* seq_t, Tensor* dk_t,
-                              Tensor* block_t) {
-  (void)block_t;  // the device tiles are 128 x 128; the result does not depend on the CPU block size
+}  // extern "C"
+
+namespace {
+
+// The three attention ops share one device path: softmax(Q K^T / sqrt(dk)) V
+// per batch row on the FlashAttention kernels (bf16 operands, fp32 softmax),
+// causal for flash_attention / attention_causal, full for attention. The
+// backward recomputes nothing on the host: it runs dgx_flash_bwd from the
+// saved bf16 Q, K, V, O and the LSE.
+Tensor* attention_impl(const char* op, Tensor* Q_, Tensor* K_, Tensor* V_, Tensor* batch_t, Tensor* seq_t,
+                       Tensor* dk_t, int causal) {
   if (!Q_ || !K_ || !V_ || !batch_t || !seq_t || !dk_t) return create_scalar(0.0);
   TensorImpl *Q = impl(Q_), *K = impl(K_), *V = impl(V_);
   const int B = (int)batch_t->data[0], S = (int)seq_t->data[0], dk = (int)dk_t->data[0];
   const long long n = (long long)B * S * dk;
   if (B <= 0 || S <= 0 || dk <= 0 || Q->size < n || K->size < n || V->size < n) {
-    report("flash_attention", "Q/K/V smaller than batch*seq*dk");
+    report(op, "Q/K/V smaller than batch*seq*dk");
     return alloc_tensor(1, 1, 1, 1);
   }
   TensorImpl* out = new_tensor(B, S * dk, 1, 1);
@@ -334,6 +342,7 @@ Tensor* dream_flash_attention(Tensor* Q_, Tensor* K_, Tensor* V_, Tensor* batch_
   out->meta[0] = B;
   out->meta[1] = S;
   out->meta[2] = dk;
+  out->meta[3] = causal;
   if (!ensure_device()) return pub(out);
   FlashSaved* fs = new FlashSaved();
   const size_t bytes = (size_t)n * 2;
@@ -341,16 +350,37 @@ Tensor* dream_flash_attention(Tensor* Q_, Tensor* K_, Tensor* V_, Tensor* batch_
             cudaMalloc(&fs->v, bytes) == cudaSuccess && cudaMalloc(&fs->o, bytes) == cudaSuccess &&
             cudaMalloc(&fs->lse, (size_t)B * S * 4) == cudaSuccess;
   ok = ok && upload(Q, fs->q, DGX_BF16) && upload(K, fs->k, DGX_BF16) && upload(V, fs->v, DGX_BF16) &&
-       dgx_flash_fwd(fs->q, fs->k, fs->v, fs->o, fs->lse, B, S, dk, (float)(1.0 / std::sqrt((double)dk)), 1,
+       dgx_flash_fwd(fs->q, fs->k, fs->v, fs->o, fs->lse, B, S, dk, (float)(1.0 / std::sqrt((double)dk)), causal,
                      DGX_BF16, g_stream) == DGX_OK &&
        download(fs->o, DGX_BF16, out->data, (size_t)n, false);
   if (!ok) {
-    report("flash_attention", dgx_last_error());
+    report(op, dgx_last_error());
     delete fs;
     return pub(out);
   }
   out->flash = fs;
   return pub(out);
+}
+
+}  // namespace
+
+extern "C" {
+
+Tensor* dream_flash_attention(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor* seq_t, Tensor* dk_t,
+                              Tensor* block_t) {
+  (void)block_t;  // the device tiles are 128 x 128; the result does not depend on the CPU block size
+  return attention_impl("flash_attention", Q, K, V, batch_t, seq_t, dk_t, 1);
+}
+
+// dream_attention (runtime/nn/training.inc:177-220): full (non-causal) SDPA.
+Tensor* dream_attention(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor* seq_t, Tensor* dk_t) {
+  return attention_impl("attention", Q, K, V, batch_t, seq_t, dk_t, 0);
+}
+
+// dream_attention_causal (runtime/nn/training.inc:222-263): the materialised
+// causal SDPA; the same function as flash_attention.
+Tensor* dream_attention_causal(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor* seq_t, Tensor* dk_t) {
+  return attention_impl("attention_causal", Q, K, V, batch_t, seq_t, dk_t, 1);
 }
 
 Tensor* dream_tp_matmul_column(Tensor* X_, Tensor* W_, Tensor* gpus_t) {
@@ -493,13 +523,12 @@ bool bwd_bmm(TensorImpl* t) {
   if (!dA.p || !dB.p || !dY.p || !gA.p || !gB.p || !upload(a, dA.p, ab) || !upload(b, dB.p, ab) ||
       !upload(&g, dY.p, ab))
     return false;
-  for (int i = 0; i < B; ++i) {
-    if (!device_gemm(dY.as<char>() + (size_t)i * M * N * es, dB.as<char>() + (size_t)i * K * N * es,
-                     gA.as<float>() + (size_t)i * M * K, M, K, N, 0, 1, ab, nullptr, DGX_EPI_NONE, 0.f) ||
-        !device_gemm(dA.as<char>() + (size_t)i * M * K * es, dY.as<char>() + (size_t)i * M * N * es,
-                     gB.as<float>() + (size_t)i * K * N, K, N, M, 1, 0, ab, nullptr, DGX_EPI_NONE, 0.f))
-      return false;
-  }
+  // One batched launch each: dA_b = dC_b . B_b^T, dB_b = A_b^T . dC_b.
+  if (dgx_gemm_batched(dY.p, dB.p, gA.p, B, M, K, N, N, N, K, (long long)M * N, (long long)K * N, (long long)M * K,
+                       0, 1, ab, DGX_F32, 0.f, g_stream) != DGX_OK ||
+      dgx_gemm_batched(dA.p, dY.p, gB.p, B, K, N, M, K, N, N, (long long)M * K, (long long)M * N, (long long)K * N,
+                       1, 0, ab, DGX_F32, 0.f, g_stream) != DGX_OK)
+    return false;
   return download(gA.p, DGX_F32, a->grad, (size_t)B * M * K, true) &&
          download(gB.p, DGX_F32, b->grad, (size_t)B * K * N, true);
 }
@@ -515,7 +544,7 @@ bool bwd_flash(TensorImpl* t) {
   g.size = (int)n;
   if (!ddO.p || !dQ.p || !dK.p || !dV.p || !upload(&g, ddO.p, DGX_BF16)) return false;
   if (dgx_flash_bwd(fs->q, fs->k, fs->v, fs->o, ddO.p, fs->lse, dQ.p, dK.p, dV.p, B, S, dk,
-                    (float)(1.0 / std::sqrt((double)dk)), 1, DGX_BF16, nullptr, 0, g_stream) != DGX_OK)
+                    (float)(1.0 / std::sqrt((double)dk)), t->meta[3], DGX_BF16, nullptr, 0, g_stream) != DGX_OK)
     return false;
   return download(dQ.p, DGX_BF16, t->parents[0]->grad, n, true) &&
          download(dK.p, DGX_BF16, t->parents[1]->grad, n, true) &&

@@ -99,11 +99,26 @@ size_t dgx_gemm_workspace_size(int M, int N, int K, int transA, int transB, dgx_
 dgx_status dgx_gemm_set_algo(int algo);
 
 /*
- * Batched GEMM C_b = A_b . B_b over `batch` contiguous [M,K] x [K,N] blocks.
- * Replaces dream_bmm (runtime/ops/elementwise.inc:1218-1252).
+ * Batched GEMM C_b = A_b . B_b over `batch` contiguous [M,K] x [K,N] blocks,
+ * all batches in one kernel launch. Replaces dream_bmm
+ * (runtime/ops/elementwise.inc:1218-1252).
  */
 dgx_status dgx_bmm(const void* A, const void* B, void* C, int batch, int M, int N, int K, dgx_dtype ab_type,
                    dgx_dtype c_type, void* stream);
+
+/*
+ * Strided batched GEMM: for b < batch,
+ *   C_b = op(A_b) . op(B_b) (+ beta*C_b),  X_b = X + b*strideX (elements),
+ * op and leading dimensions as in dgx_gemm (no bias epilogue; f32 inputs run
+ * 3xTF32 with library scratch). strideA / strideB may be 0 (one operand
+ * shared by every batch); output batches may not overlap (strideC >= M*ldc).
+ * One launch for all batches; this is what the "bmm" backward
+ * (runtime/ops/autograd.inc:549-574) needs: dA_b = dC_b . B_b^T (transB) and
+ * dB_b = A_b^T . dC_b (transA).
+ */
+dgx_status dgx_gemm_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K, int lda,
+                            int ldb, int ldc, long long strideA, long long strideB, long long strideC, int transA,
+                            int transB, dgx_dtype ab_type, dgx_dtype c_type, float beta, void* stream);
 
 /*
  * FlashAttention forward. Q, K, V, O: [BH][S][D] (heads folded into the batch,

@@ -52,6 +52,10 @@ Tensor* dream_linear_relu(Tensor* x, Tensor* W, Tensor* b);        /* elementwis
 Tensor* dream_bmm(Tensor* a, Tensor* b, Tensor* batch_t, Tensor* m_t, Tensor* k_t, Tensor* n_t); /* :1218 */
 Tensor* dream_flash_attention(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor* seq_t, Tensor* dk_t,
                               Tensor* block_t);                    /* training.inc:284 */
+Tensor* dream_attention(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor* seq_t,
+                        Tensor* dk_t);                             /* training.inc:177 */
+Tensor* dream_attention_causal(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor* seq_t,
+                               Tensor* dk_t);                      /* training.inc:222 */
 Tensor* dream_tp_matmul_column(Tensor* X, Tensor* W, Tensor* gpus_t); /* training.inc:1604 */
 
 /* the two ops programs use to seed a gradient: backward(sum(Y * G)) */

@@ -130,6 +130,22 @@ void orc_matmul_bwd(const double* A, const double* B, const double* dY, double* 
   }
 }
 
+// dream_bmm (runtime/ops/elementwise.inc:1218-1252): per batch b,
+// C_b[M,N] = A_b[M,K].B_b[K,N] in double, operands flat (batch, M*K) etc.
+void orc_bmm_f64(const double* A, const double* B, double* C, int batch, int M, int K, int N) {
+  for (int b = 0; b < batch; ++b)
+    orc_gemm_f64(A + (size_t)b * M * K, B + (size_t)b * K * N, C + (size_t)b * M * N, M, K, N);
+}
+
+// "bmm" backward (runtime/ops/autograd.inc:549-574): per batch, the "matmul"
+// backward accumulated into dA_b, dB_b.
+void orc_bmm_bwd(const double* A, const double* B, const double* dC, double* dA, double* dB, int batch, int M,
+                 int K, int N) {
+  for (int b = 0; b < batch; ++b)
+    orc_matmul_bwd(A + (size_t)b * M * K, B + (size_t)b * K * N, dC + (size_t)b * M * N, dA + (size_t)b * M * K,
+                   dB + (size_t)b * K * N, M, K, N);
+}
+
 // dream_linear / dream_linear_relu (runtime/ops/elementwise.inc:1432-1521):
 // Y[i,j] = b[j] + sum_k X[i,k]*W[j,k]  (W stored out x in), then ReLU.
 void orc_linear(const double* X, const double* W, const double* b, double* Y, int N, int in_dim, int out_dim,
@@ -319,6 +335,60 @@ void orc_attention(const double* Q, const double* K, const double* V, double* O,
         Ob[(size_t)i * dk + k] = s;
       }
     }
+  }
+}
+
+// Backward of the materialised SDPA ("attention" and "attention_causal"
+// branches, runtime/ops/autograd.inc:675-778): recompute A = softmax(QK^T*sc)
+// (masked to j <= i when causal), then dV += A^T dO, dA = dO V^T,
+// dS = A o (dA - rowsum(dA o A)), dQ += dS K sc, dK += dS^T Q sc.
+void orc_attention_bwd(const double* Q, const double* K, const double* V, const double* dO, double* dQ, double* dK,
+                       double* dV, int B, int S, int dk, int causal) {
+  const double scale = 1.0 / std::sqrt((double)dk);
+#pragma omp parallel for schedule(dynamic)
+  for (int b = 0; b < B; ++b) {
+    const size_t o = (size_t)b * S * dk;
+    const double *Qb = Q + o, *Kb = K + o, *Vb = V + o, *dOb = dO + o;
+    double *dQb = dQ + o, *dKb = dK + o, *dVb = dV + o;
+    std::vector<double> A((size_t)S * S, 0.0), dS((size_t)S * S, 0.0);
+    for (int i = 0; i < S; ++i) {
+      const int jmax = causal ? i : S - 1;
+      double mx = -1e300;
+      for (int j = 0; j <= jmax; ++j) {
+        double s = 0;
+        for (int k = 0; k < dk; ++k) s += Qb[(size_t)i * dk + k] * Kb[(size_t)j * dk + k];
+        A[(size_t)i * S + j] = s * scale;
+        mx = std::max(mx, A[(size_t)i * S + j]);
+      }
+      double sum = 0;
+      for (int j = 0; j <= jmax; ++j) sum += (A[(size_t)i * S + j] = std::exp(A[(size_t)i * S + j] - mx));
+      for (int j = 0; j <= jmax; ++j) A[(size_t)i * S + j] /= sum;
+      // dA_ij = dO_i . V_j and the row term sum_j dA_ij A_ij
+      double rd = 0;
+      for (int j = 0; j <= jmax; ++j) {
+        double s = 0;
+        for (int k = 0; k < dk; ++k) s += dOb[(size_t)i * dk + k] * Vb[(size_t)j * dk + k];
+        dS[(size_t)i * S + j] = s;
+        rd += s * A[(size_t)i * S + j];
+      }
+      for (int j = 0; j <= jmax; ++j) dS[(size_t)i * S + j] = A[(size_t)i * S + j] * (dS[(size_t)i * S + j] - rd);
+    }
+    for (int j = 0; j < S; ++j)
+      for (int k = 0; k < dk; ++k) {
+        double sv = 0, sk = 0;
+        for (int i = 0; i < S; ++i) {
+          sv += A[(size_t)i * S + j] * dOb[(size_t)i * dk + k];
+          sk += dS[(size_t)i * S + j] * Qb[(size_t)i * dk + k];
+        }
+        dVb[(size_t)j * dk + k] += sv;
+        dKb[(size_t)j * dk + k] += sk * scale;
+      }
+    for (int i = 0; i < S; ++i)
+      for (int k = 0; k < dk; ++k) {
+        double s = 0;
+        for (int j = 0; j < S; ++j) s += dS[(size_t)i * S + j] * Kb[(size_t)j * dk + k];
+        dQb[(size_t)i * dk + k] += s * scale;
+      }
   }
 }
 

@@ -121,6 +121,25 @@ def matmul_bwd(A, B, dY, dA=None, dB=None):
     return dA, dB
 
 
+def bmm(A, B):
+    """A [batch, M, K], B [batch, K, N] float64 -> C [batch, M, N] (dream_bmm)."""
+    A, B = (np.ascontiguousarray(t, np.float64) for t in (A, B))
+    nb, M, K = A.shape
+    N = B.shape[2]
+    C_ = np.empty((nb, M, N))
+    lib().orc_bmm_f64(_p(A), _p(B), _p(C_), nb, M, K, N)
+    return C_
+
+
+def bmm_bwd(A, B, dC):
+    A, B, dC = (np.ascontiguousarray(t, np.float64) for t in (A, B, dC))
+    nb, M, K = A.shape
+    N = B.shape[2]
+    dA, dB = np.zeros_like(A), np.zeros_like(B)
+    lib().orc_bmm_bwd(_p(A), _p(B), _p(dC), _p(dA), _p(dB), nb, M, K, N)
+    return dA, dB
+
+
 def linear(X, W, b, relu=False):
     X, W = (np.ascontiguousarray(t, np.float64) for t in (X, W))
     b = None if b is None else np.ascontiguousarray(b, np.float64)
@@ -165,6 +184,14 @@ def attention(Q, K, V, causal=True):
     O = np.empty_like(Q)
     lib().orc_attention(_p(Q), _p(K), _p(V), _p(O), B, S, dk, int(causal))
     return O
+
+
+def attention_bwd(Q, K, V, dO, causal=True):
+    Q, K, V, dO = (np.ascontiguousarray(t, np.float64) for t in (Q, K, V, dO))
+    B, S, dk = Q.shape
+    dQ, dK, dV = np.zeros_like(Q), np.zeros_like(K), np.zeros_like(V)
+    lib().orc_attention_bwd(_p(Q), _p(K), _p(V), _p(dO), _p(dQ), _p(dK), _p(dV), B, S, dk, int(causal))
+    return dQ, dK, dV
 
 
 # ---------------------------------------------------------------- int8

@@ -19,8 +19,12 @@ output comes from the reference's own ops:
              dream_flash_attention, gelu, log_softmax + nll_loss, backward;
              parameters from a seeded numpy generator (oracle/gpt_oracle.py)
   adamw.npz  dream_adamw_update applied twice to one parameter
+  bmm.npz    dream_bmm + its "bmm" backward (runtime/ops/elementwise.inc:1218-1252,
+             runtime/ops/autograd.inc:549-574)
+  attn.npz   dream_attention and dream_attention_causal + their backward
+             (runtime/nn/training.inc:177-263, runtime/ops/autograd.inc:675-778)
 
-Usage:  python tests/golden/make_golden.py
+Usage:  python tests/golden/make_golden.py [fixture ...]
 """
 from __future__ import annotations
 
@@ -213,13 +217,47 @@ def gen_adamw():
     np.savez_compressed(os.path.join(HERE, "adamw.npz"), **out)
 
 
+# (batch, M, K, N) and (B, S, dk); stored as float32 to keep the fixtures small
+BMM_CFGS = [(1, 1, 1, 1), (3, 5, 7, 9), (4, 33, 17, 65), (2, 64, 32, 48), (3, 130, 16, 24)]
+ATTN_CFGS = [(2, 64, 16), (1, 100, 24), (1, 160, 32)]
+
+
+def gen_bmm():
+    out = {}
+    R.set_seed(7)
+    for (B, M, K, N) in BMM_CFGS:
+        A, Bm = R.randn(B, M * K), R.randn(B, K * N)
+        C = R.call("dream_bmm", A, Bm, *(R.scalar(v) for v in (B, M, K, N)))
+        G = seeded_backward(C, (B, M * N))
+        t = f"{B}_{M}_{K}_{N}"
+        out[f"A_{t}"], out[f"B_{t}"], out[f"G_{t}"] = R.data(A), R.data(Bm), G
+        out[f"C_{t}"], out[f"dA_{t}"], out[f"dB_{t}"] = R.data(C), R.grad(A), R.grad(Bm)
+    np.savez_compressed(os.path.join(HERE, "bmm.npz"), **{k: v.astype(np.float32) for k, v in out.items()})
+
+
+def gen_attn():
+    out = {}
+    R.set_seed(31)
+    for causal in (0, 1):
+        for (B, S, dk) in ATTN_CFGS:
+            Q, K, V = R.randn(B, S * dk), R.randn(B, S * dk), R.randn(B, S * dk)
+            O = R.call("dream_attention_causal" if causal else "dream_attention", Q, K, V,
+                       *(R.scalar(v) for v in (B, S, dk)))
+            G = seeded_backward(O, (B, S * dk))
+            t = f"{causal}_{B}_{S}_{dk}"
+            out[f"G_{t}"], out[f"O_{t}"] = G.reshape(B, S, dk), R.data(O).reshape(B, S, dk)
+            for name, x in (("Q", Q), ("K", K), ("V", V)):
+                out[f"{name}_{t}"] = R.data(x).reshape(B, S, dk)
+                out[f"d{name}_{t}"] = R.grad(x).reshape(B, S, dk)
+    np.savez_compressed(os.path.join(HERE, "attn.npz"), **{k: v.astype(np.float32) for k, v in out.items()})
+
+
 if __name__ == "__main__":
-    gen_gemm()
-    gen_flash()
-    gen_linear()
-    gen_tp()
-    gen_gpt()
-    gen_adamw()
+    # optional arguments name the fixtures to regenerate (default: all)
+    gens = {"gemm": gen_gemm, "flash": gen_flash, "linear": gen_linear, "tp": gen_tp, "gpt": gen_gpt,
+            "adamw": gen_adamw, "bmm": gen_bmm, "attn": gen_attn}
+    for name in sys.argv[1:] or list(gens):
+        gens[name]()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

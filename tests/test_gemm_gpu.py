@@ -246,3 +246,89 @@ def test_two_sm_and_single_cta_kernels_agree(dgx, algo, shape, tB, cdt, beta, bi
     if relu:
         ref = ref.clamp_min(0)
     assert normwise(C.double().cpu().numpy(), ref.cpu().numpy()) < (1e-5 if cdt == "f32" else 1e-2)
+
+
+BMM_CFGS = [(1, 1, 1, 1), (3, 5, 7, 9), (4, 33, 17, 65), (2, 64, 32, 48), (3, 130, 16, 24)]
+
+
+@pytest.mark.parametrize("cfg", BMM_CFGS)
+def test_bmm_golden(dgx, orc, golden, cfg):
+    """dream_bmm's own outputs and "bmm" backward (reference runtime) through
+    dgx_bmm / dgx_gemm_batched: f32 (3xTF32) and bf16 operands."""
+    g = golden("bmm")
+    B, M, K, N = cfg
+    t = f"{B}_{M}_{K}_{N}"
+    A, Bm, G = (g[f"{n}_{t}"].reshape(s) for n, s in (("A", (B, M, K)), ("B", (B, K, N)), ("G", (B, M, N))))
+    Ad, Bd, Gd = cuda(A), cuda(Bm), cuda(G)
+    C = dgx.bmm(Ad, Bd)
+    dA = dgx.gemm_batched(Gd, Bd, transB=True)
+    dB = dgx.gemm_batched(Ad, Gd, transA=True)
+    dgx.sync_check()
+    assert normwise(C.cpu().numpy(), g[f"C_{t}"].reshape(B, M, N)) < F32_TOL
+    assert normwise(dA.cpu().numpy(), g[f"dA_{t}"].reshape(B, M, K)) < F32_TOL
+    assert normwise(dB.cpu().numpy(), g[f"dB_{t}"].reshape(B, K, N)) < F32_TOL
+    Cb = dgx.bmm(Ad.bfloat16(), Bd.bfloat16())
+    dgx.sync_check()
+    assert normwise(Cb.cpu().numpy(), orc.bmm(bf16_round(A), bf16_round(Bm))) < BF16_TOL
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("batch,M,N,K,ta,tb", [(5, 200, 136, 72, 0, 0), (3, 130, 264, 520, 1, 0),
+                                               (7, 96, 40, 1100, 0, 1), (2, 257, 300, 64, 1, 1),
+                                               (4, 33, 65, 17, 0, 0), (9, 128, 128, 128, 0, 0)])
+def test_gemm_batched_shapes(dgx, orc, dtype, batch, M, N, K, ta, tb):
+    """One launch over all batches: ragged tiles at every batch boundary,
+    transposed operands, beta=1 accumulation; K=17 (bf16) takes the SIMT
+    path. Each batch against the f64 oracle."""
+    rng = np.random.default_rng(batch * 1000 + M + N + K)
+    A = rng.standard_normal((batch, K, M) if ta else (batch, M, K))
+    B = rng.standard_normal((batch, N, K) if tb else (batch, K, N))
+    C0 = rng.standard_normal((batch, M, N))
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    Ad, Bd = cuda(A, tdt), cuda(B, tdt)
+    out = cuda(C0)
+    dgx.gemm_batched(Ad, Bd, transA=bool(ta), transB=bool(tb), out=out, beta=1.0)
+    dgx.sync_check()
+    Ar, Br = (x if dtype == "f32" else bf16_round(x) for x in (A, B))
+    if ta:
+        Ar = Ar.transpose(0, 2, 1)
+    if tb:
+        Br = Br.transpose(0, 2, 1)
+    ref = orc.bmm(Ar, Br) + C0
+    tol = F32_TOL if dtype == "f32" else BF16_TOL
+    got = out.cpu().numpy()
+    for b in range(batch):
+        assert normwise(got[b], ref[b]) < tol, b
+
+
+def test_bmm_many_batches_and_strided_views(dgx, orc):
+    """More batches than one launch's grid z extent (33000 > 32767: two
+    launches), and batch / row strides that are not the dense ones (views
+    into wider buffers)."""
+    rng = np.random.default_rng(5)
+    A, B = rng.standard_normal((33000, 2, 4)), rng.standard_normal((33000, 4, 8))
+    C = dgx.bmm(cuda(A), cuda(B))
+    dgx.sync_check()
+    assert normwise(C.cpu().numpy(), np.einsum("bmk,bkn->bmn", A, B)) < F32_TOL
+    big = torch.randn(6, 80, 96, device="cuda").bfloat16()
+    Bw = torch.randn(6, 64, 72, device="cuda").bfloat16()
+    Av, Bv = big[:, 8:72, 16:80], Bw[:, :, :40]  # [6, 64, 64] x [6, 64, 40], padded pitches
+    out = torch.zeros(6, 64, 48, device="cuda")[:, :, :40]
+    dgx.gemm_batched(Av, Bv, out=out)
+    dgx.sync_check()
+    ref = np.einsum("bmk,bkn->bmn", Av.double().cpu().numpy(), Bv.double().cpu().numpy())
+    assert normwise(out.cpu().numpy(), ref) < BF16_TOL
+
+
+def test_bmm_broadcast_operand_and_overlap_rejected(dgx):
+    """Batch stride 0 shares one operand across batches; overlapping output
+    batches are rejected with DGX_EINVAL."""
+    W = torch.randn(1, 48, 40, device="cuda")
+    X = torch.randn(5, 24, 48, device="cuda")
+    out = dgx.gemm_batched(X, W.expand(5, 48, 40))
+    dgx.sync_check()
+    ref = np.einsum("bmk,kn->bmn", X.double().cpu().numpy(), W[0].double().cpu().numpy())
+    assert normwise(out.cpu().numpy(), ref) < F32_TOL
+    A = torch.zeros(2, 4, 4, device="cuda")
+    with pytest.raises(dgx.DgxError):
+        dgx.gemm_batched(A, A, out=torch.zeros(1, 4, 4, device="cuda").expand(2, 4, 4))

@@ -171,3 +171,36 @@ def test_gemm_rows_sampling(orc):
     A, B = rng.standard_normal((50, 30)), rng.standard_normal((30, 20))
     rows = np.array([0, 7, 49, 13], np.int32)
     assert normwise(orc.gemm_rows_f64(A, B, rows), (A @ B)[rows]) < 1e-14
+
+
+BMM_CFGS = [(1, 1, 1, 1), (3, 5, 7, 9), (4, 33, 17, 65), (2, 64, 32, 48), (3, 130, 16, 24)]
+ATTN_CFGS = [(2, 64, 16), (1, 100, 24), (1, 160, 32)]
+F32_STORED = 1e-6  # the bmm / attn fixtures are stored as float32
+
+
+@pytest.mark.parametrize("cfg", BMM_CFGS)
+def test_bmm_and_backward(orc, golden, cfg):
+    """dream_bmm and its "bmm" backward (reference runtime outputs)."""
+    g = golden("bmm")
+    B, M, K, N = cfg
+    t = f"{B}_{M}_{K}_{N}"
+    A, Bm, G = g[f"A_{t}"].reshape(B, M, K), g[f"B_{t}"].reshape(B, K, N), g[f"G_{t}"].reshape(B, M, N)
+    assert normwise(orc.bmm(A, Bm), g[f"C_{t}"].reshape(B, M, N)) < F32_STORED
+    dA, dB = orc.bmm_bwd(A, Bm, G)
+    assert normwise(dA, g[f"dA_{t}"].reshape(B, M, K)) < F32_STORED
+    assert normwise(dB, g[f"dB_{t}"].reshape(B, K, N)) < F32_STORED
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+@pytest.mark.parametrize("cfg", ATTN_CFGS)
+def test_attention_and_backward(orc, golden, cfg, causal):
+    """dream_attention / dream_attention_causal and their backward."""
+    g = golden("attn")
+    t = f"{causal}_{cfg[0]}_{cfg[1]}_{cfg[2]}"
+    Q, K, V, G = (g[f"{n}_{t}"] for n in ("Q", "K", "V", "G"))
+    assert normwise(orc.attention(Q, K, V, causal=bool(causal)), g[f"O_{t}"]) < F32_STORED
+    dQ, dK, dV = orc.attention_bwd(Q, K, V, G, causal=bool(causal))
+    for name, x in (("dQ", dQ), ("dK", dK), ("dV", dV)):
+        assert normwise(x, g[f"{name}_{t}"]) < F32_STORED, name
+    if causal:  # the causal backward equals the flash backward
+        assert normwise(orc.flash_bwd(Q, K, V, G)[0], dQ) < 1e-9

@@ -95,3 +95,38 @@ def test_f32_precision_path(R):
     R.call("dream_set_precision", a, 1)
     c = R.call("tensor_matmul", a, a)
     assert R.data(R.call("sum", c))[0, 0] == 8.0
+
+
+def test_bmm_program_matches_reference(R, golden):
+    """set_seed(7); per config A, B = randn; C = bmm(A, B, batch, M, K, N);
+    backward(sum(C * randn)) — one batched launch each for C, dA and dB."""
+    g = golden("bmm")
+    R.call("dream_set_seed", R.scalar(7))
+    for (B, M, K, N) in [(1, 1, 1, 1), (3, 5, 7, 9), (4, 33, 17, 65), (2, 64, 32, 48), (3, 130, 16, 24)]:
+        t = f"{B}_{M}_{K}_{N}"
+        A = R.call("dream_randn", R.scalar(B), R.scalar(M * K))
+        Bm = R.call("dream_randn", R.scalar(B), R.scalar(K * N))
+        assert normwise(R.data(A), g[f"A_{t}"]) < 1e-7  # fixture stored as float32
+        C = R.call("dream_bmm", A, Bm, *(R.scalar(v) for v in (B, M, K, N)))
+        seeded_backward(R, C, (B, M * N))
+        assert normwise(R.data(C), g[f"C_{t}"]) < 1e-4
+        assert normwise(R.grad(A), g[f"dA_{t}"]) < 1e-4
+        assert normwise(R.grad(Bm), g[f"dB_{t}"]) < 1e-4
+
+
+def test_attention_programs_match_reference(R, golden):
+    """dream_attention (full) and dream_attention_causal on the FlashAttention
+    kernels against the reference's materialised SDPA and its backward."""
+    g = golden("attn")
+    R.call("dream_set_seed", R.scalar(31))
+    for causal in (0, 1):
+        for (B, S, dk) in [(2, 64, 16), (1, 100, 24), (1, 160, 32)]:
+            t = f"{causal}_{B}_{S}_{dk}"
+            Q, K, V = (R.call("dream_randn", R.scalar(B), R.scalar(S * dk)) for _ in range(3))
+            O = R.call("dream_attention_causal" if causal else "dream_attention", Q, K, V,
+                       *(R.scalar(v) for v in (B, S, dk)))
+            seeded_backward(R, O, (B, S * dk))
+            shape = (B, S, dk)
+            assert normwise(R.data(O, shape), g[f"O_{t}"]) < 2e-2, t
+            for name, x in (("dQ", Q), ("dK", K), ("dV", V)):
+                assert normwise(R.grad(x, shape), g[f"{name}_{t}"]) < 2e-2, (t, name)
