@@ -5,8 +5,10 @@
 // accumulator), restated for tensor cores. Layout [BH][S][D] bf16, heads
 // folded into the batch as in the reference's `(B, S*dk)` tensors.
 //
-// One CTA owns 256 query rows as two 128-row tiles (A, B) that share every
-// K/V tile load. Warps 0-3 run tile A's softmax, warps 4-7 tile B's, warp 8
+// A persistent grid (one CTA per SM) walks work items of 256 query rows,
+// the heaviest (latest causal) blocks first; Q of the next item loads into a
+// second buffer while the current one runs. An item is two 128-row tiles
+// (A, B) that share every K/V tile load. Warps 0-3 run tile A's softmax, warps 4-7 tile B's, warp 8
 // issues TMA loads, warp 9 issues tcgen05.mma. TMEM holds S_A, S_B (128 fp32
 // columns each), O_A, O_B (D fp32 columns each) and P_A, P_B (128 bf16 = 64
 // columns each, the A operand of the P.V MMA read straight from TMEM). A
@@ -61,8 +63,8 @@ constexpr uint32_t REG_SOFTMAX = 224, REG_CTRL = 56;
 constexpr float RESCALE_LOG2 = 8.0f;
 
 // shared memory map (offsets from a 1024-aligned base)
-constexpr int SM_Q = 0;                               // Q_A, Q_B
-constexpr int SM_K = SM_Q + 2 * TILE_BYTES;           // K stages
+constexpr int SM_Q = 0;                               // Q_A, Q_B (two buffers: next item's Q)
+constexpr int SM_K = SM_Q + 4 * TILE_BYTES;           // K stages
 constexpr int SM_V = SM_K + KV_STAGES * TILE_BYTES;   // V stages
 constexpr int SM_BAR = SM_V + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
@@ -78,11 +80,35 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 struct FwdBars {
-  uint64_t q_full, k_full[KV_STAGES], v_full[KV_STAGES], kv_empty[KV_STAGES];
+  uint64_t q_full[2], q_empty[2], k_full[KV_STAGES], v_full[KV_STAGES], kv_empty[KV_STAGES];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], turn[2];
   uint32_t tmem_slot;
   int abort;
 };
+
+// Work item w (heavy = late query blocks first under causal): its two 128-row
+// Q tiles, head, and how many K/V tiles each tile sees.
+struct FwdItem {
+  int q0, bh, nA, nB;
+};
+__device__ __forceinline__ FwdItem fwd_item(const FlashFwdArgs& a, int w) {
+  FwdItem I;
+  const int nqb = (a.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M);
+  const int qb = a.causal ? (nqb - 1 - w / a.BH) : (w / a.BH);
+  I.bh = w % a.BH;
+  I.q0 = qb * 2 * BLOCK_M;
+  const int nkv = (a.S + BLOCK_N - 1) / BLOCK_N;
+  int nt[2];
+  for (int x = 0; x < 2; ++x) {
+    const int qs = I.q0 + x * BLOCK_M;
+    const int qe = min(qs + BLOCK_M, a.S);  // exclusive
+    nt[x] = a.causal ? min((qe + BLOCK_N - 1) / BLOCK_N, nkv) : nkv;
+  }
+  if (I.q0 + BLOCK_M >= a.S) nt[1] = nt[0];  // tile B has no valid rows: shadow A
+  I.nA = nt[0];
+  I.nB = nt[1];
+  return I;
+}
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -92,24 +118,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + SM_BAR);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WaitCtx wc{&bars->abort, args.err};
-
-  // Heavy (late) query blocks first: block id -> (query block, head).
-  const int nqb = (args.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M);
-  const int qb = args.causal ? (nqb - 1 - (int)(blockIdx.x / args.BH)) : (int)(blockIdx.x / args.BH);
-  const int bh = blockIdx.x % args.BH;
-  const int q0 = qb * 2 * BLOCK_M;
-  const int nkv = (args.S + BLOCK_N - 1) / BLOCK_N;
-  int ntile[2];
-  for (int x = 0; x < 2; ++x) {
-    const int qs = q0 + x * BLOCK_M;
-    const int qe = min(qs + BLOCK_M, args.S);  // exclusive
-    ntile[x] = args.causal ? min((qe + BLOCK_N - 1) / BLOCK_N, nkv) : nkv;
-  }
-  if (q0 + BLOCK_M >= args.S) ntile[1] = ntile[0];  // tile B has no valid rows: shadow A
-  const int nA = ntile[0], nB = ntile[1];
+  // Persistent: this CTA walks items blockIdx.x, +gridDim.x, ...; every
+  // barrier phase counts on across items.
+  const int nitems = ((args.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M)) * args.BH;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->q_full[b], 1);
+      mbar_init(&bars->q_empty[b], 1);
+    }
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
@@ -133,7 +150,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
-  const int row_base = bh * args.S;  // row of the [BH*S, D] view
 
   // Each role's setmaxnreg sits inside its branch so that it dominates (and
   // sets the register limit for) exactly that role's code.
@@ -145,20 +161,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
-      tma_load_3d(smem + SM_Q, &tmQ, &bars->q_full, 0, q0, bh);
-      tma_load_3d(smem + SM_Q + TILE_BYTES, &tmQ, &bars->q_full, 0, q0 + BLOCK_M, bh);
-      int j = 0;
-      for (; j < nB; ++j) {
-        const int s = j % KV_STAGES;
-        if (!mbar_wait(&bars->kv_empty[s], ((j / KV_STAGES) & 1) ^ 1, wc)) break;
-        mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
-        tma_load_3d(smem + SM_K + s * TILE_BYTES, &tmK, &bars->k_full[s], 0, j * BLOCK_N, bh);
-        mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
-        tma_load_3d(smem + SM_V + s * TILE_BYTES, &tmV, &bars->v_full[s], 0, j * BLOCK_N, bh);
+      uint32_t gkv = 0, ic = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+        const FwdItem I = fwd_item(args, w);
+        const int qb2 = ic & 1;
+        if (!(ok = mbar_wait(&bars->q_empty[qb2], ((ic >> 1) & 1) ^ 1, wc))) break;
+        mbar_arrive_expect_tx(&bars->q_full[qb2], 2 * TILE_BYTES);
+        uint8_t* sq = smem + SM_Q + qb2 * 2 * TILE_BYTES;
+        tma_load_3d(sq, &tmQ, &bars->q_full[qb2], 0, I.q0, I.bh);
+        tma_load_3d(sq + TILE_BYTES, &tmQ, &bars->q_full[qb2], 0, I.q0 + BLOCK_M, I.bh);
+        ++ic;  // counted as issued before any later wait can fail
+        for (int j = 0; j < I.nB; ++j, ++gkv) {
+          const int s = gkv % KV_STAGES;
+          if (!(ok = mbar_wait(&bars->kv_empty[s], ((gkv / KV_STAGES) & 1) ^ 1, wc))) break;
+          mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
+          tma_load_3d(smem + SM_K + s * TILE_BYTES, &tmK, &bars->k_full[s], 0, j * BLOCK_N, I.bh);
+          mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
+          tma_load_3d(smem + SM_V + s * TILE_BYTES, &tmV, &bars->v_full[s], 0, j * BLOCK_N, I.bh);
+        }
       }
-      mbar_drain(&bars->q_full, 0);
-      for (int f = max(0, j - KV_STAGES); f < j; ++f) {
+      // Teardown: every copy issued must have landed before the CTA leaves.
+      for (uint32_t f = ic > 2 ? ic - 2 : 0; f < ic; ++f) mbar_drain(&bars->q_full[f & 1], (f >> 1) & 1);
+      for (uint32_t f = gkv > KV_STAGES ? gkv - KV_STAGES : 0; f < gkv; ++f) {
         mbar_drain(&bars->k_full[f % KV_STAGES], (f / KV_STAGES) & 1);
         mbar_drain(&bars->v_full[f % KV_STAGES], (f / KV_STAGES) & 1);
       }
@@ -168,58 +193,79 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (elect_one_lane()) {
       constexpr uint32_t idesc_s = make_idesc(1, 0, 0, BLOCK_M, BLOCK_N);  // Q.K^T, both K-major
       constexpr uint32_t idesc_o = make_idesc(1, 0, 1, BLOCK_M, DP);       // P (TMEM) . V (MN-major)
-      const uint32_t sq = smem_u32(smem + SM_Q), sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V);
+      const uint32_t sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V);
+      // issued S / PV per softmax group, over all items
+      uint32_t ns[2] = {0, 0}, np[2] = {0, 0};
+      uint32_t gkv = 0, ic = 0;
+      bool ok = true;
       // Descriptors advance by adding (byte offset >> 4) to the start field.
-      auto issue_s = [&](int x, int j) {
+      auto issue_s = [&](uint32_t sq, int x, uint32_t kvi) {
         const uint64_t dq = sw128_desc(sq + x * TILE_BYTES, 16, 1024);
-        const uint64_t dk = sw128_desc(sk + (j % KV_STAGES) * TILE_BYTES, 16, 1024);
+        const uint64_t dk = sw128_desc(sk + (kvi % KV_STAGES) * TILE_BYTES, 16, 1024);
         const uint32_t d = tmem + (x ? T_S1 : T_S0);
 #pragma unroll 1
         for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(d, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
         tc_commit(&bars->s_full[x]);
+        ++ns[x];
       };
-      auto issue_pv = [&](int x, int j) {
-        const uint64_t dv = sw128_desc(sv + (j % KV_STAGES) * TILE_BYTES, DP * 128, 1024);
+      auto issue_pv = [&](int x, uint32_t kvi, bool first) {
+        const uint64_t dv = sw128_desc(sv + (kvi % KV_STAGES) * TILE_BYTES, DP * 128, 1024);
         const uint32_t d = tmem + (x ? T_O1 : T_O0), a = tmem + (x ? T_P1 : T_P0);
 #pragma unroll 1
         for (int kk = 0; kk < BLOCK_N / 16; ++kk)  // 16 keys = 8 packed bf16 columns per step
-          mma_f16_ts(d, a + kk * 8, dv + 128 * kk, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_f16_ts(d, a + kk * 8, dv + 128 * kk, idesc_o, (!first || kk > 0) ? 1u : 0u);
         tc_commit(&bars->pv_done[x]);
+        ++np[x];
       };
-      bool ok = mbar_wait(&bars->q_full, 0, wc) && mbar_wait(&bars->k_full[0], 0, wc);
-      if (ok) {
+      // The S buffer of group x is free once the softmax read the previous S.
+      auto s_ready = [&](int x) { return ns[x] == 0 || mbar_wait(&bars->s_free[x], (ns[x] - 1) & 1, wc); };
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+        const FwdItem I = fwd_item(args, w);
+        const int qb2 = ic & 1;
+        const uint32_t sq = smem_u32(smem + SM_Q + qb2 * 2 * TILE_BYTES);
+        if (!(ok = mbar_wait(&bars->q_full[qb2], (ic >> 1) & 1, wc) &&
+                   mbar_wait(&bars->k_full[gkv % KV_STAGES], (gkv / KV_STAGES) & 1, wc)))
+          break;
+        if (I.nA > 0) {
+          if (!(ok = s_ready(0))) break;
+          tc_fence_after();
+          issue_s(sq, 0, gkv);
+        }
+        if (!(ok = s_ready(1))) break;
         tc_fence_after();
-        if (nA > 0) issue_s(0, 0);
-        issue_s(1, 0);
-      }
-      for (int j = 0; ok && j < nB; ++j) {
-        const int s = j % KV_STAGES;
-        FWD_TRACE(8192 + j * 8 + 0);
-        if (j + 1 < nB) {
-          if (!(ok = mbar_wait(&bars->k_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, wc))) break;
-          if (j + 1 < nA) {
-            if (!(ok = mbar_wait(&bars->s_free[0], j & 1, wc))) break;
+        issue_s(sq, 1, gkv);
+        for (int j = 0; ok && j < I.nB; ++j) {
+          const uint32_t kvi = gkv + j;
+          const int s = kvi % KV_STAGES;
+          FWD_TRACE(8192 + j * 8 + 0);
+          if (j + 1 < I.nB) {
+            if (!(ok = mbar_wait(&bars->k_full[(kvi + 1) % KV_STAGES], ((kvi + 1) / KV_STAGES) & 1, wc))) break;
+            if (j + 1 < I.nA) {
+              if (!(ok = s_ready(0))) break;
+              tc_fence_after();
+              FWD_TRACE(8192 + j * 8 + 1);
+              issue_s(sq, 0, kvi + 1);
+            }
+            if (!(ok = s_ready(1))) break;
             tc_fence_after();
-            FWD_TRACE(8192 + j * 8 + 1);
-            issue_s(0, j + 1);
+            FWD_TRACE(8192 + j * 8 + 2);
+            issue_s(sq, 1, kvi + 1);
           }
-          if (!(ok = mbar_wait(&bars->s_free[1], j & 1, wc))) break;
+          if (!(ok = mbar_wait(&bars->v_full[s], (kvi / KV_STAGES) & 1, wc))) break;
+          if (j < I.nA) {
+            if (!(ok = mbar_wait(&bars->p_full[0], np[0] & 1, wc))) break;
+            tc_fence_after();
+            FWD_TRACE(8192 + j * 8 + 3);
+            issue_pv(0, kvi, j == 0);
+          }
+          if (!(ok = mbar_wait(&bars->p_full[1], np[1] & 1, wc))) break;
           tc_fence_after();
-          FWD_TRACE(8192 + j * 8 + 2);
-          issue_s(1, j + 1);
+          FWD_TRACE(8192 + j * 8 + 4);
+          issue_pv(1, kvi, j == 0);
+          tc_commit(&bars->kv_empty[s]);
         }
-        if (!(ok = mbar_wait(&bars->v_full[s], (j / KV_STAGES) & 1, wc))) break;
-        if (j < nA) {
-          if (!(ok = mbar_wait(&bars->p_full[0], j & 1, wc))) break;
-          tc_fence_after();
-          FWD_TRACE(8192 + j * 8 + 3);
-          issue_pv(0, j);
-        }
-        if (!(ok = mbar_wait(&bars->p_full[1], j & 1, wc))) break;
-        tc_fence_after();
-        FWD_TRACE(8192 + j * 8 + 4);
-        issue_pv(1, j);
-        tc_commit(&bars->kv_empty[s]);
+        tc_commit(&bars->q_empty[qb2]);  // every S of this item has read Q
+        gkv += I.nB;
       }
     }
     __syncwarp();
@@ -230,127 +276,145 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int x = warp >> 2;
     const int q = warp & 3;
     const int r = q * 32 + lane;
-    const int qrow = q0 + x * BLOCK_M + r;
-    const int n = ntile[x];
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t t_s = tmem + lane_off + (x ? T_S1 : T_S0);
     const uint32_t t_o = tmem + lane_off + (x ? T_O1 : T_O0);
     const float sl2 = args.scale * 1.4426950408889634f;  // scores -> log2 units
     const uint32_t t_p = tmem + lane_off + (x ? T_P1 : T_P0);
-    float m_run = -INFINITY, l_run = 0.f;
+    // Phases consumed so far across items: S / PV tiles of this group, and
+    // completions of the turn barrier this group waits on (A: turn[0], which
+    // completes nA-1 times per item; B: turn[1], nA times per item).
+    uint32_t kbase = 0, tbase = 0;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      const bool trc = (warp & 3) == 0 && lane == 0;
-      const int tb = x * 4096 + j * 8;
-      if (trc) FWD_TRACE(tb + 0);
-      if (!(ok = mbar_wait(&bars->s_full[x], j & 1, wc))) break;
-      if (trc) FWD_TRACE(tb + 1);
-      tc_fence_after();
-      float s[BLOCK_N];
-#pragma unroll
-      for (int c = 0; c < BLOCK_N; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&s[c]));
-      tmem_ld_wait();
-      // S is in registers: let the MMA warp compute the next S into this buffer.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->s_free[x]);
-      const int k0 = j * BLOCK_N;
-      const bool need_mask = (args.causal && k0 + BLOCK_N - 1 > q0 + x * BLOCK_M) || (k0 + BLOCK_N > args.S);
-      if (need_mask) {
-        const int lim = (args.causal ? min(qrow, args.S - 1) : args.S - 1) - k0;  // last visible column
-#pragma unroll
-        for (int c = 0; c < BLOCK_N; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
-      }
-      // Row max of the raw scores with 8 independent partial maxima (short
-      // dependency chains); scale > 0, so max(s)*sl2 = max(s*sl2).
-      float pm[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = s[i];
-#pragma unroll
-      for (int c = 8; c < BLOCK_N; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
-      const float mt = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
-      // lazy rescale
-      float factor = 1.f;
-      if (mt > m_run + RESCALE_LOG2 || m_run == -INFINITY) {
-        factor = (m_run == -INFINITY) ? 0.f : ex2(m_run - mt);
-        m_run = mt;
-      }
-      const float nmb = (m_run == -INFINITY) ? 0.f : -m_run;
-      // Exponential phase turn: A_j waits for B_(j-1), B_j waits for A_j.
-      if (x == 0 ? j > 0 : j < ntile[0]) {
-        if (!(ok = mbar_wait(&bars->turn[x], x == 0 ? (j - 1) & 1 : j & 1, wc))) break;
-      }
-      if (trc) FWD_TRACE(tb + 2);
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t p[BLOCK_N / 2];
-      auto step = [&](auto cc) {
-        constexpr int c = decltype(cc)::value;
-        const float e0 = ex2_col<c, DGX_EXP_EMU_FWD>(fmaf(s[c], sl2, nmb)), e1 = ex2_col<c + 1, DGX_EXP_EMU_FWD>(fmaf(s[c + 1], sl2, nmb));
-        ps[(c >> 1) & 7] += e0 + e1;
-        p[c / 2] = pack_bf16x2_fast(e0, e1);
-      };
-      static_for<0, BLOCK_N, 2>(step);
-      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      if (trc) FWD_TRACE(tb + 3);
-      // Hand the turn to the other group (B only while A has tiles left).
-      __syncwarp();
-      if (lane == 0 && (x == 0 || j + 1 < ntile[0])) mbar_arrive(&bars->turn[x ^ 1]);
-      l_run = l_run * factor + rs;
-      if (j > 0) {
-        // PV(j-1) must be done: it reads the P buffer and accumulates O.
-        if (!(ok = mbar_wait(&bars->pv_done[x], (j - 1) & 1, wc))) break;
+    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+      const FwdItem I = fwd_item(args, w);
+      const int n = x ? I.nB : I.nA;
+      const int qrow = I.q0 + x * BLOCK_M + r;
+      const int row_base = I.bh * args.S;  // row of the [BH*S, D] view
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const uint32_t k = kbase + j;
+        const bool trc = (warp & 3) == 0 && lane == 0;
+        const int tb = x * 4096 + j * 8;
+        if (trc) FWD_TRACE(tb + 0);
+        if (!(ok = mbar_wait(&bars->s_full[x], k & 1, wc))) break;
+        if (trc) FWD_TRACE(tb + 1);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, factor != 1.f)) {
-          uint32_t o[32];
+        float s[BLOCK_N];
 #pragma unroll
-          for (int c = 0; c < DP; c += 32) {
-            tmem_ld32(t_o + c, o);
-            tmem_ld_wait();
+        for (int c = 0; c < BLOCK_N; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&s[c]));
+        tmem_ld_wait();
+        // S is in registers: let the MMA warp compute the next S into this buffer.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->s_free[x]);
+        const int k0 = j * BLOCK_N;
+        const bool need_mask = (args.causal && k0 + BLOCK_N - 1 > I.q0 + x * BLOCK_M) || (k0 + BLOCK_N > args.S);
+        if (need_mask) {
+          const int lim = (args.causal ? min(qrow, args.S - 1) : args.S - 1) - k0;  // last visible column
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-            tmem_st16(t_o + c, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-            tmem_st16(t_o + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+          for (int c = 0; c < BLOCK_N; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
+        }
+        // Row max of the raw scores with 8 independent partial maxima (short
+        // dependency chains); scale > 0, so max(s)*sl2 = max(s*sl2).
+        float pm[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pm[i] = s[i];
+#pragma unroll
+        for (int c = 8; c < BLOCK_N; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+        const float mt = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
+        // lazy rescale
+        float factor = 1.f;
+        if (mt > m_run + RESCALE_LOG2 || m_run == -INFINITY) {
+          factor = (m_run == -INFINITY) ? 0.f : ex2(m_run - mt);
+          m_run = mt;
+        }
+        const float nmb = (m_run == -INFINITY) ? 0.f : -m_run;
+        // Exponential phase turn: A_j waits for B_(j-1), B_j waits for A_j.
+        if (x == 0 ? j > 0 : j < I.nA) {
+          if (!(ok = mbar_wait(&bars->turn[x], (x == 0 ? tbase + j - 1 : tbase + j) & 1, wc))) break;
+        }
+        if (trc) FWD_TRACE(tb + 2);
+        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t p[BLOCK_N / 2];
+        auto step = [&](auto cc) {
+          constexpr int c = decltype(cc)::value;
+          const float e0 = ex2_col<c, DGX_EXP_EMU_FWD>(fmaf(s[c], sl2, nmb)), e1 = ex2_col<c + 1, DGX_EXP_EMU_FWD>(fmaf(s[c + 1], sl2, nmb));
+          ps[(c >> 1) & 7] += e0 + e1;
+          p[c / 2] = pack_bf16x2_fast(e0, e1);
+        };
+        static_for<0, BLOCK_N, 2>(step);
+        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        if (trc) FWD_TRACE(tb + 3);
+        // Hand the turn to the other group (B only while A has tiles left).
+        __syncwarp();
+        if (lane == 0 && (x == 0 || j + 1 < I.nA)) mbar_arrive(&bars->turn[x ^ 1]);
+        l_run = l_run * factor + rs;
+        if (j > 0) {
+          // PV(j-1) must be done: it reads the P buffer and accumulates O.
+          if (!(ok = mbar_wait(&bars->pv_done[x], (k - 1) & 1, wc))) break;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, factor != 1.f)) {
+            uint32_t o[32];
+#pragma unroll
+            for (int c = 0; c < DP; c += 32) {
+              tmem_ld32(t_o + c, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+              tmem_st16(t_o + c, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+              tmem_st16(t_o + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+            }
+            tmem_st_wait();
           }
-          tmem_st_wait();
+        }
+        if (trc) FWD_TRACE(tb + 4);
+        // P(j) overwrites P(j-1), which PV(j-1) (waited for above, or of the
+        // previous item, which the epilogue waited for) has read.
+#pragma unroll
+        for (int c = 0; c < BLOCK_N / 2; c += 16) tmem_st16(t_p + c, *reinterpret_cast<uint32_t(*)[16]>(&p[c]));
+        tmem_st_wait();
+        if (trc) FWD_TRACE(tb + 5);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[x]);
+      }
+      if (!ok) break;
+      // ------------------------------------------------------------ item epilogue
+      // The next item's first PV overwrites O: it follows this warp's next
+      // p_full arrival, which comes after these loads.
+      if (n > 0) {
+        if (!(ok = mbar_wait(&bars->pv_done[x], (kbase + n - 1) & 1, wc))) break;
+        tc_fence_after();
+        uint32_t o[DP];
+#pragma unroll
+        for (int c = 0; c < DP; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
+        tmem_ld_wait();
+        tc_fence_before();
+        if (qrow < args.S) {
+          const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+          __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.O) + ((size_t)row_base + qrow) * args.D;
+          if (args.D == DP) {
+#pragma unroll
+            for (int c = 0; c < DP; c += 8) {
+              uint4 wv;
+              wv.x = pack_bf16x2(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
+              wv.y = pack_bf16x2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
+              wv.z = pack_bf16x2(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
+              wv.w = pack_bf16x2(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c) = wv;
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < DP; ++c)
+              if (c < args.D) orow[c] = __float2bfloat16_rn(__uint_as_float(o[c]) * inv);
+          }
+          if (args.lse) args.lse[(size_t)row_base + qrow] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
         }
       }
-      if (trc) FWD_TRACE(tb + 4);
-#pragma unroll
-      for (int c = 0; c < BLOCK_N / 2; c += 16) tmem_st16(t_p + c, *reinterpret_cast<uint32_t(*)[16]>(&p[c]));
-      tmem_st_wait();
-      if (trc) FWD_TRACE(tb + 5);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[x]);
-    }
-    // ------------------------------------------------------------ epilogue
-    if (ok && n > 0 && mbar_wait(&bars->pv_done[x], (n - 1) & 1, wc)) {
-      tc_fence_after();
-      uint32_t o[DP];
-#pragma unroll
-      for (int c = 0; c < DP; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
-      tmem_ld_wait();
-      if (qrow < args.S) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.O) + ((size_t)row_base + qrow) * args.D;
-        if (args.D == DP) {
-#pragma unroll
-          for (int c = 0; c < DP; c += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c) = w;
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < DP; ++c)
-            if (c < args.D) orow[c] = __float2bfloat16_rn(__uint_as_float(o[c]) * inv);
-        }
-        if (args.lse) args.lse[(size_t)row_base + qrow] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
-      }
+      kbase += n;
+      tbase += x == 0 ? (I.nA - 1) : I.nA;
     }
   }
 
@@ -397,9 +461,10 @@ cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s) {
     attr = true;
   }
   const int nqb = (a.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M);
+  const int items = nqb * a.BH;
   {
     TimerScope timer(s);
-    flash_fwd_kernel<<<nqb * a.BH, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, a);
+    flash_fwd_kernel<<<items < num_sms() ? items : num_sms(), NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, a);
   }
   return cudaGetLastError();
 }
