@@ -309,11 +309,13 @@ def run_tp_gemm(args, rank, world, local_rank):
 def run_secondary(local_rank):
     """The other BASELINE configs on this GPU, each timed with CUDA events
     after warm-up (rank 0 at N=1 only):
+      configs[4]  int8 weight-only dense 4096x4096, B in {1, 16, 256}, both modes
       configs[0]  f32 GEMM 1024^3 + dA/dB backward (3xTF32 tcgen05)
       configs[3]  bf16 GEMM 4096/8192/16384^3, single GPU
-      configs[4]  int8 weight-only dense 4096x4096, B in {1, 16, 256}, both modes
       configs[2]  char-level GPT training step (fwd + bwd + AdamW), tokens/s
-    Operands that fit in L2 are cycled through enough copies to exceed it."""
+    Operands that fit in L2 are cycled through enough copies to exceed it.
+    Each entry carries the median SM clock sampled over its timed replays
+    (the latency-bound int8 layer runs first, before the GEMM sweeps)."""
     import torch
     import dreamcompiler_b200 as dgx
     dev = torch.device("cuda", local_rank)
@@ -337,14 +339,37 @@ def run_secondary(local_rank):
         graph.replay()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize(dev)
+        with ClockSampler(local_rank) as clk:
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+        last_clk["sm_mhz"] = clk.summary()["sm_mhz"]
         dgx.sync_check()
         del graph
         return e0.elapsed_time(e1) / 1e3 / (iters * reps)
+
+    last_clk = {}
+
+    # configs[4]: int8 weight-only 4096x4096; 16 weight copies (256 MB) cycle past L2
+    N = K = 4096
+    Ws = [torch.randint(-127, 128, (N, K), device=dev, dtype=torch.int8, generator=g) for _ in range(16)]
+    sc = torch.rand(N, device=dev, generator=g) * 9e-3 + 1e-3
+    bias = torch.randn(N, device=dev, generator=g)
+    w8 = {}
+    for Bn in (1, 16, 256):
+        X = torch.randn(Bn, K, device=dev, generator=g)
+        Y = torch.empty(Bn, N, device=dev)
+        for mode in (0, 1):
+            t = timed(lambda i: dgx.gemm_w8(X, Ws[i % 16], sc, bias, mode=mode, out=Y), 64)
+            byts = N * K + Bn * K * 4 + Bn * N * 4 + N * 8
+            w8[f"B{Bn}_{'w8a32' if mode == 0 else 'w8a8'}"] = {"us": t * 1e6, "gb_s": byts / t / 1e9,
+                                                               "tops": 2 * Bn * N * K / t / 1e12,
+                                                               "sm_mhz": last_clk["sm_mhz"]}
+    res["config5_int8_w8"] = w8
+    del Ws
+    torch.cuda.empty_cache()
 
     # f32 1024^3 forward + backward; 24 operand sets (288 MB) cycle past L2
     n = 1024
@@ -361,6 +386,7 @@ def run_secondary(local_rank):
         dgx.gemm(A, dC, transA=True, out=dB, workspace=ws)
     t = timed(f32_step, 50)
     res["config1_f32_gemm_1024_fwd_bwd"] = {"ms_per_step": t * 1e3, "tflops": 6 * n ** 3 / t / 1e12,
+                                            "sm_mhz": last_clk["sm_mhz"],
                                             "path": "3xTF32 on tcgen05 kind::tf32 (3 MMAs per K step)"}
     del sets, C, dA, dB, ws
 
@@ -372,28 +398,10 @@ def run_secondary(local_rank):
         B = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
         Cb = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
         t = timed(lambda i: dgx.gemm(A[i % copies], B[i % copies], out=Cb), 20 if n < 16384 else 6)
-        sweep[str(n)] = {"ms": t * 1e3, "tflops": 2 * n ** 3 / t / 1e12}
+        sweep[str(n)] = {"ms": t * 1e3, "tflops": 2 * n ** 3 / t / 1e12, "sm_mhz": last_clk["sm_mhz"]}
         del A, B, Cb
         torch.cuda.empty_cache()
     res["config4_bf16_gemm"] = sweep
-
-    # configs[4]: int8 weight-only 4096x4096; 16 weight copies (256 MB) cycle past L2
-    N = K = 4096
-    Ws = [torch.randint(-127, 128, (N, K), device=dev, dtype=torch.int8, generator=g) for _ in range(16)]
-    sc = torch.rand(N, device=dev, generator=g) * 9e-3 + 1e-3
-    bias = torch.randn(N, device=dev, generator=g)
-    w8 = {}
-    for Bn in (1, 16, 256):
-        X = torch.randn(Bn, K, device=dev, generator=g)
-        Y = torch.empty(Bn, N, device=dev)
-        for mode in (0, 1):
-            t = timed(lambda i: dgx.gemm_w8(X, Ws[i % 16], sc, bias, mode=mode, out=Y), 64)
-            byts = N * K + Bn * K * 4 + Bn * N * 4 + N * 8
-            w8[f"B{Bn}_{'w8a32' if mode == 0 else 'w8a8'}"] = {"us": t * 1e6, "gb_s": byts / t / 1e9,
-                                                               "tops": 2 * Bn * N * K / t / 1e12}
-    res["config5_int8_w8"] = w8
-    del Ws
-    torch.cuda.empty_cache()
 
     # char-level GPT training step (6 layers, d 384, 6 heads, seq 256,
     # batch 64, vocab 65): forward, backward and AdamW, synthetic uniform token ids
@@ -406,6 +414,7 @@ def run_secondary(local_rank):
     t = timed(lambda i: model.step(), 4)
     res["config3_gpt_train_step"] = {"ms_per_step": t * 1e3, "tokens_per_s": cfg.batch * cfg.seq_len / t,
                                      "tflops": cfg.flops_per_step() / t / 1e12, "loss": float(model.loss.item()),
+                                     "sm_mhz": last_clk["sm_mhz"],
                                      "params": cfg.n_params(), "algorithmic_flop_per_step": cfg.flops_per_step(),
                                      "precision": "bf16 GEMM/attention operands, fp32 master weights, grads, AdamW"}
     del model

@@ -35,6 +35,7 @@ struct FlashBwdArgs {
   float scale;
   int causal;
   uint32_t* err;
+  int zero_acc;    // the row pre-pass also zeroes dq_acc (tensor-core path)
 };
 
 // Scratch bytes the backward needs (dQ accumulator + padded row statistics).

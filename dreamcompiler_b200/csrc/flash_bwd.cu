@@ -144,6 +144,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
+  // Launched as a programmatic dependent of the row pre-pass: its statistics
+  // and the zeroed dQ accumulator are visible after this wait. The dQ
+  // conversion kernel may be scheduled from here on (it waits for this grid).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // Each role's setmaxnreg sits inside its branch so that it dominates (and
   // sets the register limit for) exactly that role's code.
@@ -456,6 +461,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // layout (rows past S: D = 0, L2 = +inf so that exp2(s - L2) = 0). Eight
 // lanes per row, 16-byte loads when D % 8 == 0.
 __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
+  // The main kernel may be scheduled now; it waits for this grid's results.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const long long rows = (long long)a.BH * a.Spad;
   const int sub = threadIdx.x & 7;
   const long long groups = (long long)gridDim.x * (blockDim.x >> 3);
@@ -485,6 +492,13 @@ __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
     s += __shfl_xor_sync(0xffffffffu, s, 4);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
     s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (a.zero_acc && q < a.S) {  // fresh fp32 dQ accumulator rows for the bulk reduce-adds
+      float* acc = a.dq_acc + ((long long)bh * a.S + q) * a.D;
+      if (vec)
+        for (int c = sub * 4; c < a.D; c += 32) *reinterpret_cast<float4*>(acc + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+      else
+        for (int c = sub; c < a.D; c += 8) acc[c] = 0.f;
+    }
     if (sub == 0) {
       a.rowstat[r] = q < a.S ? s : 0.f;
       a.rowstat[rows + r] = q < a.S ? a.lse[(long long)bh * a.S + q] * 1.4426950408889634f : INFINITY;
@@ -492,8 +506,11 @@ __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
   }
 }
 
-// dQ = bf16(scale * dQ_acc), four elements per thread step.
+// dQ = bf16(scale * dQ_acc), four elements per thread step. Launched as a
+// programmatic dependent of the main kernel: it starts on SMs the main
+// kernel has left and waits here for that grid to finish.
 __global__ void flash_bwd_post_kernel(FlashBwdArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long total = (long long)a.BH * a.S * a.D;
   const long long quads = total / 4;
   __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(a.dQ);
@@ -553,16 +570,41 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
       return cudaErrorInvalidValue;
   }
   const int sms = num_sms();
-  cudaError_t e = cudaMemsetAsync(a.dq_acc, 0, (size_t)a.BH * a.S * a.D * sizeof(float), s);
-  if (e != cudaSuccess) return e;
-  flash_bwd_pre_kernel<<<8 * sms, 256, 0, s>>>(a);
+  // Three launches chained by programmatic dependent launch: the row
+  // pre-pass (which also zeroes the dQ accumulator), the main kernel, the
+  // dQ conversion. Each dependent waits (griddepcontrol.wait) for its
+  // predecessor's results; only its launch overlaps the predecessor's tail.
+  FlashBwdArgs pa = a;
+  pa.zero_acc = 1;
+  flash_bwd_pre_kernel<<<8 * sms, 256, 0, s>>>(pa);
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
   const int nkv = (a.S + BKV - 1) / BKV;
+  cudaError_t e;
   {
-    TimerScope timer(s);
     const int items = nkv * a.BH;
-    flash_bwd_kernel<<<items < sms ? items : sms, NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, mdo, mdq, a);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(items < sms ? items : sms);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = s;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    TimerScope timer(s);
+    e = cudaLaunchKernelEx(&cfg, flash_bwd_kernel, mq, mk, mv, mdo, mdq, a);
+    if (e != cudaSuccess) return e;
   }
-  flash_bwd_post_kernel<<<4 * sms, 256, 0, s>>>(a);
+  {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(4 * sms);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, flash_bwd_post_kernel, a);
+    if (e != cudaSuccess) return e;
+  }
   return cudaGetLastError();
 }
 
