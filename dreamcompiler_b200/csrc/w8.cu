@@ -33,7 +33,7 @@ template <int MODE>
 __global__ void __launch_bounds__(256) w8_kernel(const void* __restrict__ X, const int8_t* __restrict__ W,
                                                  const float* __restrict__ scale, const float* __restrict__ bias,
                                                  const float* __restrict__ sx, float* __restrict__ Y,
-                                                 int32_t* __restrict__ acc_out, int B, int N, int K) {
+                                                 int32_t* __restrict__ acc_out, int B, int N, int K, W8Epi epi) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = (blockIdx.x * WARPS + warp) * CPW;
   const int b0 = blockIdx.y * BT;
@@ -117,14 +117,20 @@ __global__ void __launch_bounds__(256) w8_kernel(const void* __restrict__ X, con
         float v = facc[c][b];
 #pragma unroll
         for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0 && n < N && b < nb) Y[(size_t)(b0 + b) * N + n] = (bias ? bias[n] : 0.f) + scale[n] * v;
+        if (lane == 0 && n < N && b < nb) {
+          const float y = (bias ? bias[n] : 0.f) + (scale ? scale[n] : epi.scale_all) * v;
+          Y[(size_t)(b0 + b) * N + n] = epi.relu ? fmaxf(y, 0.f) : y;
+        }
       } else {
         int v = iacc[c][b];
 #pragma unroll
         for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
         if (lane == 0 && n < N && b < nb) {
           if (acc_out) acc_out[(size_t)(b0 + b) * N + n] = v;
-          if (Y) Y[(size_t)(b0 + b) * N + n] = (bias ? bias[n] : 0.f) + scale[n] * sx[b0 + b] * (float)v;
+          if (Y) {
+            const float y = (bias ? bias[n] : 0.f) + (scale ? scale[n] : epi.scale_all) * sx[b0 + b] * (float)v;
+            Y[(size_t)(b0 + b) * N + n] = epi.relu ? fmaxf(y, 0.f) : y;
+          }
         }
       }
     }
@@ -210,12 +216,13 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const float* __rest
 }  // namespace
 
 cudaError_t w8_simt(const void* X, const int8_t* W, const float* scale, const float* bias, const float* sx,
-                    float* Y, int32_t* acc, int B, int N, int K, int mode, cudaStream_t s) {
+                    float* Y, int32_t* acc, int B, int N, int K, int mode, cudaStream_t s,
+                    const W8Epi& epi = W8Epi()) {
   dim3 grid((N + WARPS * CPW - 1) / (WARPS * CPW), (B + BT - 1) / BT);
   if (mode == 0)
-    w8_kernel<0><<<grid, 256, 0, s>>>(X, W, scale, bias, sx, Y, acc, B, N, K);
+    w8_kernel<0><<<grid, 256, 0, s>>>(X, W, scale, bias, sx, Y, acc, B, N, K, epi);
   else
-    w8_kernel<1><<<grid, 256, 0, s>>>(X, W, scale, bias, sx, Y, acc, B, N, K);
+    w8_kernel<1><<<grid, 256, 0, s>>>(X, W, scale, bias, sx, Y, acc, B, N, K, epi);
   return cudaGetLastError();
 }
 
@@ -265,6 +272,37 @@ dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B
                      "dgx_gemm_i8i32");
 }
 
+}  // extern "C"
+
+namespace dgx {
+
+// The fp32-activation int8 layer of dgx_gemm_w8 and dgx_dense_q.
+static dgx_status w8_layer(const char* op, const float* X, const int8_t* W, const float* scale, const float* bias,
+                           float* Y, int B, int N, int K, int mode, const W8Epi& epi, cudaStream_t s) {
+  if (mode == 0 && (K % 16 != 0 || K > kW8MaxK))
+    return cuda_status(w8_simt(X, W, scale, bias, nullptr, Y, nullptr, B, N, K, 0, s, epi), op);
+  // Library scratch: the int8 activation planes (3 for W8A32, 1 for W8A8)
+  // and one fp32 scale per row.
+  const int planes = mode == 0 ? 3 : 1;
+  const size_t xq_bytes = ((size_t)planes * B * K + 255) & ~size_t(255);
+  uint8_t* ws = (uint8_t*)library_scratch(xq_bytes + (size_t)B * sizeof(float), s);
+  if (!ws) return set_error(DGX_ENOMEM, "%s: scratch", op);
+  int8_t* xq = reinterpret_cast<int8_t*>(ws);
+  float* rs = reinterpret_cast<float*>(ws + xq_bytes);
+  if (mode == 0) {
+    cudaError_t e = w8_split_planes(X, xq, rs, B, K, s);
+    if (e != cudaSuccess) return cuda_status(e, op);
+    return cuda_status(w8_tc_gemm(xq, 3, W, scale, bias, rs, Y, nullptr, B, N, K, true, s, epi), op);
+  }
+  cudaError_t e = quantize_rows(X, xq, rs, B, K, s);
+  if (e != cudaSuccess) return cuda_status(e, op);
+  return cuda_status(w8a8_from_q(xq, W, scale, bias, rs, Y, nullptr, B, N, K, true, s), op);
+}
+
+}  // namespace dgx
+
+extern "C" {
+
 dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y, int B,
                        int N, int K, int mode, void* stream) {
   if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_w8: negative size");
@@ -272,25 +310,19 @@ dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, cons
   if (B == 0 || N == 0) return DGX_OK;
   if (!X || !W || !scale || !Y) return set_error(DGX_EINVAL, "dgx_gemm_w8: null pointer");
   if (((uintptr_t)X | (uintptr_t)W) & 15) return set_error(DGX_EINVAL, "dgx_gemm_w8: X and W must be 16-byte aligned");
-  cudaStream_t s = (cudaStream_t)stream;
-  if (mode == 0 && (K % 16 != 0 || K > kW8MaxK))
-    return cuda_status(w8_simt(X, W, scale, bias, nullptr, Y, nullptr, B, N, K, 0, s), "dgx_gemm_w8");
-  // Library scratch: the int8 activation planes (3 for W8A32, 1 for W8A8)
-  // and one fp32 scale per row.
-  const int planes = mode == 0 ? 3 : 1;
-  const size_t xq_bytes = ((size_t)planes * B * K + 255) & ~size_t(255);
-  uint8_t* ws = (uint8_t*)library_scratch(xq_bytes + (size_t)B * sizeof(float), s);
-  if (!ws) return set_error(DGX_ENOMEM, "dgx_gemm_w8: scratch");
-  int8_t* xq = reinterpret_cast<int8_t*>(ws);
-  float* rs = reinterpret_cast<float*>(ws + xq_bytes);
-  if (mode == 0) {
-    cudaError_t e = w8_split_planes(X, xq, rs, B, K, s);
-    if (e != cudaSuccess) return cuda_status(e, "dgx_gemm_w8 split");
-    return cuda_status(w8_tc_gemm(xq, 3, W, scale, bias, rs, Y, nullptr, B, N, K, true, s), "dgx_gemm_w8");
-  }
-  cudaError_t e = quantize_rows(X, xq, rs, B, K, s);
-  if (e != cudaSuccess) return cuda_status(e, "dgx_gemm_w8 quantize");
-  return cuda_status(w8a8_from_q(xq, W, scale, bias, rs, Y, nullptr, B, N, K, true, s), "dgx_gemm_w8");
+  return w8_layer("dgx_gemm_w8", X, W, scale, bias, Y, B, N, K, mode, W8Epi(), (cudaStream_t)stream);
+}
+
+dgx_status dgx_dense_q(const float* X, const int8_t* W, float scale, const float* scales, const float* bias,
+                       float* Y, int B, int out_dim, int in_dim, int relu, void* stream) {
+  if (B < 0 || out_dim < 0 || in_dim < 0) return set_error(DGX_EINVAL, "dgx_dense_q: negative size");
+  if (B == 0 || out_dim == 0) return DGX_OK;
+  if (!X || !W || !Y) return set_error(DGX_EINVAL, "dgx_dense_q: null pointer");
+  if (((uintptr_t)X | (uintptr_t)W) & 15) return set_error(DGX_EINVAL, "dgx_dense_q: X and W must be 16-byte aligned");
+  W8Epi epi;
+  epi.scale_all = scale;
+  epi.relu = relu ? 1 : 0;
+  return w8_layer("dgx_dense_q", X, W, scales, bias, Y, B, out_dim, in_dim, 0, epi, (cudaStream_t)stream);
 }
 
 }  // extern "C"

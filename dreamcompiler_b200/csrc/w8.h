@@ -5,6 +5,13 @@
 
 namespace dgx {
 
+// Output options for the exported-network form (dgx_dense_q): one scale for
+// every channel when the per-channel `scale` pointer is null, and ReLU.
+struct W8Epi {
+  float scale_all = 0.f;
+  int relu = 0;
+};
+
 // Largest K for which the exact int32 accumulators of the tensor-core path
 // cannot overflow: |w*q| <= 128*127 per product.
 constexpr int kW8MaxK = 131072;
@@ -22,7 +29,7 @@ constexpr int kW8MaxK = 131072;
 // has finished.
 cudaError_t w8_tc_gemm(const int8_t* Xp, int planes, const int8_t* W, const float* scale, const float* bias,
                        const float* rowscale, float* Y, int32_t* acc_out, int B, int N, int K,
-                       bool after_producer, cudaStream_t s);
+                       bool after_producer, cudaStream_t s, const W8Epi& epi = W8Epi());
 
 // Split fp32 rows into the three int8 planes above (Xp[3][B][K]) and the
 // power-of-two row scales. K % 16 == 0.

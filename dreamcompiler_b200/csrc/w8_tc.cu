@@ -89,7 +89,12 @@ struct W8TcArgs {
   int inbox_bytes;  // splits > 1: partials received, [splits][planes][per][128] int32
   int tma_out;      // 1: the single output (Y, or acc_out) leaves by one TMA tensor store per CTA
   uint32_t* err;
+  float scale_all;  // the scale of every channel when `scale` is null
+  int relu;         // Y <- max(Y, 0)
 };
+
+// ReLU of the exported-network layers (dgx_dense_q); identity otherwise.
+__device__ __forceinline__ float w8_act(const W8TcArgs& a, float y) { return a.relu ? fmaxf(y, 0.f) : y; }
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -132,11 +137,11 @@ __device__ __forceinline__ void w8_store(const W8TcArgs& a, int b, int n, float 
   const size_t o = (size_t)b * a.N + n;
   if (a.planes == 1) {
     if (a.acc_out) a.acc_out[o] = a0;
-    if (a.Y) a.Y[o] = fmaf(sc * rs, (float)a0, bi);
+    if (a.Y) a.Y[o] = w8_act(a, fmaf(sc * rs, (float)a0, bi));
   } else {
     // exact A0*2^14 + A1*2^7 + A2, rounded once
     const long long t = ((long long)a0 << 14) + ((long long)a1 << 7) + (long long)a2;
-    a.Y[o] = fmaf(sc, __ll2float_rn(t) * (0x1p-14f * rs), bi);
+    a.Y[o] = w8_act(a, fmaf(sc, __ll2float_rn(t) * (0x1p-14f * rs), bi));
   }
 }
 
@@ -265,7 +270,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // Everything the stores need is fetched while the MMAs run.
     grid_dep_wait();  // the row scales come from the producer kernel
     if (n < a.N && a.Y) {
-      sc = a.scale[n];
+      sc = a.scale ? a.scale[n] : a.scale_all;
       bi = a.bias ? a.bias[n] : 0.f;
     }
     for (int b = threadIdx.x; b < nb; b += 128) rs_s[b] = a.rowscale ? a.rowscale[b0 + b] : 0.f;
@@ -296,7 +301,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) f[j] = sc * rs_s[c + j];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) tile[(c + j) * TC_BM] = fmaf(f[j], (float)(int)v[j], bi);
+            for (int j = 0; j < 32; ++j) tile[(c + j) * TC_BM] = w8_act(a, fmaf(f[j], (float)(int)v[j], bi));
           }
         }
       } else {
@@ -314,7 +319,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int j = 0; j < 16; ++j) {
             // exact A0*2^14 + A1*2^7 + A2, rounded once
             const long long t = ((long long)(int)v0[j] << 14) + ((long long)(int)v1[j] << 7) + (int)v2[j];
-            tile[(c + j) * TC_BM] = fmaf(sc, __ll2float_rn(t) * f[j], bi);
+            tile[(c + j) * TC_BM] = w8_act(a, fmaf(sc, __ll2float_rn(t) * f[j], bi));
           }
         }
       }
@@ -351,10 +356,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               const size_t o = (size_t)(c + j) * ld;
               if (a.planes == 1) {
                 if (ap) ap[o] = (int)v0[j];
-                if (yp) yp[o] = fmaf(sc * rsv[j], (float)(int)v0[j], bi);
+                if (yp) yp[o] = w8_act(a, fmaf(sc * rsv[j], (float)(int)v0[j], bi));
               } else {
                 const long long t = ((long long)(int)v0[j] << 14) + ((long long)(int)v1[j] << 7) + (int)v2[j];
-                yp[o] = fmaf(sc, __ll2float_rn(t) * (0x1p-14f * rsv[j]), bi);
+                yp[o] = w8_act(a, fmaf(sc, __ll2float_rn(t) * (0x1p-14f * rsv[j]), bi));
               }
             }
           }
@@ -527,9 +532,11 @@ int round16(int x) { return (x + 15) & ~15; }
 
 cudaError_t w8_tc_gemm(const int8_t* Xp, int planes, const int8_t* W, const float* scale, const float* bias,
                        const float* rowscale, float* Y, int32_t* acc_out, int B, int N, int K, bool after_producer,
-                       cudaStream_t s) {
+                       cudaStream_t s, const W8Epi& epi) {
   W8TcArgs a{};
   a.scale = scale;
+  a.scale_all = epi.scale_all;
+  a.relu = epi.relu;
   a.bias = bias;
   a.rowscale = rowscale;
   a.Y = Y;

@@ -178,6 +178,21 @@ dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, cons
  */
 dgx_status dgx_gemm_w8a8_noalloc(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y,
                                  int B, int N, int K, void* stream);
+/*
+ * One layer of the C inference code export_c_header_int8 writes
+ * (runtime/nn/training.inc:3694-3752), for a batch of B inputs at once:
+ *   Y[b][j] = relu?( bias[j] + s_j * sum_k W[j][k] * X[b][k] ),
+ * with W the emitted `static const int8_t <layer>_weight[out_dim*in_dim]`
+ * array as is ([out][in], row = output channel), s_j = `scale` (the emitted
+ * per-tensor `<layer>_weight_scale`) when `scales` is NULL, else scales[j]
+ * (the per-channel variant of the exporter), bias the emitted float array,
+ * relu = 1 for every layer but the last (the emitted relu_inplace). The
+ * products are exact (the fp32 activations go through the 3-plane int8
+ * split) and each output is rounded once, where the emitted dense_q adds
+ * fp32 terms one by one.
+ */
+dgx_status dgx_dense_q(const float* X, const int8_t* W, float scale, const float* scales, const float* bias,
+                       float* Y, int B, int out_dim, int in_dim, int relu, void* stream);
 /* Exact int32 accumulators acc[b,n] = sum_k Xq[b,k]*W[n,k] (the W8A8 core). */
 dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream);
 /* Per-row symmetric quantisation used by mode 1: Xq = clamp(round(X/sx)), sx = max|X_b|/127. */

@@ -58,6 +58,10 @@ _SIG = {
     "dream_nll_loss": [TP, TP],
     "dream_adamw_update": [TP, TP, TP, TP, TP, TP],
     "zero_grad": [TP],
+    "dream_str_create": [C.c_char_p],
+    "dream_ckpt_new": [],
+    "dream_ckpt_add": [TP, TP, TP],
+    "dream_export_c_header_int8": [TP, TP, TP],
     "gemm_selftest": [],
     "flash_attention_selftest": [],
     "tensor_parallel_selftest": [],

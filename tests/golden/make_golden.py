@@ -23,6 +23,12 @@ output comes from the reference's own ops:
              runtime/ops/autograd.inc:549-574)
   attn.npz   dream_attention and dream_attention_causal + their backward
              (runtime/nn/training.inc:177-263, runtime/ops/autograd.inc:675-778)
+  int8_export/mlp_int8.{c,h} + int8_export.npz
+             a 3-layer MLP checkpoint exported by the reference's own
+             export_c_header_int8 (runtime/nn/training.inc:3494-3817); inputs
+             X and the outputs Y of that emitted C code (compiled with cc),
+             plus Ypc from the per-channel variant this repository writes
+             (dreamcompiler_b200/int8_export.py) for the same weights
 
 Usage:  python tests/golden/make_golden.py [fixture ...]
 """
@@ -30,7 +36,10 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import shutil
+import subprocess
 import sys
+import tempfile
 
 import numpy as np
 
@@ -252,10 +261,64 @@ def gen_attn():
     np.savez_compressed(os.path.join(HERE, "attn.npz"), **{k: v.astype(np.float32) for k, v in out.items()})
 
 
+INT8_DIMS = [(48, 40), (24, 48), (10, 24)]  # (out, in) per layer
+
+
+def _compiled_predict(c_path, func, X, workdir):
+    """Outputs of an emitted predict function (compiled with cc) for the rows of X."""
+    so = os.path.join(workdir, os.path.basename(c_path) + ".so")
+    subprocess.run(["cc", "-O2", "-shared", "-fPIC", c_path, "-o", so, "-lm"], check=True)
+    lib = C.CDLL(so)
+    fn = getattr(lib, func)
+    fn.argtypes = [C.c_void_p, C.c_void_p]
+    fn.restype = None
+    Y = []
+    for x in np.ascontiguousarray(X, np.float32):
+        y = np.zeros(INT8_DIMS[-1][0], np.float32)
+        fn(x.ctypes.data, y.ctypes.data)
+        Y.append(y)
+    return np.stack(Y)
+
+
+def gen_int8_export():
+    from dreamcompiler_b200 import int8_export as IE
+    R.set_seed(42)
+    ck = R.call("dream_ckpt_new")
+    layers = []
+    for i, (o, n) in enumerate(INT8_DIMS):
+        W, b = R.randn(o, n), R.randn(1, o)
+        R.call("dream_ckpt_add", ck, R.call("dream_str_create", f"fc{i + 1}.weight".encode()), W)
+        R.call("dream_ckpt_add", ck, R.call("dream_str_create", f"fc{i + 1}.bias".encode()), b)
+        layers.append((f"fc{i + 1}", R.data(W), R.data(b)[0]))
+    out_dir = os.path.join(HERE, "int8_export")
+    os.makedirs(out_dir, exist_ok=True)
+    X = np.random.default_rng(1).standard_normal((16, INT8_DIMS[0][1])).astype(np.float32)
+    with tempfile.TemporaryDirectory(dir=HERE) as td:
+        # relative prefix, so the emitted #include names the header alone
+        cwd = os.getcwd()
+        os.chdir(td)
+        try:
+            R.call("dream_export_c_header_int8", ck, R.call("dream_str_create", b"mlp_int8"),
+                   R.call("dream_str_create", b"mlp_predict_int8"))
+        finally:
+            os.chdir(cwd)
+        prefix = os.path.join(td, "mlp_int8")
+        Y = _compiled_predict(prefix + ".c", "mlp_predict_int8", X, td)
+        for ext in (".c", ".h"):
+            shutil.copy(prefix + ext, os.path.join(out_dir, "mlp_int8" + ext))
+        pc = os.path.join(td, "mlp_int8_pc")
+        IE.export_c_header_int8_per_channel(layers, pc, "mlp_predict_int8_pc")
+        Ypc = _compiled_predict(pc + ".c", "mlp_predict_int8_pc", X, td)
+    arrays = {"X": X, "Y": Y, "Ypc": Ypc}
+    for name, W, b in layers:
+        arrays[f"{name}_W"], arrays[f"{name}_b"] = W, b
+    np.savez_compressed(os.path.join(HERE, "int8_export.npz"), **arrays)
+
+
 if __name__ == "__main__":
     # optional arguments name the fixtures to regenerate (default: all)
     gens = {"gemm": gen_gemm, "flash": gen_flash, "linear": gen_linear, "tp": gen_tp, "gpt": gen_gpt,
-            "adamw": gen_adamw, "bmm": gen_bmm, "attn": gen_attn}
+            "adamw": gen_adamw, "bmm": gen_bmm, "attn": gen_attn, "int8_export": gen_int8_export}
     for name in sys.argv[1:] or list(gens):
         gens[name]()
     for f in sorted(os.listdir(HERE)):
