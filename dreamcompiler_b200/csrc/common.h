@@ -29,8 +29,9 @@ dgx_status cuda_status(cudaError_t e, const char* what);
 // cudaMalloc, reused across calls on the same stream order). Separate slots
 // for buffers that are live at the same time within one call: the GEMM's
 // split-K partial tiles (kScratchSplitK) while its operands may sit in the
-// general buffer (the 3xTF32 planes).
-constexpr int kScratchGeneral = 0, kScratchSplitK = 1, kScratchSlots = 2;
+// general buffer (the 3xTF32 planes); the convolution's im2col matrices
+// (kScratchConv) while its GEMMs use both.
+constexpr int kScratchGeneral = 0, kScratchSplitK = 1, kScratchConv = 2, kScratchSlots = 3;
 void* library_scratch_slot(int slot, size_t bytes, cudaStream_t s);
 void* library_scratch(size_t bytes, cudaStream_t s);  // the general slot
 

@@ -27,7 +27,7 @@ _SIG = {
     "tensor_get_grad": [TP], "zero_grad": [TP], "dream_set_seed": [TP], "dream_randn": [TP, TP],
     "dream_set_precision": [TP, C.c_int], "dream_enable_fp16": [], "tensor_matmul": [TP, TP],
     "dream_linear": [TP, TP, TP], "dream_linear_relu": [TP, TP, TP], "dream_bmm": [TP] * 6,
-    "dream_flash_attention": [TP] * 7, "dream_attention": [TP] * 6, "dream_attention_causal": [TP] * 6, "dream_tp_matmul_column": [TP] * 3, "tensor_mul": [TP, TP], "sum": [TP],
+    "dream_flash_attention": [TP] * 7, "dream_conv2d": [TP] * 7, "dream_conv2d_padded": [TP] * 9, "dream_attention": [TP] * 6, "dream_attention_causal": [TP] * 6, "dream_tp_matmul_column": [TP] * 3, "tensor_mul": [TP, TP], "sum": [TP],
     "backward": [TP],
 }
 _rt = None

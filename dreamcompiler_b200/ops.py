@@ -99,6 +99,33 @@ def gemm_batched(A: torch.Tensor, B: torch.Tensor, *, transA: bool = False, tran
     return out
 
 
+def conv2d(X: torch.Tensor, Kw: torch.Tensor, bias: Optional[torch.Tensor], KH: int, KW: int, *, pad: int = 0,
+           stride: int = 1, operands: torch.dtype = torch.float32) -> torch.Tensor:
+    """X [N, Cin, H, W] fp32, Kw [Cout, Cin*KH*KW] fp32 (row per output
+    channel), bias [Cout] or None -> Y [N, Cout, OH, OW] fp32. `operands`
+    float32 runs 3xTF32 GEMMs, bfloat16 bf16 ones."""
+    assert X.dtype == torch.float32 and Kw.dtype == torch.float32 and X.is_contiguous() and Kw.is_contiguous()
+    N, Cin, H, W = X.shape
+    Cout = Kw.shape[0]
+    OH, OW = (H + 2 * pad - KH) // stride + 1, (W + 2 * pad - KW) // stride + 1
+    Y = torch.empty(N, Cout, OH, OW, device=X.device, dtype=torch.float32)
+    L.call("dgx_conv2d_fwd", X.data_ptr(), Kw.data_ptr(), _ptr(bias), Y.data_ptr(), N, Cin, H, W, Cout, KH, KW, pad,
+           stride, _DT[operands], _stream(X))
+    return Y
+
+
+def conv2d_backward(X: torch.Tensor, Kw: torch.Tensor, dY: torch.Tensor, KH: int, KW: int, *, pad: int = 0,
+                    stride: int = 1, operands: torch.dtype = torch.float32):
+    """(dX, dK) of conv2d for the output gradient dY [N, Cout, OH, OW]."""
+    N, Cin, H, W = X.shape
+    Cout = Kw.shape[0]
+    dX = torch.empty_like(X)
+    dK = torch.empty_like(Kw)
+    L.call("dgx_conv2d_bwd", X.data_ptr(), Kw.data_ptr(), dY.contiguous().data_ptr(), dX.data_ptr(), dK.data_ptr(),
+           N, Cin, H, W, Cout, KH, KW, pad, stride, _DT[operands], 0, _stream(X))
+    return dX, dK
+
+
 def flash_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, causal: bool = True,
               scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
               lse: Optional[torch.Tensor] = None, want_lse: bool = True):

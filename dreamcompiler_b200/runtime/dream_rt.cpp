@@ -26,7 +26,7 @@
 
 namespace {
 
-enum class Fn { None, Matmul, Linear, LinearRelu, Bmm, Flash, Mul, Sum };
+enum class Fn { None, Matmul, Linear, LinearRelu, Bmm, Flash, Conv, Mul, Sum };
 
 struct FlashSaved;
 
@@ -43,7 +43,7 @@ struct TensorImpl {
   Fn fn;
   TensorImpl* parents[3];
   int nparents;
-  int meta[4];    // op dimensions (B,S,dk / batch,M,K,N)
+  int meta[8];    // op dimensions (B,S,dk,causal / batch,M,K,N / H,W,KH,KW,pad,stride,Cin,Cout)
   FlashSaved* flash;
 };
 
@@ -383,6 +383,78 @@ Tensor* dream_attention_causal(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t,
   return attention_impl("attention_causal", Q, K, V, batch_t, seq_t, dk_t, 1);
 }
 
+}  // extern "C"
+
+namespace {
+
+// dream_conv2d / dream_conv2d_padded: NCHW rows (N, Cin*H*W) and kernel
+// (Cout, Cin*KH*KW) as the reference stores them, one batched device
+// convolution (dgx_conv2d_fwd). The graph keeps input and kernel as parents
+// (the reference's lhs / rhs; bias is not differentiated there either).
+Tensor* conv_impl(const char* op, Tensor* input_, Tensor* kernel_, Tensor* bias_, Tensor* h_t, Tensor* w_t,
+                  Tensor* kh_t, Tensor* kw_t, int pad, int stride) {
+  if (!input_ || !kernel_ || !h_t || !w_t || !kh_t || !kw_t) {
+    report(op, "null arg");
+    return alloc_tensor(1, 1, 1, 1);
+  }
+  TensorImpl *x = impl(input_), *k = impl(kernel_), *b = bias_ ? impl(bias_) : nullptr;
+  const int H = (int)h_t->data[0], W = (int)w_t->data[0], KH = (int)kh_t->data[0], KW = (int)kw_t->data[0];
+  if (stride < 1) stride = 1;
+  if (pad < 0 || H <= 0 || W <= 0 || KH <= 0 || KW <= 0 || H + 2 * pad < KH || W + 2 * pad < KW) {
+    report(op, "kernel larger than input");
+    return alloc_tensor(1, 1, 1, 1);
+  }
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  const int N = x->d0, Cout = k->d0;
+  int Cin = x->d1 / (H * W);
+  if (Cin < 1) Cin = 1;
+  if ((long long)N * Cin * H * W > x->size || (long long)Cout * Cin * KH * KW > k->size) {
+    report(op, "input / kernel smaller than their geometry");
+    return alloc_tensor(1, 1, 1, 1);
+  }
+  TensorImpl* out = new_tensor(N, Cout * OH * OW, 1, 1);
+  set_parents(out, Fn::Conv, {x, k});
+  const int geo[8] = {H, W, KH, KW, pad, stride, Cin, Cout};
+  for (int i = 0; i < 8; ++i) out->meta[i] = geo[i];
+  if (!ensure_device()) return pub(out);
+  const dgx_dtype ab = gemm_type();
+  DevBuf dX((size_t)x->size * 4), dK((size_t)k->size * 4), dB((size_t)Cout * 4), dY((size_t)N * Cout * OH * OW * 4);
+  bool ok = dX.p && dK.p && dB.p && dY.p && upload(x, dX.p, DGX_F32) && upload(k, dK.p, DGX_F32);
+  if (ok && b) {
+    // bias entries past its size add nothing (conv_add_bias, conv.inc:5-10)
+    TensorImpl bb{};
+    std::vector<double> host((size_t)Cout, 0.0);
+    for (int i = 0; i < Cout && i < b->size; ++i) host[i] = b->data[i];
+    bb.data = host.data();
+    bb.size = Cout;
+    ok = upload(&bb, dB.p, DGX_F32) && cudaStreamSynchronize(g_stream) == cudaSuccess;
+  }
+  ok = ok && dgx_conv2d_fwd(dX.as<float>(), dK.as<float>(), b ? dB.as<float>() : nullptr, dY.as<float>(), N, Cin, H,
+                            W, Cout, KH, KW, pad, stride, ab, g_stream) == DGX_OK &&
+       download(dY.p, DGX_F32, out->data, (size_t)N * Cout * OH * OW, false);
+  if (!ok) report(op, dgx_last_error());
+  return pub(out);
+}
+
+}  // namespace
+
+extern "C" {
+
+// dream_conv2d (runtime/nn/conv.inc:12-110): valid convolution, stride 1.
+Tensor* dream_conv2d(Tensor* input, Tensor* kernel, Tensor* bias, Tensor* h_t, Tensor* w_t, Tensor* kh_t,
+                     Tensor* kw_t) {
+  return conv_impl("conv2d", input, kernel, bias, h_t, w_t, kh_t, kw_t, 0, 1);
+}
+
+// dream_conv2d_padded (runtime/nn/conv.inc:111-187): zero padding and stride.
+// Its backward is the gradient of this geometry (the reference's reuses the
+// unpadded one).
+Tensor* dream_conv2d_padded(Tensor* input, Tensor* kernel, Tensor* bias, Tensor* h_t, Tensor* w_t, Tensor* kh_t,
+                            Tensor* kw_t, Tensor* pad_t, Tensor* stride_t) {
+  return conv_impl("conv2d", input, kernel, bias, h_t, w_t, kh_t, kw_t, pad_t ? (int)pad_t->data[0] : 0,
+                   stride_t ? (int)stride_t->data[0] : 1);
+}
+
 Tensor* dream_tp_matmul_column(Tensor* X_, Tensor* W_, Tensor* gpus_t) {
   if (!X_ || !W_) {
     report("tp_matmul_column", "null operand");
@@ -533,6 +605,26 @@ bool bwd_bmm(TensorImpl* t) {
          download(gB.p, DGX_F32, b->grad, (size_t)B * K * N, true);
 }
 
+// "conv2d" backward (runtime/ops/autograd.inc:507-535): dK += dY . col^T,
+// dX += col2im(K^T . dY), both on the device in one call.
+bool bwd_conv(TensorImpl* t) {
+  TensorImpl *x = t->parents[0], *k = t->parents[1];
+  const int H = t->meta[0], W = t->meta[1], KH = t->meta[2], KW = t->meta[3], pad = t->meta[4], stride = t->meta[5];
+  const int Cin = t->meta[6], Cout = t->meta[7], N = x->d0;
+  const size_t nx = (size_t)N * Cin * H * W, nk = (size_t)Cout * Cin * KH * KW;
+  DevBuf dX((size_t)x->size * 4), dK((size_t)k->size * 4), dY((size_t)t->size * 4), gX(nx * 4), gK(nk * 4);
+  TensorImpl g{};
+  g.data = t->grad;
+  g.size = t->size;
+  if (!dX.p || !dK.p || !dY.p || !gX.p || !gK.p || !upload(x, dX.p, DGX_F32) || !upload(k, dK.p, DGX_F32) ||
+      !upload(&g, dY.p, DGX_F32))
+    return false;
+  if (dgx_conv2d_bwd(dX.as<float>(), dK.as<float>(), dY.as<float>(), gX.as<float>(), gK.as<float>(), N, Cin, H, W,
+                     Cout, KH, KW, pad, stride, gemm_type(), 0, g_stream) != DGX_OK)
+    return false;
+  return download(gX.p, DGX_F32, x->grad, nx, true) && download(gK.p, DGX_F32, k->grad, nk, true);
+}
+
 bool bwd_flash(TensorImpl* t) {
   FlashSaved* fs = t->flash;
   if (!fs) return false;
@@ -594,6 +686,10 @@ extern "C" Tensor* backward(Tensor* root_) {
       case Fn::Flash:
         op = "flash_attention";
         ok = ensure_device() && bwd_flash(t);
+        break;
+      case Fn::Conv:
+        op = "conv2d";
+        ok = ensure_device() && bwd_conv(t);
         break;
       case Fn::None:
         break;

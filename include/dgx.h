@@ -121,6 +121,31 @@ dgx_status dgx_gemm_batched(const void* A, const void* B, void* C, int batch, in
                             int transB, dgx_dtype ab_type, dgx_dtype c_type, float beta, void* stream);
 
 /*
+ * 2-D convolution, NCHW fp32 tensors as the reference stores them:
+ * X [N][Cin][H][W], Kw [Cout][Cin*KH*KW] (row = output channel), bias [Cout]
+ * (may be NULL), Y [N][Cout][OH][OW], OH = (H + 2*pad - KH)/stride + 1.
+ * One tensor-core GEMM for the whole batch over a positions-major im2col
+ * matrix (library scratch, dgx_conv2d_workspace_size bytes). ab_type DGX_F32
+ * runs 3xTF32, DGX_BF16 bf16 operands (fp32 accumulate either way).
+ * Replaces dream_conv2d (runtime/nn/conv.inc:12-110, pad 0, stride 1) and
+ * dream_conv2d_padded (:111-187), im2col (runtime/nn/im2col.inc:2-13).
+ */
+dgx_status dgx_conv2d_fwd(const float* X, const float* Kw, const float* bias, float* Y, int N, int Cin, int H, int W,
+                          int Cout, int KH, int KW, int pad, int stride, dgx_dtype ab_type, void* stream);
+/*
+ * Convolution backward: dK = sum_n dY_n . col_n^T and dX = col2im(K^T . dY)
+ * (either may be NULL to skip it); accumulate = 1 adds into dX / dK, as
+ * autograd's `grad +=` does. Replaces the "conv2d" backward branch
+ * (runtime/ops/autograd.inc:507-535) and col2im (runtime/nn/im2col.inc:14-25);
+ * with pad / stride it is the gradient of dgx_conv2d_fwd's geometry.
+ */
+dgx_status dgx_conv2d_bwd(const float* X, const float* Kw, const float* dY, float* dX, float* dK, int N, int Cin, int H,
+                          int W, int Cout, int KH, int KW, int pad, int stride, dgx_dtype ab_type, int accumulate,
+                          void* stream);
+size_t dgx_conv2d_workspace_size(int N, int Cin, int H, int W, int Cout, int KH, int KW, int pad, int stride,
+                                 dgx_dtype ab_type);
+
+/*
  * FlashAttention forward. Q, K, V, O: [BH][S][D] (heads folded into the batch,
  * as dream_flash_attention's `(B, S*dk)` layout), dtype DGX_BF16.
  * LSE [BH][S] fp32 receives the natural-log row log-sum-exp of scale*QK^T

@@ -56,6 +56,10 @@ Tensor* dream_attention(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor
                         Tensor* dk_t);                             /* training.inc:177 */
 Tensor* dream_attention_causal(Tensor* Q, Tensor* K, Tensor* V, Tensor* batch_t, Tensor* seq_t,
                                Tensor* dk_t);                      /* training.inc:222 */
+Tensor* dream_conv2d(Tensor* input, Tensor* kernel, Tensor* bias, Tensor* h_t, Tensor* w_t, Tensor* kh_t,
+                     Tensor* kw_t);                                 /* conv.inc:12 */
+Tensor* dream_conv2d_padded(Tensor* input, Tensor* kernel, Tensor* bias, Tensor* h_t, Tensor* w_t, Tensor* kh_t,
+                            Tensor* kw_t, Tensor* pad_t, Tensor* stride_t); /* conv.inc:116 */
 Tensor* dream_tp_matmul_column(Tensor* X, Tensor* W, Tensor* gpus_t); /* training.inc:1604 */
 
 /* the two ops programs use to seed a gradient: backward(sum(Y * G)) */

@@ -392,6 +392,79 @@ void orc_attention_bwd(const double* Q, const double* K, const double* V, const 
   }
 }
 
+// ---------------------------------------------------------------- convolution
+// dream_conv2d / dream_conv2d_padded (runtime/nn/conv.inc:12-187): per
+// sample, col = im2col(zero-padded input, stride) [Cin*KH*KW][OH*OW]
+// (runtime/nn/im2col.inc:2-13, conv.inc:151-163), Y_n = K . col (f64),
+// then + bias[co] on every position of channel co.
+static void orc_im2col(const double* x, double* col, int Cin, int H, int W, int KH, int KW, int pad, int stride,
+                       int OH, int OW) {
+  int r = 0;
+  for (int ci = 0; ci < Cin; ++ci)
+    for (int kh = 0; kh < KH; ++kh)
+      for (int kw = 0; kw < KW; ++kw, ++r)
+        for (int oh = 0; oh < OH; ++oh)
+          for (int ow = 0; ow < OW; ++ow) {
+            const int h = oh * stride - pad + kh, w = ow * stride - pad + kw;
+            col[(size_t)r * OH * OW + oh * OW + ow] =
+                (h >= 0 && h < H && w >= 0 && w < W) ? x[((size_t)ci * H + h) * W + w] : 0.0;
+          }
+}
+
+void orc_conv2d_fwd(const double* X, const double* K, const double* bias, double* Y, int N, int Cin, int H, int W,
+                    int Cout, int KH, int KW, int pad, int stride) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  const int ckk = Cin * KH * KW, ohw = OH * OW;
+#pragma omp parallel for schedule(dynamic)
+  for (int n = 0; n < N; ++n) {
+    std::vector<double> col((size_t)ckk * ohw);
+    orc_im2col(X + (size_t)n * Cin * H * W, col.data(), Cin, H, W, KH, KW, pad, stride, OH, OW);
+    double* y = Y + (size_t)n * Cout * ohw;
+    orc_gemm_f64(K, col.data(), y, Cout, ckk, ohw);
+    if (bias)
+      for (int co = 0; co < Cout; ++co)
+        for (int j = 0; j < ohw; ++j) y[(size_t)co * ohw + j] += bias[co];
+  }
+}
+
+// "conv2d" backward (runtime/ops/autograd.inc:507-535), accumulating:
+// dK[co][r] += sum_j dY_n[co][j] col_n[r][j]; dX_n += col2im(K^T . dY_n)
+// (runtime/nn/im2col.inc:14-25), with the forward's pad / stride geometry.
+void orc_conv2d_bwd(const double* X, const double* K, const double* dY, double* dX, double* dK, int N, int Cin,
+                    int H, int W, int Cout, int KH, int KW, int pad, int stride) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  const int ckk = Cin * KH * KW, ohw = OH * OW;
+  std::vector<double> col((size_t)ckk * ohw), dcol((size_t)ckk * ohw);
+  for (int n = 0; n < N; ++n) {
+    const double* go = dY + (size_t)n * Cout * ohw;
+    orc_im2col(X + (size_t)n * Cin * H * W, col.data(), Cin, H, W, KH, KW, pad, stride, OH, OW);
+#pragma omp parallel for schedule(static)
+    for (int co = 0; co < Cout; ++co)
+      for (int r = 0; r < ckk; ++r) {
+        double s = 0;
+        for (int j = 0; j < ohw; ++j) s += go[(size_t)co * ohw + j] * col[(size_t)r * ohw + j];
+        dK[(size_t)co * ckk + r] += s;
+      }
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < ckk; ++r)
+      for (int j = 0; j < ohw; ++j) {
+        double s = 0;
+        for (int co = 0; co < Cout; ++co) s += K[(size_t)co * ckk + r] * go[(size_t)co * ohw + j];
+        dcol[(size_t)r * ohw + j] = s;
+      }
+    double* dx = dX + (size_t)n * Cin * H * W;
+    int r = 0;
+    for (int ci = 0; ci < Cin; ++ci)
+      for (int kh = 0; kh < KH; ++kh)
+        for (int kw = 0; kw < KW; ++kw, ++r)
+          for (int oh = 0; oh < OH; ++oh)
+            for (int ow = 0; ow < OW; ++ow) {
+              const int h = oh * stride - pad + kh, w = ow * stride - pad + kw;
+              if (h >= 0 && h < H && w >= 0 && w < W) dx[((size_t)ci * H + h) * W + w] += dcol[(size_t)r * ohw + oh * OW + ow];
+            }
+  }
+}
+
 // ---------------------------------------------------------------- int8
 // Per-tensor symmetric quantiser of export_c_header_int8
 // (runtime/nn/training.inc:3668-3692): scale = max|w|/127 (1 if ~0),

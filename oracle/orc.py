@@ -194,6 +194,32 @@ def attention_bwd(Q, K, V, dO, causal=True):
     return dQ, dK, dV
 
 
+# ---------------------------------------------------------------- convolution
+def conv_out(H, W, KH, KW, pad=0, stride=1):
+    return (H + 2 * pad - KH) // stride + 1, (W + 2 * pad - KW) // stride + 1
+
+
+def conv2d_fwd(X, K, bias, KH, KW, pad=0, stride=1):
+    """X [N, Cin, H, W], K [Cout, Cin*KH*KW], bias [Cout] or None -> Y [N, Cout, OH, OW] (f64)."""
+    X, K = (np.ascontiguousarray(t, np.float64) for t in (X, K))
+    N, Cin, H, W = X.shape
+    Cout = K.shape[0]
+    OH, OW = conv_out(H, W, KH, KW, pad, stride)
+    Y = np.empty((N, Cout, OH, OW))
+    bp = None if bias is None else _p(np.ascontiguousarray(bias, np.float64))
+    lib().orc_conv2d_fwd(_p(X), _p(K), bp, _p(Y), N, Cin, H, W, Cout, KH, KW, pad, stride)
+    return Y
+
+
+def conv2d_bwd(X, K, dY, KH, KW, pad=0, stride=1):
+    X, K, dY = (np.ascontiguousarray(t, np.float64) for t in (X, K, dY))
+    N, Cin, H, W = X.shape
+    Cout = K.shape[0]
+    dX, dK = np.zeros_like(X), np.zeros_like(K)
+    lib().orc_conv2d_bwd(_p(X), _p(K), _p(dY), _p(dX), _p(dK), N, Cin, H, W, Cout, KH, KW, pad, stride)
+    return dX, dK
+
+
 # ---------------------------------------------------------------- int8
 def quantize_per_tensor(w: np.ndarray):
     w = np.ascontiguousarray(w, np.float64)

@@ -59,6 +59,8 @@ _SIG = {
     "dream_adamw_update": [TP, TP, TP, TP, TP, TP],
     "zero_grad": [TP],
     "dream_str_create": [C.c_char_p],
+    "dream_conv2d": [TP] * 7,
+    "dream_conv2d_padded": [TP] * 9,
     "dream_ckpt_new": [],
     "dream_ckpt_add": [TP, TP, TP],
     "dream_export_c_header_int8": [TP, TP, TP],

@@ -23,6 +23,8 @@ output comes from the reference's own ops:
              runtime/ops/autograd.inc:549-574)
   attn.npz   dream_attention and dream_attention_causal + their backward
              (runtime/nn/training.inc:177-263, runtime/ops/autograd.inc:675-778)
+  conv.npz   dream_conv2d + its "conv2d" backward, dream_conv2d_padded forward
+             (runtime/nn/conv.inc:12-187, runtime/ops/autograd.inc:507-535)
   int8_export/mlp_int8.{c,h} + int8_export.npz
              a 3-layer MLP checkpoint exported by the reference's own
              export_c_header_int8 (runtime/nn/training.inc:3494-3817); inputs
@@ -261,6 +263,30 @@ def gen_attn():
     np.savez_compressed(os.path.join(HERE, "attn.npz"), **{k: v.astype(np.float32) for k, v in out.items()})
 
 
+# (N, Cin, H, W, Cout, KH, KW) for conv2d; plus (pad, stride) for the padded form
+CONV_CFGS = [(2, 3, 8, 9, 4, 3, 3), (1, 2, 7, 5, 3, 2, 4), (3, 4, 10, 10, 8, 1, 1), (2, 5, 12, 11, 6, 5, 3)]
+CONV_PAD_CFGS = [(2, 3, 8, 9, 4, 3, 3, 1, 1), (1, 2, 9, 7, 3, 3, 3, 1, 2), (2, 4, 11, 10, 5, 4, 2, 2, 3)]
+
+
+def gen_conv():
+    out = {}
+    R.set_seed(13)
+    for (N, Cin, H, W, Cout, KH, KW) in CONV_CFGS:
+        X, K, b = R.randn(N, Cin * H * W), R.randn(Cout, Cin * KH * KW), R.randn(1, Cout)
+        Y = R.call("dream_conv2d", X, K, b, *(R.scalar(v) for v in (H, W, KH, KW)))
+        OH, OW = H - KH + 1, W - KW + 1
+        G = seeded_backward(Y, (N, Cout * OH * OW))
+        t = f"{N}_{Cin}_{H}_{W}_{Cout}_{KH}_{KW}"
+        out[f"X_{t}"], out[f"K_{t}"], out[f"b_{t}"], out[f"G_{t}"] = R.data(X), R.data(K), R.data(b)[0], G
+        out[f"Y_{t}"], out[f"dX_{t}"], out[f"dK_{t}"] = R.data(Y), R.grad(X), R.grad(K)
+    for (N, Cin, H, W, Cout, KH, KW, pad, stride) in CONV_PAD_CFGS:
+        X, K, b = R.randn(N, Cin * H * W), R.randn(Cout, Cin * KH * KW), R.randn(1, Cout)
+        Y = R.call("dream_conv2d_padded", X, K, b, *(R.scalar(v) for v in (H, W, KH, KW, pad, stride)))
+        t = f"p{N}_{Cin}_{H}_{W}_{Cout}_{KH}_{KW}_{pad}_{stride}"
+        out[f"X_{t}"], out[f"K_{t}"], out[f"b_{t}"], out[f"Y_{t}"] = R.data(X), R.data(K), R.data(b)[0], R.data(Y)
+    np.savez_compressed(os.path.join(HERE, "conv.npz"), **{k: v.astype(np.float32) for k, v in out.items()})
+
+
 INT8_DIMS = [(48, 40), (24, 48), (10, 24)]  # (out, in) per layer
 
 
@@ -318,7 +344,8 @@ def gen_int8_export():
 if __name__ == "__main__":
     # optional arguments name the fixtures to regenerate (default: all)
     gens = {"gemm": gen_gemm, "flash": gen_flash, "linear": gen_linear, "tp": gen_tp, "gpt": gen_gpt,
-            "adamw": gen_adamw, "bmm": gen_bmm, "attn": gen_attn, "int8_export": gen_int8_export}
+            "adamw": gen_adamw, "bmm": gen_bmm, "attn": gen_attn, "int8_export": gen_int8_export,
+            "conv": gen_conv}
     for name in sys.argv[1:] or list(gens):
         gens[name]()
     for f in sorted(os.listdir(HERE)):

@@ -204,3 +204,52 @@ def test_attention_and_backward(orc, golden, cfg, causal):
         assert normwise(x, g[f"{name}_{t}"]) < F32_STORED, name
     if causal:  # the causal backward equals the flash backward
         assert normwise(orc.flash_bwd(Q, K, V, G)[0], dQ) < 1e-9
+
+
+CONV_CFGS = [(2, 3, 8, 9, 4, 3, 3), (1, 2, 7, 5, 3, 2, 4), (3, 4, 10, 10, 8, 1, 1), (2, 5, 12, 11, 6, 5, 3)]
+CONV_PAD_CFGS = [(2, 3, 8, 9, 4, 3, 3, 1, 1), (1, 2, 9, 7, 3, 3, 3, 1, 2), (2, 4, 11, 10, 5, 4, 2, 2, 3)]
+
+
+@pytest.mark.parametrize("cfg", CONV_CFGS)
+def test_conv2d_and_backward(orc, golden, cfg):
+    """dream_conv2d and its "conv2d" backward (reference runtime outputs)."""
+    g = golden("conv")
+    N, Cin, H, W, Cout, KH, KW = cfg
+    t = "_".join(map(str, cfg))
+    X = g[f"X_{t}"].reshape(N, Cin, H, W)
+    K, b = g[f"K_{t}"], g[f"b_{t}"]
+    OH, OW = orc.conv_out(H, W, KH, KW)
+    G = g[f"G_{t}"].reshape(N, Cout, OH, OW)
+    assert normwise(orc.conv2d_fwd(X, K, b, KH, KW), g[f"Y_{t}"].reshape(N, Cout, OH, OW)) < F32_STORED
+    dX, dK = orc.conv2d_bwd(X, K, G, KH, KW)
+    assert normwise(dX, g[f"dX_{t}"].reshape(X.shape)) < F32_STORED
+    assert normwise(dK, g[f"dK_{t}"]) < F32_STORED
+
+
+@pytest.mark.parametrize("cfg", CONV_PAD_CFGS)
+def test_conv2d_padded(orc, golden, cfg):
+    g = golden("conv")
+    N, Cin, H, W, Cout, KH, KW, pad, stride = cfg
+    t = "p" + "_".join(map(str, cfg))
+    X = g[f"X_{t}"].reshape(N, Cin, H, W)
+    OH, OW = orc.conv_out(H, W, KH, KW, pad, stride)
+    Y = orc.conv2d_fwd(X, g[f"K_{t}"], g[f"b_{t}"], KH, KW, pad, stride)
+    assert normwise(Y, g[f"Y_{t}"].reshape(N, Cout, OH, OW)) < F32_STORED
+
+
+def test_conv2d_backward_is_the_gradient(orc):
+    """With padding and stride (where the reference's backward reuses the
+    unpadded geometry), the oracle's backward is checked by finite
+    differences of its forward: <dY, conv(X + e*V)> - <dY, conv(X - e*V)>."""
+    rng = np.random.default_rng(3)
+    N, Cin, H, W, Cout, KH, KW, pad, stride = 2, 3, 7, 6, 4, 3, 2, 1, 2
+    X = rng.standard_normal((N, Cin, H, W))
+    K = rng.standard_normal((Cout, Cin * KH * KW))
+    OH, OW = orc.conv_out(H, W, KH, KW, pad, stride)
+    G = rng.standard_normal((N, Cout, OH, OW))
+    dX, dK = orc.conv2d_bwd(X, K, G, KH, KW, pad, stride)
+    VX, VK = rng.standard_normal(X.shape), rng.standard_normal(K.shape)
+    e = 1e-6
+    f = lambda x, k: float((orc.conv2d_fwd(x, k, None, KH, KW, pad, stride) * G).sum())
+    assert abs((f(X + e * VX, K) - f(X - e * VX, K)) / (2 * e) - (dX * VX).sum()) < 1e-5 * abs((dX * VX).sum()) + 1e-6
+    assert abs((f(X, K + e * VK) - f(X, K - e * VK)) / (2 * e) - (dK * VK).sum()) < 1e-5 * abs((dK * VK).sum()) + 1e-6

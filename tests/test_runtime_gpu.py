@@ -130,3 +130,30 @@ def test_attention_programs_match_reference(R, golden):
             assert normwise(R.data(O, shape), g[f"O_{t}"]) < 2e-2, t
             for name, x in (("dQ", Q), ("dK", K), ("dV", V)):
                 assert normwise(R.grad(x, shape), g[f"{name}_{t}"]) < 2e-2, (t, name)
+
+
+def test_conv_programs_match_reference(R, golden):
+    """set_seed(13); X, K, b = randn; Y = conv2d(X, K, b, H, W, KH, KW);
+    backward(sum(Y * randn)); then conv2d_padded forwards — the generator's
+    program, replayed on the device path."""
+    g = golden("conv")
+    R.call("dream_set_seed", R.scalar(13))
+    for (N, Cin, H, W, Cout, KH, KW) in [(2, 3, 8, 9, 4, 3, 3), (1, 2, 7, 5, 3, 2, 4), (3, 4, 10, 10, 8, 1, 1),
+                                         (2, 5, 12, 11, 6, 5, 3)]:
+        t = f"{N}_{Cin}_{H}_{W}_{Cout}_{KH}_{KW}"
+        X = R.call("dream_randn", R.scalar(N), R.scalar(Cin * H * W))
+        K = R.call("dream_randn", R.scalar(Cout), R.scalar(Cin * KH * KW))
+        b = R.call("dream_randn", R.scalar(1), R.scalar(Cout))
+        Y = R.call("dream_conv2d", X, K, b, *(R.scalar(v) for v in (H, W, KH, KW)))
+        seeded_backward(R, Y, (N, Cout * (H - KH + 1) * (W - KW + 1)))
+        assert normwise(R.data(Y), g[f"Y_{t}"]) < 1e-4
+        assert normwise(R.grad(X), g[f"dX_{t}"]) < 1e-4
+        assert normwise(R.grad(K), g[f"dK_{t}"]) < 1e-4
+    for (N, Cin, H, W, Cout, KH, KW, pad, stride) in [(2, 3, 8, 9, 4, 3, 3, 1, 1), (1, 2, 9, 7, 3, 3, 3, 1, 2),
+                                                      (2, 4, 11, 10, 5, 4, 2, 2, 3)]:
+        t = f"p{N}_{Cin}_{H}_{W}_{Cout}_{KH}_{KW}_{pad}_{stride}"
+        X = R.call("dream_randn", R.scalar(N), R.scalar(Cin * H * W))
+        K = R.call("dream_randn", R.scalar(Cout), R.scalar(Cin * KH * KW))
+        b = R.call("dream_randn", R.scalar(1), R.scalar(Cout))
+        Y = R.call("dream_conv2d_padded", X, K, b, *(R.scalar(v) for v in (H, W, KH, KW, pad, stride)))
+        assert normwise(R.data(Y), g[f"Y_{t}"]) < 1e-4
