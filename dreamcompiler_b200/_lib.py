@@ -42,8 +42,8 @@ SIGNATURES = {
     "dgx_gemm_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
     "dgx_gemm_set_algo": (_i, [_i]),
     "dgx_bmm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
-    "dgx_conv2d_fwd": (_i, [_vp, _vp, _vp, _vp] + [_i] * 11 + [_vp]),
-    "dgx_conv2d_bwd": (_i, [_vp, _vp, _vp, _vp, _vp] + [_i] * 11 + [_i, _vp]),
+    "dgx_conv2d_fwd": (_i, [_vp] * 4 + [_i] * 10 + [_vp]),
+    "dgx_conv2d_bwd": (_i, [_vp] * 5 + [_i] * 11 + [_vp]),
     "dgx_conv2d_workspace_size": (_sz, [_i] * 10),
     "dgx_dense_q": (_i, [_vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "dgx_gemm_batched": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, C.c_longlong, C.c_longlong, C.c_longlong,

@@ -35,6 +35,17 @@ def test_python_binding_covers_header():
     assert set(declared("dgx.h")) <= set(_lib.SIGNATURES)
 
 
+def test_python_binding_arity_matches_header():
+    """Every ctypes signature has as many parameters as its prototype."""
+    from dreamcompiler_b200 import _lib
+    text = re.sub(r"/\*.*?\*/", "", open(os.path.join(INCLUDE, "dgx.h")).read(), flags=re.S)
+    protos = dict(re.findall(r"\b(dgx_\w+)\s*\(([^)]*)\)\s*;", text))
+    assert len(protos) >= 15
+    for name, params in protos.items():
+        n = 0 if params.strip() in ("", "void") else params.count(",") + 1
+        assert len(_lib.SIGNATURES[name][1]) == n, f"{name}: binding has {len(_lib.SIGNATURES[name][1])}, header {n}"
+
+
 def test_dream_runtime_exports(lib):
     from dreamcompiler_b200 import dream_rt
     rt = dream_rt.load()
