@@ -61,6 +61,11 @@ constexpr int NUM_THREADS = 384;  // WG0: softmax A, WG1: softmax B, WG2: TMA wa
 // setmaxnreg split (per thread): 2 x 224 + 56 = 504 <= 3 x 168 (65536 / 384 rounded down to 8).
 constexpr uint32_t REG_SOFTMAX = 224, REG_CTRL = 56;
 constexpr float RESCALE_LOG2 = 8.0f;
+// Exponential column after which a softmax group hands the MUFU turn over.
+#ifndef DGX_FWD_TURN_AT
+#define DGX_FWD_TURN_AT 80
+#endif
+constexpr int TURN_AT = DGX_FWD_TURN_AT;
 
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int SM_Q = 0;                               // Q_A, Q_B (two buffers: next item's Q)
@@ -344,12 +349,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ps[(c >> 1) & 7] += e0 + e1;
           p[c / 2] = pack_bf16x2_fast(e0, e1);
         };
-        static_for<0, BLOCK_N, 2>(step);
-        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-        if (trc) FWD_TRACE(tb + 3);
-        // Hand the turn to the other group (B only while A has tiles left).
+        // Hand the turn to the other group (B only while A has tiles left)
+        // before the last columns: the other group's wait ends while these
+        // exponentials still keep MUFU busy, so the barrier's hand-off
+        // latency does not leave it idle.
+        static_for<0, TURN_AT, 2>(step);
         __syncwarp();
         if (lane == 0 && (x == 0 || j + 1 < I.nA)) mbar_arrive(&bars->turn[x ^ 1]);
+        static_for<TURN_AT, BLOCK_N, 2>(step);
+        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        if (trc) FWD_TRACE(tb + 3);
         l_run = l_run * factor + rs;
         if (j > 0) {
           // PV(j-1) must be done: it reads the P buffer and accumulates O.
