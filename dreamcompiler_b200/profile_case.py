@@ -5,6 +5,9 @@ two launches of each kernel).
     python -m dreamcompiler_b200.profile_case flash --bh 16      # S=2048, D=64
     python -m dreamcompiler_b200.profile_case gemm --n 4096
     python -m dreamcompiler_b200.profile_case w8 --batch 1 --mode 1   # int8 layer, N=K=4096
+    python -m dreamcompiler_b200.profile_case gemm_f32 --n 1024       # 3xTF32
+    python -m dreamcompiler_b200.profile_case conv --batch 8          # 64 -> 128 channels, 3x3, 32x32
+    python -m dreamcompiler_b200.profile_case gpt                     # one config-3 training step
 """
 from __future__ import annotations
 
@@ -16,7 +19,7 @@ def main() -> None:
     import dreamcompiler_b200 as dgx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["flash", "gemm", "w8"])
+    ap.add_argument("kind", choices=["flash", "gemm", "w8", "gemm_f32", "conv", "gpt"])
     ap.add_argument("--bh", type=int, default=16)
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--dim", type=int, default=64)
@@ -38,6 +41,28 @@ def main() -> None:
         C = torch.empty(a.n, a.n, device="cuda", dtype=torch.bfloat16)
         for _ in range(a.reps):
             dgx.gemm(A, B, out=C)
+    elif a.kind == "gemm_f32":
+        A, B, dC = (torch.randn(a.n, a.n, device="cuda", generator=g) for _ in range(3))
+        for _ in range(a.reps):
+            dgx.gemm(A, B)
+            dgx.gemm(dC, B, transB=True)
+            dgx.gemm(A, dC, transA=True)
+    elif a.kind == "conv":
+        X = torch.randn(a.batch, 64, 32, 32, device="cuda", generator=g)
+        Kw = torch.randn(128, 64 * 9, device="cuda", generator=g) / 24.0
+        b = torch.randn(128, device="cuda", generator=g)
+        for _ in range(a.reps):
+            Y = dgx.conv2d(X, Kw, b, 3, 3, pad=1, operands=torch.bfloat16)
+            dgx.conv2d_backward(X, Kw, Y, 3, 3, pad=1, operands=torch.bfloat16)
+    elif a.kind == "gpt":
+        from dreamcompiler_b200.gpt import GPT, GPTConfig
+        cfg = GPTConfig()
+        model = GPT(cfg, device="cuda", seed=0)
+        gt = torch.Generator().manual_seed(3)
+        tok = torch.randint(0, cfg.vocab, (cfg.batch * cfg.seq_len,), generator=gt, dtype=torch.int32)
+        model.set_batch(tok, torch.randint(0, cfg.vocab, tok.shape, generator=gt, dtype=torch.int32))
+        for _ in range(a.reps):
+            model.step()
     else:
         X = torch.randn(a.batch, a.n, device="cuda", generator=g)
         W = torch.randint(-127, 128, (a.n, a.n), device="cuda", dtype=torch.int8, generator=g)
