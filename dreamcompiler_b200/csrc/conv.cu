@@ -44,26 +44,31 @@ struct ConvGeom {
 
 // colT[p][r] = x[n][ci][oh*s - pad + kh][ow*s - pad + kw] (0 outside the
 // image, and 0 in the pitch padding r >= ckk), p = n*OH*OW + oh*OW + ow,
-// r = (ci*KH + kh)*KW + kw. One thread per element of colT, consecutive
-// threads along r (coalesced stores; the gathered loads hit L1/L2).
+// r = (ci*KH + kh)*KW + kw. One warp per position row p (its image
+// coordinates computed once), lanes along r: coalesced stores, and the
+// gathered loads of neighbouring taps hit the same lines in L1/L2.
 template <typename T>
 __global__ void im2col_rows_kernel(const float* __restrict__ x, T* __restrict__ col, ConvGeom g) {
-  const long long total = (long long)g.N * g.OH * g.OW * g.ldk;
+  const int rows = g.N * g.OH * g.OW;
   const int kk = g.KH * g.KW, ohw = g.OH * g.OW;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long p = i / g.ldk;
-    const int r = (int)(i - p * g.ldk);
-    float v = 0.f;
-    if (r < g.ckk) {
-      const int n = (int)(p / ohw), rem = (int)(p - (long long)n * ohw);
-      const int oh = rem / g.OW, ow = rem - oh * g.OW;
-      const int ci = r / kk, t = r - ci * kk;
-      const int kh = t / g.KW, kw = t - kh * g.KW;
-      const int h = oh * g.stride - g.pad + kh, w = ow * g.stride - g.pad + kw;
-      if (h >= 0 && h < g.H && w >= 0 && w < g.W) v = x[(((size_t)n * g.Cin + ci) * g.H + h) * g.W + w];
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < rows; p += warps) {
+    const int n = p / ohw, rem = p - n * ohw;
+    const int oh = rem / g.OW, ow = rem - oh * g.OW;
+    const int h0 = oh * g.stride - g.pad, w0 = ow * g.stride - g.pad;
+    const float* xn = x + (size_t)n * g.Cin * g.H * g.W;
+    T* out = col + (size_t)p * g.ldk;
+    for (int r = lane; r < g.ldk; r += 32) {
+      float v = 0.f;
+      if (r < g.ckk) {
+        const int ci = r / kk, t = r - ci * kk;
+        const int kh = t / g.KW, kw = t - kh * g.KW;
+        const int h = h0 + kh, w = w0 + kw;
+        if (h >= 0 && h < g.H && w >= 0 && w < g.W) v = __ldg(xn + ((size_t)ci * g.H + h) * g.W + w);
+      }
+      out[r] = from_f32<T>(v);
     }
-    col[i] = from_f32<T>(v);
   }
 }
 
@@ -103,34 +108,32 @@ __global__ void transpose_kernel(const float* __restrict__ in, Tout* __restrict_
 // dX[n][ci][h][w] (+)= sum over the window taps (kh, kw) whose output
 // position (oh, ow) = ((h + pad - kh)/s, (w + pad - kw)/s) is integral and in
 // range of dcolT[n*OHW + oh*OW + ow][(ci*KH + kh)*KW + kw]; taps in order.
+// blockIdx.y walks the (n, ci) planes, threads the H*W pixels of a plane.
 __global__ void col2im_gather_kernel(const float* __restrict__ dcol, float* __restrict__ dx, ConvGeom g,
                                      int accumulate) {
-  const long long total = (long long)g.N * g.Cin * g.H * g.W;
-  const int kk = g.KH * g.KW;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int w = (int)(i % g.W);
-    long long t = i / g.W;
-    const int h = (int)(t % g.H);
-    t /= g.H;
-    const int ci = (int)(t % g.Cin);
-    const int n = (int)(t / g.Cin);
-    float s = 0.f;
-    for (int kh = 0; kh < g.KH; ++kh) {
-      const int hh = h + g.pad - kh;
-      if (hh < 0 || hh % g.stride) continue;
-      const int oh = hh / g.stride;
-      if (oh >= g.OH) continue;
-      for (int kw = 0; kw < g.KW; ++kw) {
-        const int ww = w + g.pad - kw;
-        if (ww < 0 || ww % g.stride) continue;
-        const int ow = ww / g.stride;
-        if (ow >= g.OW) continue;
-        const size_t p = ((size_t)n * g.OH + oh) * g.OW + ow;
-        s += dcol[p * g.ldk + ci * kk + kh * g.KW + kw];
+  const int kk = g.KH * g.KW, hw_n = g.H * g.W, planes = g.N * g.Cin;
+  for (int pc = blockIdx.y; pc < planes; pc += gridDim.y) {
+    const int n = pc / g.Cin, ci = pc - n * g.Cin;
+    const float* dc = dcol + (size_t)n * g.OH * g.OW * g.ldk + ci * kk;
+    float* dxp = dx + (size_t)pc * hw_n;
+    for (int hw = blockIdx.x * blockDim.x + threadIdx.x; hw < hw_n; hw += gridDim.x * blockDim.x) {
+      const int h = hw / g.W, w = hw - h * g.W;
+      float s = 0.f;
+      for (int kh = 0; kh < g.KH; ++kh) {
+        const int hh = h + g.pad - kh;
+        if (hh < 0 || hh % g.stride) continue;
+        const int oh = hh / g.stride;
+        if (oh >= g.OH) continue;
+        for (int kw = 0; kw < g.KW; ++kw) {
+          const int ww = w + g.pad - kw;
+          if (ww < 0 || ww % g.stride) continue;
+          const int ow = ww / g.stride;
+          if (ow >= g.OW) continue;
+          s += dc[(size_t)(oh * g.OW + ow) * g.ldk + kh * g.KW + kw];
+        }
       }
+      dxp[hw] = accumulate ? dxp[hw] + s : s;
     }
-    dx[i] = accumulate ? dx[i] + s : s;
   }
 }
 
@@ -169,6 +172,8 @@ dgx_status make_geom(const char* op, int N, int Cin, int H, int W, int Cout, int
                      W + 2 * pad);
   const long long ckk = (long long)Cin * KH * KW;
   if (ckk > (1 << 30)) return set_error(DGX_EINVAL, "%s: Cin*KH*KW too large", op);
+  if ((long long)N * g->OH * g->OW >= (1LL << 31) || (long long)N * Cin >= (1LL << 31) || (long long)H * W >= (1LL << 31))
+    return set_error(DGX_EINVAL, "%s: too many output positions", op);
   g->ckk = (int)ckk;
   g->ldk = round8(g->ckk);
   g->ldo = round8(Cout);
@@ -217,7 +222,7 @@ dgx_status dgx_conv2d_fwd(const float* X, const float* Kw, const float* bias, fl
   void* colT = ws;
   float* yT = (float*)(ws + ((rows * g.ldk * esz + 255) & ~size_t(255)));
   void* kpad = (char*)yT + ((rows * g.ldo * 4 + 255) & ~size_t(255)) + ((rows * g.ldk * 4 + 255) & ~size_t(255));
-  const int ib = blocks_for(rows * g.ldk, 256);
+  const int ib = blocks_for(rows * 32, 256);  // a warp per position row
   if (ab_type == DGX_BF16) {
     im2col_rows_kernel<__nv_bfloat16><<<ib, 256, 0, s>>>(X, (__nv_bfloat16*)colT, g);
     pad_rows_kernel<__nv_bfloat16><<<blocks_for((long long)Cout * g.ldk, 256), 256, 0, s>>>(
@@ -274,7 +279,7 @@ dgx_status dgx_conv2d_bwd(const float* X, const float* Kw, const float* dY, floa
   if (e != cudaSuccess) return cuda_status(e, "dgx_conv2d_bwd transpose");
   if (dK) {
     // dK[Cout][ckk] (+)= dYT^T . colT: A = dYT stored [K = rows][M = Cout].
-    const int ib = blocks_for(rows * g.ldk, 256);
+    const int ib = blocks_for(rows * 32, 256);  // a warp per position row
     if (ab_type == DGX_BF16)
       im2col_rows_kernel<__nv_bfloat16><<<ib, 256, 0, s>>>(X, (__nv_bfloat16*)colT, g);
     else
@@ -296,7 +301,9 @@ dgx_status dgx_conv2d_bwd(const float* X, const float* Kw, const float* dY, floa
     st = dgx_gemm(dyT, kpad, dcolT, (int)rows, g.ckk, Cout, g.ldo, g.ldk, g.ldk, 0, 0, ab_type, DGX_F32,
                   DGX_F32_3XTF32, nullptr, DGX_EPI_NONE, 0.f, nullptr, 0, stream);
     if (st != DGX_OK) return st;
-    col2im_gather_kernel<<<blocks_for((long long)N * Cin * H * W, 256), 256, 0, s>>>(dcolT, dX, g, accumulate);
+    const int hw = H * W, planes = N * Cin;
+    dim3 cg((hw + 255) / 256 < 64 ? (hw + 255) / 256 : 64, planes < 65535 ? planes : 65535);
+    col2im_gather_kernel<<<cg, 256, 0, s>>>(dcolT, dX, g, accumulate);
   }
   return cuda_status(cudaGetLastError(), "dgx_conv2d_bwd");
 }
