@@ -16,6 +16,7 @@
 #include <cmath>
 
 #include "common.h"
+#include "sm100.cuh"
 
 namespace dgx {
 namespace {
@@ -94,6 +95,56 @@ __global__ void gelu_fwd_kernel(const TX* __restrict__ x, __nv_bfloat16* __restr
     const float v = ld_as_float(x, i);
     const float t = tanhf(kGeluK * fmaf(kGeluC * v, v * v, v));
     y[i] = __float2bfloat16_rn(0.5f * v * (1.f + t));
+  }
+}
+
+// bf16 in, bf16 out, 8 elements per thread (16-byte loads and stores) with
+// the hardware tanh (tanh.approx.f32: relative error about 2^-11, far below
+// the bf16 output's 2^-8): the MLP activation of the GPT step.
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+__global__ void gelu_fwd_bf16x8_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, int n8) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += gridDim.x * blockDim.x) {
+    const uint4 v = __ldg(x + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float a = bf_lo(w[k]), b = bf_hi(w[k]);
+      const float ta = tanh_fast(kGeluK * fmaf(kGeluC * a, a * a, a));
+      const float tb = tanh_fast(kGeluK * fmaf(kGeluC * b, b * b, b));
+      o[k] = pack_bf16x2(0.5f * a * (1.f + ta), 0.5f * b * (1.f + tb));
+    }
+    y[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void gelu_bwd_bf16x8_kernel(const uint4* __restrict__ x, const uint4* __restrict__ dy, uint4* __restrict__ dx,
+                                       int n8) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += gridDim.x * blockDim.x) {
+    const uint4 v = __ldg(x + i), gv = __ldg(dy + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float r[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float a = h ? bf_hi(w[k]) : bf_lo(w[k]);
+        const float th = tanh_fast(kGeluK * fmaf(kGeluC * a, a * a, a));
+        const float dinner = kGeluK * fmaf(3.f * kGeluC * a, a, 1.f);
+        const float gg = 0.5f * (1.f + th) + 0.5f * a * (1.f - th * th) * dinner;
+        r[h] = gg * (h ? bf_hi(gw[k]) : bf_lo(gw[k]));
+      }
+      o[k] = pack_bf16x2(r[0], r[1]);
+    }
+    dx[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -336,10 +387,18 @@ dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void*
   if (n == 0) return DGX_OK;
   if (!x || !y16) return set_error(DGX_EINVAL, "dgx_gelu_fwd: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
-  if (x_type == DGX_F32)
+  if (x_type == DGX_BF16 && ((((uintptr_t)x) | (uintptr_t)y16) & 15) == 0 && n < (1LL << 33)) {
+    // bf16 -> bf16: 8-wide vector kernel, the last n % 8 elements by the scalar one
+    const long long n8 = n / 8;
+    if (n8) gelu_fwd_bf16x8_kernel<<<ew_grid(n8), 256, 0, s>>>((const uint4*)x, (uint4*)y16, (int)n8);
+    if (n % 8)
+      gelu_fwd_kernel<__nv_bfloat16><<<1, 256, 0, s>>>((const __nv_bfloat16*)x + n8 * 8,
+                                                     (__nv_bfloat16*)y16 + n8 * 8, n % 8);
+  } else if (x_type == DGX_F32) {
     gelu_fwd_kernel<float><<<ew_grid(n), 256, 0, s>>>((const float*)x, (__nv_bfloat16*)y16, n);
-  else
+  } else {
     gelu_fwd_kernel<__nv_bfloat16><<<ew_grid(n), 256, 0, s>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)y16, n);
+  }
   return cuda_status(cudaGetLastError(), "dgx_gelu_fwd");
 }
 
@@ -352,6 +411,15 @@ dgx_status dgx_gelu_bwd(const void* x, int x_type, const void* dy, int dy_type, 
   cudaStream_t s = (cudaStream_t)stream;
   __nv_bfloat16* o = (__nv_bfloat16*)dx16;
   const int g = ew_grid(n);
+  if (x_type == DGX_BF16 && dy_type == DGX_BF16 && ((((uintptr_t)x) | (uintptr_t)dy | (uintptr_t)dx16) & 15) == 0 &&
+      n < (1LL << 33)) {
+    const long long n8 = n / 8;
+    if (n8) gelu_bwd_bf16x8_kernel<<<ew_grid(n8), 256, 0, s>>>((const uint4*)x, (const uint4*)dy, (uint4*)dx16, (int)n8);
+    if (n % 8)
+      gelu_bwd_kernel<__nv_bfloat16, __nv_bfloat16><<<1, 256, 0, s>>>(
+          (const __nv_bfloat16*)x + n8 * 8, (const __nv_bfloat16*)dy + n8 * 8, o + n8 * 8, n % 8);
+    return cuda_status(cudaGetLastError(), "dgx_gelu_bwd");
+  }
   if (x_type == DGX_F32 && dy_type == DGX_F32)
     gelu_bwd_kernel<float, float><<<g, 256, 0, s>>>((const float*)x, (const float*)dy, o, n);
   else if (x_type == DGX_F32)

@@ -109,3 +109,26 @@ def test_training_reduces_loss(dgx):
             first = loss.item()
     dgx.sync_check()
     assert loss.item() < 0.8 * first, (first, loss.item())
+
+
+@pytest.mark.parametrize("n", [8 * 1000, 8 * 1000 + 5, 3])
+def test_gelu_kernels_against_oracle(dgx, n):
+    """dgx_gelu_fwd / dgx_gelu_bwd on bf16 (the 8-wide vector kernel plus the
+    scalar tail) against the oracle's f64 GELU (runtime/io/builtins.inc:548-560)
+    and its derivative (runtime/ops/autograd.inc:293-303) of the same bf16
+    inputs; tolerance 1e-2 normwise (bf16 output)."""
+    from dreamcompiler_b200 import _lib as L
+    g = torch.Generator(device="cuda").manual_seed(n)
+    x = (torch.randn(n, device="cuda", generator=g) * 3).bfloat16()
+    dy = torch.randn(n, device="cuda", generator=g).bfloat16()
+    y = torch.empty_like(x)
+    dx = torch.empty_like(x)
+    s = torch.cuda.current_stream().cuda_stream
+    L.call("dgx_gelu_fwd", x.data_ptr(), L.DGX_BF16, y.data_ptr(), n, s)
+    L.call("dgx_gelu_bwd", x.data_ptr(), L.DGX_BF16, dy.data_ptr(), L.DGX_BF16, dx.data_ptr(), n, s)
+    dgx.sync_check()
+    xf, df = x.double().cpu().numpy(), dy.double().cpu().numpy()
+    ry, rdx = G.gelu(xf), G.gelu_bwd(xf, df)
+    nw = lambda a, r: np.abs(a - r).max() / max(np.abs(r).max(), 1e-30)
+    assert nw(y.double().cpu().numpy(), ry) < 1e-2
+    assert nw(dx.double().cpu().numpy(), rdx) < 1e-2
