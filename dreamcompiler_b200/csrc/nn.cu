@@ -299,10 +299,57 @@ __global__ void colsum_partial_kernel(const T* __restrict__ dy, float* __restric
     part[(size_t)blockIdx.y * N + c] = t;
   }
 }
-__global__ void colsum_final_kernel(const float* __restrict__ part, float* __restrict__ db, int N, int accumulate) {
+// Vector form (N a multiple of 16 bytes' worth of columns, aligned rows):
+// a thread sums VEC adjacent columns with 16-byte loads; `slices` row slices
+// sized so that the grid covers the SMs.
+template <typename T>
+__global__ void colsum_partial_vec_kernel(const T* __restrict__ dy, float* __restrict__ part, int R, int N,
+                                          int slices) {
+  constexpr int VEC = 16 / sizeof(T);
+  __shared__ float red[8][32 * VEC + 1];
+  const int cv = blockIdx.x * 32 + (threadIdx.x & 31);  // column vector index
+  const int ty = threadIdx.x >> 5;                       // 8 row groups
+  const int rows_per = (R + slices - 1) / slices;
+  const int r0 = blockIdx.y * rows_per, r1 = min(R, r0 + rows_per);
+  float acc[VEC];
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
+  if (cv * VEC < N)
+    for (int r = r0 + ty; r < r1; r += 8) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(dy + (size_t)r * N) + cv);
+      if constexpr (sizeof(T) == 2) {
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[2 * k] += __uint_as_float(u[k] << 16);
+          acc[2 * k + 1] += __uint_as_float(u[k] & 0xFFFF0000u);
+        }
+      } else {
+        acc[0] += __uint_as_float(w.x);
+        acc[1] += __uint_as_float(w.y);
+        acc[2] += __uint_as_float(w.z);
+        acc[3] += __uint_as_float(w.w);
+      }
+    }
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) red[ty][(threadIdx.x & 31) * VEC + k] = acc[k];
+  __syncthreads();
+  for (int j = threadIdx.x; j < 32 * VEC; j += blockDim.x) {
+    const int c = blockIdx.x * 32 * VEC + j;
+    if (c < N) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t += red[k][j];
+      part[(size_t)blockIdx.y * N + c] = t;
+    }
+  }
+}
+
+__global__ void colsum_final_kernel(const float* __restrict__ part, float* __restrict__ db, int N, int accumulate,
+                                    int slices) {
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < N; c += gridDim.x * blockDim.x) {
     float s = 0.f;
-    for (int k = 0; k < CS_SLICES; ++k) s += part[(size_t)k * N + c];
+    for (int k = 0; k < slices; ++k) s += part[(size_t)k * N + c];
     db[c] = accumulate ? db[c] + s : s;
   }
 }
@@ -490,14 +537,28 @@ dgx_status dgx_colsum(const void* dy, int dy_type, float* db, int R, int N, int 
   if (dy_type != DGX_F32 && dy_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_colsum: type %d", dy_type);
   if (!dy || !db) return set_error(DGX_EINVAL, "dgx_colsum: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
-  float* part = (float*)library_scratch((size_t)CS_SLICES * N * sizeof(float), s);
+  constexpr int kMaxSlices = 128;
+  float* part = (float*)library_scratch((size_t)kMaxSlices * N * sizeof(float), s);
   if (!part) return set_error(DGX_ENOMEM, "dgx_colsum: scratch");
-  dim3 grid((N + 31) / 32, CS_SLICES);
-  if (dy_type == DGX_F32)
-    colsum_partial_kernel<float><<<grid, 256, 0, s>>>((const float*)dy, part, R, N);
-  else
-    colsum_partial_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part, R, N);
-  colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(part, db, N, accumulate);
+  const int esz = dy_type == DGX_F32 ? 4 : 2, vec = 16 / esz;
+  int slices = CS_SLICES;
+  if (N % vec == 0 && ((uintptr_t)dy & 15) == 0) {
+    const int cblocks = (N / vec + 31) / 32;
+    slices = (2 * num_sms() + cblocks - 1) / cblocks;
+    slices = slices < 1 ? 1 : (slices > kMaxSlices ? kMaxSlices : slices);
+    dim3 grid(cblocks, slices);
+    if (dy_type == DGX_F32)
+      colsum_partial_vec_kernel<float><<<grid, 256, 0, s>>>((const float*)dy, part, R, N, slices);
+    else
+      colsum_partial_vec_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part, R, N, slices);
+  } else {
+    dim3 grid((N + 31) / 32, CS_SLICES);
+    if (dy_type == DGX_F32)
+      colsum_partial_kernel<float><<<grid, 256, 0, s>>>((const float*)dy, part, R, N);
+    else
+      colsum_partial_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part, R, N);
+  }
+  colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(part, db, N, accumulate, slices);
   return cuda_status(cudaGetLastError(), "dgx_colsum");
 }
 

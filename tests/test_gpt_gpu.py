@@ -132,3 +132,23 @@ def test_gelu_kernels_against_oracle(dgx, n):
     nw = lambda a, r: np.abs(a - r).max() / max(np.abs(r).max(), 1e-30)
     assert nw(y.double().cpu().numpy(), ry) < 1e-2
     assert nw(dx.double().cpu().numpy(), rdx) < 1e-2
+
+
+@pytest.mark.parametrize("dtype,R,N", [("bf16", 16384, 1536), ("bf16", 16384, 384), ("f32", 16384, 65),
+                                       ("f32", 1000, 384), ("bf16", 77, 24)])
+def test_colsum_kernels(dgx, dtype, R, N):
+    """dgx_colsum (bias gradients: column sums of dY, fixed-order slices) on
+    the vector path (16-byte rows) and the scalar one, with accumulate."""
+    from dreamcompiler_b200 import _lib as L
+    g = torch.Generator(device="cuda").manual_seed(R + N)
+    dy = torch.randn(R, N, device="cuda", generator=g)
+    if dtype == "bf16":
+        dy = dy.bfloat16()
+    db = torch.ones(N, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    t = L.DGX_BF16 if dtype == "bf16" else L.DGX_F32
+    L.call("dgx_colsum", dy.data_ptr(), t, db.data_ptr(), R, N, 1, s)
+    dgx.sync_check()
+    ref = dy.double().sum(0).cpu().numpy() + 1.0
+    got = db.double().cpu().numpy()
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 1e-5
