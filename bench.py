@@ -88,6 +88,46 @@ def cpu_workers() -> int:
 
 
 # ---------------------------------------------------------------- clocks
+def nvml_handle(pynvml, device_index: int):
+    """NVML handle of CUDA device `device_index`, matched by UUID (NVML
+    numbers every GPU of the machine, CUDA only the visible ones), else by
+    PCI bus id, else by index."""
+    try:
+        import torch
+        props = torch.cuda.get_device_properties(device_index)
+        uuid = getattr(props, "uuid", None)
+        if uuid is not None:
+            u = str(uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(u if u.startswith("GPU-") else "GPU-" + u)
+    except Exception:
+        pass
+    try:
+        import torch
+        props = torch.cuda.get_device_properties(device_index)
+        bus = "%08X:%02X:%02X.0" % (getattr(props, "pci_domain_id"), getattr(props, "pci_bus_id"),
+                                    getattr(props, "pci_device_id"))
+        return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+    except Exception:
+        pass
+    return pynvml.nvmlDeviceGetHandleByIndex(device_index)
+
+
+def pin_to_gpu_cpus(device_index: int) -> None:
+    """Restrict this process to the CPU cores NVML reports as local to the
+    GPU, so that pinned host buffers allocated afterwards sit on the GPU's
+    own socket (the end-to-end copies cross PCIe from there)."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        words = pynvml.nvmlDeviceGetCpuAffinity(nvml_handle(pynvml, device_index), 64)
+        cpus = {w * 64 + b for w, m in enumerate(words) for b in range(64) if (int(m) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+    except Exception:
+        pass
+
+
 class ClockSampler:
     """Polls NVML (SM clock, throttle reasons) in a thread during a region."""
 
@@ -98,7 +138,7 @@ class ClockSampler:
             import pynvml
             pynvml.nvmlInit()
             self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.h = nvml_handle(pynvml, device_index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
             self.ok = True
         except Exception:
@@ -204,6 +244,7 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- end to end: host bf16 buffers in pinned memory, H2D -> fwd -> bwd -> D2H,
     # pipelined over head chunks on three streams.
+    pin_to_gpu_cpus(local_rank)
     host_in = [torch.empty(BH, S, D, dtype=torch.bfloat16, pin_memory=True) for _ in range(4)]
     for h, d in zip(host_in, sets[0]):
         h.copy_(d)
@@ -514,6 +555,7 @@ def main():
                      "algorithmic": f"{BWD_FLOP:.4g} FLOP per launch = 10*BH*S^2*D/2 (causal)"},
         "e2e": {"value": n * step_flop / e2e_s / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": 4 * BH * S * D * 2,
                 "d2h_bytes_per_step": 4 * BH * S * D * 2,
+                "host_cpus": len(os.sched_getaffinity(0)),
                 "path": "pinned host bf16 Q,K,V,dO -> dgx_flash_fwd/bwd -> O,dQ,dK,dV to host, 32-head chunks "
                         "pipelined on 3 streams, consecutive steps overlapped (PCIe Gen5 x16: about 49 GB/s "
                         "each way when both directions run)"},
