@@ -45,6 +45,9 @@ SIGNATURES = {
     "dgx_conv2d_fwd": (_i, [_vp] * 4 + [_i] * 10 + [_vp]),
     "dgx_conv2d_bwd": (_i, [_vp] * 5 + [_i] * 11 + [_vp]),
     "dgx_conv2d_workspace_size": (_sz, [_i] * 10),
+    "dgx_flash_fwd_rows": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _f, _i, _vp]),
+    "dgx_flash_bwd_rows": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _vp, _i, _vp, _vp, _i, _vp, _i, _vp, _i,
+                                _i, _i, _i, _i, _f, _i, _vp, _sz, _vp]),
     "dgx_dense_q": (_i, [_vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "dgx_gemm_batched": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, C.c_longlong, C.c_longlong, C.c_longlong,
                                _i, _i, _i, _i, _f, _vp]),

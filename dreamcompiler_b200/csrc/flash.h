@@ -6,6 +6,10 @@
 
 namespace dgx {
 
+// Head layout of a tensor: head h of batch b, position s, starts at element
+// (b*S + s)*ld + h*D of its base pointer, with BH = B*H. [BH][S][D] is H = 1,
+// ld = D; the token rows a fused QKV projection writes ([B*S][3*H*D], Q, K, V
+// at column offsets 0, H*D, 2*H*D folded into the base) are H heads, ld = 3*H*D.
 struct FlashFwdArgs {
   const void* Q;
   const void* K;
@@ -16,6 +20,8 @@ struct FlashFwdArgs {
   float scale;
   int causal;
   uint32_t* err;
+  int H;                    // heads per batch row (1: the [BH][S][D] layout)
+  int ldq, ldk, ldv, ldo;   // row pitches (elements)
 };
 
 struct FlashBwdArgs {
@@ -36,13 +42,27 @@ struct FlashBwdArgs {
   int causal;
   uint32_t* err;
   int zero_acc;    // the row pre-pass also zeroes dq_acc (tensor-core path)
+  int H;                                        // heads per batch row (1: [BH][S][D])
+  int ldq, ldk, ldv, ldo, lddo, lddq, lddk, lddv;  // row pitches (elements); dq_acc stays [BH][S][D]
+  int dense3d;     // set by the launcher: every tensor is [BH][S][D], loaded through 3-D maps
 };
+
+// The [BH][S][D] layout for every tensor.
+inline void flash_dense_layout(FlashFwdArgs& a) {
+  a.H = 1;
+  a.ldq = a.ldk = a.ldv = a.ldo = a.D;
+}
+inline void flash_dense_layout(FlashBwdArgs& a) {
+  a.H = 1;
+  a.ldq = a.ldk = a.ldv = a.ldo = a.lddo = a.lddq = a.lddk = a.lddv = a.D;
+}
 
 // Scratch bytes the backward needs (dQ accumulator + padded row statistics).
 inline int flash_spad(int S) { return (S + 127) / 128 * 128; }
 size_t flash_bwd_scratch_bytes(int BH, int S, int D);
 
 bool flash_tc_supported(int D, const void* const* ptrs, int n);
+bool make_head_map(CUtensorMap* map, const void* base, int BH, int H, int S, int D, int ld);
 cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s);
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s);
 // SIMT kernels for head dims the tensor-core kernels do not take (D % 8 != 0

@@ -109,11 +109,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int nitems = ((args.S + BKV - 1) / BKV) * args.BH;
   struct Item {
     int j, bh, i0, n;
+    int b, h;  // bh = b*H + h
   };
   auto item = [&](int w) {
     Item it;
     it.j = w / args.BH;
     it.bh = w % args.BH;
+    it.b = it.bh / args.H;
+    it.h = it.bh - it.b * args.H;
     it.i0 = args.causal ? (it.j * BKV) / BQ : 0;
     it.n = nq - it.i0;
     return it;
@@ -173,8 +176,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int kb = ic & 1;
         if (!(ok = mbar_wait(&bars->kv_empty[kb], ((ic >> 1) & 1) ^ 1, wc))) break;
         mbar_arrive_expect_tx(&bars->kv_full[kb], 2 * TILE);
-        tma_load_3d(smem + SM_K + kb * TILE, &tmK, &bars->kv_full[kb], 0, I.j * BKV, I.bh);
-        tma_load_3d(smem + SM_V + kb * TILE, &tmV, &bars->kv_full[kb], 0, I.j * BKV, I.bh);
+        if (args.dense3d) {
+          tma_load_3d(smem + SM_K + kb * TILE, &tmK, &bars->kv_full[kb], 0, I.j * BKV, I.bh);
+          tma_load_3d(smem + SM_V + kb * TILE, &tmV, &bars->kv_full[kb], 0, I.j * BKV, I.bh);
+        } else {
+          tma_load_4d(smem + SM_K + kb * TILE, &tmK, &bars->kv_full[kb], 0, I.h, I.j * BKV, I.b);
+          tma_load_4d(smem + SM_V + kb * TILE, &tmV, &bars->kv_full[kb], 0, I.h, I.j * BKV, I.b);
+        }
         ++kv_filled;
         const float* Dstat = args.rowstat + (size_t)I.bh * args.Spad;
         const float* L2stat = args.rowstat + (size_t)args.BH * args.Spad + (size_t)I.bh * args.Spad;
@@ -182,8 +190,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int s = gt % Q_STAGES;
           if (!(ok = mbar_wait(&bars->q_empty[s], ((gt / Q_STAGES) & 1) ^ 1, wc))) break;
           mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE + STAT_BYTES);
-          tma_load_3d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
-          tma_load_3d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
+          if (args.dense3d) {
+            tma_load_3d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
+            tma_load_3d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
+          } else {
+            tma_load_4d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, I.h, (I.i0 + it) * BQ, I.b);
+            tma_load_4d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, I.h, (I.i0 + it) * BQ, I.b);
+          }
           uint8_t* st = smem + SM_STAT + s * STAT_BYTES;
           bulk_load(st, L2stat + (I.i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
           bulk_load(st + BQ * 4, Dstat + (I.i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
@@ -448,8 +461,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();  // the next item's first dV / dK MMAs follow this warp's next p_ready
       if (key < args.S) {
         const float mul = h ? args.scale : 1.f;
-        __nv_bfloat16* dst =
-            reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) + ((size_t)I.bh * args.S + key) * args.D;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) +
+                             ((size_t)I.b * args.S + key) * (h ? args.lddk : args.lddv) + (size_t)I.h * args.D;
         if (args.D == DP) {
 #pragma unroll
           for (int c = 0; c < DP; c += 8) {
@@ -491,9 +504,10 @@ __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
     const int bh = (int)(r / a.Spad), q = (int)(r % a.Spad);
     float s = 0.f;
     if (q < a.S) {
-      const long long src = ((long long)bh * a.S + q) * a.D;
-      const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.O) + src;
-      const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.dO) + src;
+      const int b = bh / a.H, h = bh - b * a.H;
+      const long long row = (long long)b * a.S + q;
+      const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.O) + row * a.ldo + (long long)h * a.D;
+      const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.dO) + row * a.lddo + (long long)h * a.D;
       if (vec) {
         for (int c = sub * 8; c < a.D; c += 64) {
           const uint4 ov = *reinterpret_cast<const uint4*>(o + c), gv = *reinterpret_cast<const uint4*>(g + c);
@@ -546,7 +560,29 @@ __global__ void flash_bwd_post_kernel(FlashBwdArgs a) {
     dq[i] = __float2bfloat16_rn(a.dq_acc[i] * a.scale);
 }
 
-bool make_map(CUtensorMap* map, const void* base, int BH, int S, int D) {
+// The same for dQ in a head layout other than [BH][S][D]: quad c4 of row
+// (bh, s) goes to dQ + (b*S + s)*lddq + h*D + 4*c4 (D % 4 == 0 and
+// BH*S*D < 2^31, both checked by the caller).
+__global__ void flash_bwd_post_rows_kernel(FlashBwdArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int qpr = a.D >> 2;
+  const int quads = a.BH * a.S * qpr;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += gridDim.x * blockDim.x) {
+    const int row = i / qpr, c = (i - row * qpr) << 2;
+    const int bh = row / a.S, s = row - bh * a.S;
+    const int b = bh / a.H, h = bh - b * a.H;
+    const float4 v = reinterpret_cast<const float4*>(a.dq_acc)[i];
+    uint2 w;
+    w.x = pack_bf16x2(v.x * a.scale, v.y * a.scale);
+    w.y = pack_bf16x2(v.z * a.scale, v.w * a.scale);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.dQ) + ((size_t)b * a.S + s) * a.lddq +
+                              (size_t)h * a.D + c) = w;
+  }
+}
+
+
+// The dense [BH][S][D] view through a 3-D map (box 64 x 128 x 1).
+bool make_map3(CUtensorMap* map, const void* base, int BH, int S, int D) {
   auto enc = get_tensor_map_encoder();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
@@ -566,9 +602,18 @@ size_t flash_bwd_scratch_bytes(int BH, int S, int D) {
 
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
   CUtensorMap mq{}, mk{}, mv{}, mdo{};
-  if (!make_map(&mq, a.Q, a.BH, a.S, a.D) || !make_map(&mk, a.K, a.BH, a.S, a.D) ||
-      !make_map(&mv, a.V, a.BH, a.S, a.D) || !make_map(&mdo, a.dO, a.BH, a.S, a.D))
+  FlashBwdArgs la = a;
+  la.dense3d = a.H == 1 && a.ldq == a.D && a.ldk == a.D && a.ldv == a.D && a.lddo == a.D;
+  if (la.dense3d) {
+    if (!make_map3(&mq, a.Q, a.BH, a.S, a.D) || !make_map3(&mk, a.K, a.BH, a.S, a.D) ||
+        !make_map3(&mv, a.V, a.BH, a.S, a.D) || !make_map3(&mdo, a.dO, a.BH, a.S, a.D))
+      return cudaErrorInvalidValue;
+  } else if (!make_head_map(&mq, a.Q, a.BH, a.H, a.S, a.D, a.ldq) ||
+             !make_head_map(&mk, a.K, a.BH, a.H, a.S, a.D, a.ldk) ||
+             !make_head_map(&mv, a.V, a.BH, a.H, a.S, a.D, a.ldv) ||
+             !make_head_map(&mdo, a.dO, a.BH, a.H, a.S, a.D, a.lddo)) {
     return cudaErrorInvalidValue;
+  }
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
@@ -612,7 +657,7 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
     TimerScope timer(s);
-    e = cudaLaunchKernelEx(&cfg, flash_bwd_kernel, mq, mk, mv, mdo, mdq, a);
+    e = cudaLaunchKernelEx(&cfg, flash_bwd_kernel, mq, mk, mv, mdo, mdq, la);
     if (e != cudaSuccess) return e;
   }
   {
@@ -622,7 +667,9 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
     cfg.stream = s;
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, flash_bwd_post_kernel, a);
+    const bool dense_dq = a.H == 1 && a.lddq == a.D;
+    e = dense_dq ? cudaLaunchKernelEx(&cfg, flash_bwd_post_kernel, a)
+                 : cudaLaunchKernelEx(&cfg, flash_bwd_post_rows_kernel, a);
     if (e != cudaSuccess) return e;
   }
   return cudaGetLastError();

@@ -95,12 +95,15 @@ struct FwdBars {
 // Q tiles, head, and how many K/V tiles each tile sees.
 struct FwdItem {
   int q0, bh, nA, nB;
+  int b, h;  // bh = b*H + h
 };
 __device__ __forceinline__ FwdItem fwd_item(const FlashFwdArgs& a, int w) {
   FwdItem I;
   const int nqb = (a.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M);
   const int qb = a.causal ? (nqb - 1 - w / a.BH) : (w / a.BH);
   I.bh = w % a.BH;
+  I.b = I.bh / a.H;
+  I.h = I.bh - I.b * a.H;
   I.q0 = qb * 2 * BLOCK_M;
   const int nkv = (a.S + BLOCK_N - 1) / BLOCK_N;
   int nt[2];
@@ -174,16 +177,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!(ok = mbar_wait(&bars->q_empty[qb2], ((ic >> 1) & 1) ^ 1, wc))) break;
         mbar_arrive_expect_tx(&bars->q_full[qb2], 2 * TILE_BYTES);
         uint8_t* sq = smem + SM_Q + qb2 * 2 * TILE_BYTES;
-        tma_load_3d(sq, &tmQ, &bars->q_full[qb2], 0, I.q0, I.bh);
-        tma_load_3d(sq + TILE_BYTES, &tmQ, &bars->q_full[qb2], 0, I.q0 + BLOCK_M, I.bh);
+        tma_load_4d(sq, &tmQ, &bars->q_full[qb2], 0, I.h, I.q0, I.b);
+        tma_load_4d(sq + TILE_BYTES, &tmQ, &bars->q_full[qb2], 0, I.h, I.q0 + BLOCK_M, I.b);
         ++ic;  // counted as issued before any later wait can fail
         for (int j = 0; j < I.nB; ++j, ++gkv) {
           const int s = gkv % KV_STAGES;
           if (!(ok = mbar_wait(&bars->kv_empty[s], ((gkv / KV_STAGES) & 1) ^ 1, wc))) break;
           mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
-          tma_load_3d(smem + SM_K + s * TILE_BYTES, &tmK, &bars->k_full[s], 0, j * BLOCK_N, I.bh);
+          tma_load_4d(smem + SM_K + s * TILE_BYTES, &tmK, &bars->k_full[s], 0, I.h, j * BLOCK_N, I.b);
           mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
-          tma_load_3d(smem + SM_V + s * TILE_BYTES, &tmV, &bars->v_full[s], 0, j * BLOCK_N, I.bh);
+          tma_load_4d(smem + SM_V + s * TILE_BYTES, &tmV, &bars->v_full[s], 0, I.h, j * BLOCK_N, I.b);
         }
       }
       // Teardown: every copy issued must have landed before the CTA leaves.
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const FwdItem I = fwd_item(args, w);
       const int n = x ? I.nB : I.nA;
       const int qrow = I.q0 + x * BLOCK_M + r;
-      const int row_base = I.bh * args.S;  // row of the [BH*S, D] view
+      const int row_base = I.bh * args.S;  // row of the [BH*S] LSE view
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < n; ++j) {
         const uint32_t k = kbase + j;
@@ -403,7 +406,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_before();
         if (qrow < args.S) {
           const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-          __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.O) + ((size_t)row_base + qrow) * args.D;
+          __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.O) +
+                                ((size_t)I.b * args.S + qrow) * args.ldo + (size_t)I.h * args.D;
           if (args.D == DP) {
 #pragma unroll
             for (int c = 0; c < DP; c += 8) {
@@ -435,21 +439,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-bool make_qkv_map(CUtensorMap* map, const void* base, int BH, int S, int D) {
+}  // namespace
+
+// 4-D view [B][S][H][D] of a bf16 head tensor (row pitch ld elements; H = 1,
+// ld = D is the dense [BH][S][D] layout): a box of 64 columns x 1 head x 128
+// rows never crosses a head; rows past S and columns past D read as zero.
+bool make_head_map(CUtensorMap* map, const void* base, int BH, int H, int S, int D, int ld) {
   auto enc = get_tensor_map_encoder();
-  if (!enc) return false;
-  // 3-D view [BH][S][D]: a box of 128 rows x 64 columns never crosses a head,
-  // rows past S and columns past D read as zero.
-  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
-  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
-  cuuint32_t box[3] = {DP, BLOCK_M, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  if (!enc || H <= 0 || BH % H) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)(BH / H)};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)ld * 2, (cuuint64_t)S * ld * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-
-}  // namespace
 
 bool flash_tc_supported(int D, const void* const* ptrs, int n) {
   if (D < 8 || D > DP || D % 8) return false;
@@ -460,8 +465,8 @@ bool flash_tc_supported(int D, const void* const* ptrs, int n) {
 
 cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s) {
   CUtensorMap mq{}, mk{}, mv{};
-  if (!make_qkv_map(&mq, a.Q, a.BH, a.S, a.D) || !make_qkv_map(&mk, a.K, a.BH, a.S, a.D) ||
-      !make_qkv_map(&mv, a.V, a.BH, a.S, a.D))
+  if (!make_head_map(&mq, a.Q, a.BH, a.H, a.S, a.D, a.ldq) || !make_head_map(&mk, a.K, a.BH, a.H, a.S, a.D, a.ldk) ||
+      !make_head_map(&mv, a.V, a.BH, a.H, a.S, a.D, a.ldv))
     return cudaErrorInvalidValue;
   static bool attr = false;
   if (!attr) {

@@ -5,7 +5,8 @@ restatement in oracle/gpt_oracle.py): token + position embedding, L pre-LN
 blocks of causal multi-head attention and a 4x GELU(tanh) MLP, a final
 layer_norm, a linear head, log_softmax + nll_loss, and AdamW. Every `linear`
 runs on dgx_gemm (bf16 operands, fp32 accumulate and bias epilogue), the
-attention on dgx_flash_fwd / dgx_flash_bwd, everything else on the libdgx
+attention on dgx_flash_fwd_rows / dgx_flash_bwd_rows (heads read from and
+written to token rows), everything else on the libdgx
 device ops (dgx_layernorm_*, dgx_gelu_*, dgx_embedding_*, dgx_softmax_nll,
 dgx_colsum, dgx_adamw, the head layout permutes). Parameters, gradients and
 AdamW state are fp32; the GEMMs read bf16 copies of the weights refreshed
@@ -24,7 +25,7 @@ from typing import Dict
 import torch
 
 from . import _lib as L
-from .ops import _stream, flash_bwd, flash_bwd_workspace_size, flash_fwd, gemm
+from .ops import _stream, flash_bwd_workspace_size, gemm
 
 
 @dataclass
@@ -111,9 +112,9 @@ class GPT:
         self.h16 = [torch.empty(R, d, device=dev, dtype=bf16) for _ in range(2 * c.n_layer + 1)]
         self.mu = [torch.empty(R, device=dev, dtype=f32) for _ in range(2 * c.n_layer + 1)]
         self.rs = [torch.empty(R, device=dev, dtype=f32) for _ in range(2 * c.n_layer + 1)]
-        self.qkv16 = torch.empty(R, 3 * d, device=dev, dtype=bf16)
-        heads = lambda: torch.empty(B * H, S, hd, device=dev, dtype=bf16)
-        self.q, self.k, self.v, self.o = ([heads() for _ in range(c.n_layer)] for _ in range(4))
+        # Q, K, V stay inside the QKV projection's token rows: the attention
+        # kernels read heads there (dgx_flash_fwd_rows) and write O as rows.
+        self.qkv16 = [torch.empty(R, 3 * d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
         self.lse = [torch.empty(B * H, S, device=dev, dtype=f32) for _ in range(c.n_layer)]
         self.att16 = [torch.empty(R, d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
         self.u16 = [torch.empty(R, 4 * d, device=dev, dtype=bf16) for _ in range(c.n_layer)]
@@ -128,7 +129,7 @@ class GPT:
         self.dg16 = torch.empty(R, 4 * d, device=dev, dtype=bf16)
         self.du16 = torch.empty(R, 4 * d, device=dev, dtype=bf16)
         self.dqkv16 = torch.empty(R, 3 * d, device=dev, dtype=bf16)
-        self.dO, self.dq, self.dk, self.dv = (heads() for _ in range(4))
+        self.datt16 = torch.empty(R, d, device=dev, dtype=bf16)
         self.fa_ws = torch.empty(flash_bwd_workspace_size(B * H, S, hd) // 4 + 1, device=dev, dtype=f32)
 
     # ------------------------------------------------------------ setup
@@ -174,11 +175,11 @@ class GPT:
             h, h2 = self.h16[2 * l], self.h16[2 * l + 1]
             _c("dgx_layernorm_fwd", x0.data_ptr(), h.data_ptr(), self.mu[2 * l].data_ptr(), self.rs[2 * l].data_ptr(),
                R, d, s)
-            gemm(h, w[f"Wqkv{l}"], transB=True, out=self.qkv16, bias=p[f"bqkv{l}"])
-            for i, dst in enumerate((self.q[l], self.k[l], self.v[l])):
-                _c("dgx_rows_to_heads", self.qkv16.data_ptr(), L.DGX_BF16, 3 * d, i * d, dst.data_ptr(), B, S, H, hd, s)
-            flash_fwd(self.q[l], self.k[l], self.v[l], out=self.o[l], lse=self.lse[l])
-            _c("dgx_heads_to_rows", self.o[l].data_ptr(), self.att16[l].data_ptr(), d, 0, B, S, H, hd, s)
+            qkv = self.qkv16[l]
+            gemm(h, w[f"Wqkv{l}"], transB=True, out=qkv, bias=p[f"bqkv{l}"])
+            qp = qkv.data_ptr()
+            _c("dgx_flash_fwd_rows", qp, 3 * d, qp + 2 * d, 3 * d, qp + 4 * d, 3 * d, self.att16[l].data_ptr(), d,
+               self.lse[l].data_ptr(), B, H, S, hd, hd ** -0.5, 1, s)
             x1.copy_(x0)
             gemm(self.att16[l], w[f"Wo{l}"], transB=True, out=x1, bias=p[f"bo{l}"], beta=1.0)  # x1 = x0 + att Wo^T + bo
             _c("dgx_layernorm_fwd", x1.data_ptr(), h2.data_ptr(), self.mu[2 * l + 1].data_ptr(),
@@ -217,14 +218,14 @@ class GPT:
                self.dh.data_ptr(), self.dx.data_ptr(), R, d, 1, s)
             # attention: x1 = x0 + merge(attn(split(h Wqkv^T + bqkv))) Wo^T + bo
             conv16(self.dx, self.dx16)
-            gemm(self.dx16, w[f"Wo{l}"], out=self.dh)                     # datt = dx Wo
+            gemm(self.dx16, w[f"Wo{l}"], out=self.datt16)                 # datt = dx Wo (bf16 rows)
             gemm(self.dx16, self.att16[l], transA=True, out=g[f"Wo{l}"])   # dWo = dx^T att
             _c("dgx_colsum", self.dx.data_ptr(), L.DGX_F32, g[f"bo{l}"].data_ptr(), R, d, 0, s)
-            _c("dgx_rows_to_heads", self.dh.data_ptr(), L.DGX_F32, d, 0, self.dO.data_ptr(), B, S, H, hd, s)
-            flash_bwd(self.q[l], self.k[l], self.v[l], self.o[l], self.dO, self.lse[l], dQ=self.dq, dK=self.dk,
-                      dV=self.dv, workspace=self.fa_ws)
-            for i, src in enumerate((self.dq, self.dk, self.dv)):
-                _c("dgx_heads_to_rows", src.data_ptr(), self.dqkv16.data_ptr(), 3 * d, i * d, B, S, H, hd, s)
+            # dQ, dK, dV land in the dQKV rows the next GEMMs read
+            qp, gp = self.qkv16[l].data_ptr(), self.dqkv16.data_ptr()
+            _c("dgx_flash_bwd_rows", qp, 3 * d, qp + 2 * d, 3 * d, qp + 4 * d, 3 * d, self.att16[l].data_ptr(), d,
+               self.datt16.data_ptr(), d, self.lse[l].data_ptr(), gp, 3 * d, gp + 2 * d, 3 * d, gp + 4 * d, 3 * d,
+               B, H, S, hd, hd ** -0.5, 1, self.fa_ws.data_ptr(), self.fa_ws.numel() * 4, s)
             gemm(self.dqkv16, w[f"Wqkv{l}"], out=self.dh)                 # dh = dqkv Wqkv
             gemm(self.dqkv16, h, transA=True, out=g[f"Wqkv{l}"])           # dWqkv = dqkv^T h
             _c("dgx_colsum", self.dqkv16.data_ptr(), L.DGX_BF16, g[f"bqkv{l}"].data_ptr(), R, 3 * d, 0, s)

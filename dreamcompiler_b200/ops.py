@@ -99,6 +99,31 @@ def gemm_batched(A: torch.Tensor, B: torch.Tensor, *, transA: bool = False, tran
     return out
 
 
+def flash_fwd_rows(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, O: torch.Tensor, lse: torch.Tensor,
+                   B: int, H: int, S: int, D: int, *, causal: bool = True, scale: Optional[float] = None) -> None:
+    """FlashAttention forward on heads inside token rows: Q, K, V, O are 2-D
+    bf16 views [B*S, >= H*D] (column slices of one buffer allowed, e.g.
+    qkv[:, 0:HD], qkv[:, HD:2HD], qkv[:, 2HD:]); head h is columns
+    [h*D, (h+1)*D). lse: [B*H, S] fp32."""
+    for t in (Q, K, V, O):
+        assert t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1
+    L.call("dgx_flash_fwd_rows", Q.data_ptr(), Q.stride(0), K.data_ptr(), K.stride(0), V.data_ptr(), V.stride(0),
+           O.data_ptr(), O.stride(0), lse.data_ptr(), B, H, S, D, D ** -0.5 if scale is None else scale,
+           int(causal), _stream(Q))
+
+
+def flash_bwd_rows(Q, K, V, O, dO, lse, dQ, dK, dV, B: int, H: int, S: int, D: int, *, causal: bool = True,
+                   scale: Optional[float] = None, workspace: Optional[torch.Tensor] = None) -> None:
+    """Backward of flash_fwd_rows; dQ, dK, dV are row views like Q, K, V."""
+    for t in (Q, K, V, O, dO, dQ, dK, dV):
+        assert t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1
+    ws, wsb = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
+    L.call("dgx_flash_bwd_rows", Q.data_ptr(), Q.stride(0), K.data_ptr(), K.stride(0), V.data_ptr(), V.stride(0),
+           O.data_ptr(), O.stride(0), dO.data_ptr(), dO.stride(0), lse.data_ptr(), dQ.data_ptr(), dQ.stride(0),
+           dK.data_ptr(), dK.stride(0), dV.data_ptr(), dV.stride(0), B, H, S, D, D ** -0.5 if scale is None else scale,
+           int(causal), ws, wsb, _stream(Q))
+
+
 def conv2d(X: torch.Tensor, Kw: torch.Tensor, bias: Optional[torch.Tensor], KH: int, KW: int, *, pad: int = 0,
            stride: int = 1, operands: torch.dtype = torch.float32) -> torch.Tensor:
     """X [N, Cin, H, W] fp32, Kw [Cout, Cin*KH*KW] fp32 (row per output

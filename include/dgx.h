@@ -170,6 +170,26 @@ dgx_status dgx_flash_bwd(const void* Q, const void* K, const void* V, const void
 size_t dgx_flash_bwd_workspace_size(int BH, int S, int D);
 
 /*
+ * FlashAttention forward / backward on heads stored inside token rows (bf16):
+ * head h of batch b, position s of tensor X starts at element
+ * (b*S + s)*ldX + h*D of X's pointer, BH = B*H. This is how a fused QKV
+ * projection writes its output ([B*S][3*H*D]: pass Q = qkv, K = qkv + H*D,
+ * V = qkv + 2*H*D, all with ld = 3*H*D) and how the output projection reads
+ * O ([B*S][H*D], ld = H*D), so no head transposes run around the kernels.
+ * LSE stays [BH][S]; the workspace is dgx_flash_bwd_workspace_size(B*H, S, D).
+ * Tensor-core kernels only: D % 8 == 0, D <= 64, 16-byte aligned pointers,
+ * pitches multiples of 8 elements. No reference counterpart: the
+ * reference's flash_attention takes one head per batch row ((B, S*dk)); this
+ * form lets a caller that keeps heads inside token rows skip the transposes.
+ */
+dgx_status dgx_flash_fwd_rows(const void* Q, int ldq, const void* K, int ldk, const void* V, int ldv, void* O,
+                              int ldo, float* LSE, int B, int H, int S, int D, float scale, int causal, void* stream);
+dgx_status dgx_flash_bwd_rows(const void* Q, int ldq, const void* K, int ldk, const void* V, int ldv, const void* O,
+                              int ldo, const void* dO, int lddo, const float* LSE, void* dQ, int lddq, void* dK,
+                              int lddk, void* dV, int lddv, int B, int H, int S, int D, float scale, int causal,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * int8 weight-only dense layer, Y[B,N] = bias[N] + scale[n] * sum_k W[n,k] * X[b,k].
  *   W int8 [N][K] (row n = output channel, the dense_q layout), scale [N] fp32
  *   per output channel (a per-tensor scale is N copies of one value), bias [N]

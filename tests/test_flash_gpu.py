@@ -141,3 +141,40 @@ def test_workspace_contract(dgx):
     # key tiles with fp32 atomics, so its last bits may differ between runs.
     assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])
     assert ((a[0].float() - b[0].float()).abs().max() / b[0].float().abs().max()).item() < 1e-2
+
+
+@pytest.mark.parametrize("B,H,S,causal", [(2, 6, 256, True), (1, 3, 300, True), (2, 2, 200, False), (1, 4, 128, True)])
+def test_head_rows_layout_matches_dense(dgx, B, H, S, causal):
+    """dgx_flash_fwd_rows / dgx_flash_bwd_rows on heads inside token rows
+    (a fused QKV buffer [B*S][3*H*D], O and dO [B*S][H*D]) give exactly the
+    dense [BH][S][D] kernels' results on the same values (same tiles, same
+    arithmetic: bit-identical)."""
+    D = 64
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + H * 10 + S)
+    qkv = torch.randn(B * S, 3 * H * D, device="cuda", generator=g).bfloat16()
+    do_rows = torch.randn(B * S, H * D, device="cuda", generator=g).bfloat16()
+    HD = H * D
+    heads = lambda x: x.reshape(B, S, H, D).permute(0, 2, 1, 3).reshape(B * H, S, D).contiguous()
+    rows = lambda x: x.reshape(B, H, S, D).permute(0, 2, 1, 3).reshape(B * S, HD)
+    q, k, v, do = heads(qkv[:, :HD]), heads(qkv[:, HD:2 * HD]), heads(qkv[:, 2 * HD:]), heads(do_rows)
+    O, L = dgx.flash_fwd(q, k, v, causal=causal)
+    dQ, dK, dV = dgx.flash_bwd(q, k, v, O, do, L, causal=causal)
+    o_rows = torch.empty(B * S, HD, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * H, S, device="cuda")
+    dgx.flash_fwd_rows(qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:], o_rows, lse, B, H, S, D, causal=causal)
+    dqkv = torch.zeros(B * S, 3 * HD, device="cuda", dtype=torch.bfloat16)
+    dgx.flash_bwd_rows(qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:], o_rows, do_rows, lse, dqkv[:, :HD],
+                       dqkv[:, HD:2 * HD], dqkv[:, 2 * HD:], B, H, S, D, causal=causal)
+    dgx.sync_check()
+    assert torch.equal(o_rows, rows(O))
+    assert torch.equal(lse, L)
+    assert torch.equal(dqkv[:, :HD], rows(dQ))
+    assert torch.equal(dqkv[:, HD:2 * HD], rows(dK))
+    assert torch.equal(dqkv[:, 2 * HD:], rows(dV))
+
+
+def test_head_rows_rejects_unsupported(dgx):
+    x = torch.zeros(256, 3 * 2 * 40, device="cuda", dtype=torch.bfloat16)
+    o = torch.zeros(256, 80, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(dgx.DgxError):  # D = 48 is fine, but O's pitch 80 < H*D = 96 is not
+        dgx.flash_fwd_rows(x[:, :80], x[:, 80:160], x[:, 160:], o, torch.empty(2, 256, device="cuda"), 1, 2, 256, 48)
