@@ -8,6 +8,14 @@
  * dgx_last_error() holds a one-line message for the calling thread. No call
  * throws, aborts or falls back to the CPU.
  *
+ * Library scratch: calls given no workspace (and the ones that take none:
+ * split-K partials, int8 activation planes, conv im2col matrices) use
+ * buffers the library owns per device and grows with cudaMalloc on demand,
+ * syncing the calling stream before it frees a smaller one. Calls that use
+ * the library's buffers must be ordered (one stream, or streams joined by
+ * events); calls that overlap on the GPU from different streams would share
+ * them. Pass a workspace where the entry point takes one to avoid that.
+ *
  * Each entry point names the reference interface it replaces
  * (heellowdsf/DreamCompiler, paths relative to the project root).
  */
