@@ -152,3 +152,27 @@ def test_colsum_kernels(dgx, dtype, R, N):
     ref = dy.double().sum(0).cpu().numpy() + 1.0
     got = db.double().cpu().numpy()
     assert np.abs(got - ref).max() / np.abs(ref).max() < 1e-5
+
+
+@pytest.mark.parametrize("src_type", ["bf16", "f32"])
+def test_head_layout_kernels(dgx, src_type):
+    """dgx_rows_to_heads / dgx_heads_to_rows: [B*S][ld] rows (head h at
+    column col0 + h*D) <-> [B*H][S][D] heads, bit-exact moves (bf16 source)
+    and round-to-nearest for fp32 rows."""
+    from dreamcompiler_b200 import _lib as L
+    B, S, H, D, ld, col0 = 3, 40, 4, 64, 3 * 256 + 8, 256
+    g = torch.Generator(device="cuda").manual_seed(9)
+    rows = torch.randn(B * S, ld, device="cuda", generator=g)
+    if src_type == "bf16":
+        rows = rows.bfloat16()
+    heads = torch.empty(B * H, S, D, device="cuda", dtype=torch.bfloat16)
+    s = torch.cuda.current_stream().cuda_stream
+    t = L.DGX_BF16 if src_type == "bf16" else L.DGX_F32
+    L.call("dgx_rows_to_heads", rows.data_ptr(), t, ld, col0, heads.data_ptr(), B, S, H, D, s)
+    back = torch.zeros(B * S, ld, device="cuda", dtype=torch.bfloat16)
+    L.call("dgx_heads_to_rows", heads.data_ptr(), back.data_ptr(), ld, col0, B, S, H, D, s)
+    dgx.sync_check()
+    ref = rows[:, col0:col0 + H * D].bfloat16().reshape(B, S, H, D).permute(0, 2, 1, 3).reshape(B * H, S, D)
+    assert torch.equal(heads, ref)
+    assert torch.equal(back[:, col0:col0 + H * D], rows[:, col0:col0 + H * D].bfloat16())
+    assert not back[:, :col0].any()
