@@ -157,3 +157,31 @@ def test_conv_programs_match_reference(R, golden):
         b = R.call("dream_randn", R.scalar(1), R.scalar(Cout))
         Y = R.call("dream_conv2d_padded", X, K, b, *(R.scalar(v) for v in (H, W, KH, KW, pad, stride)))
         assert normwise(R.data(Y), g[f"Y_{t}"]) < 1e-4
+
+
+def test_repeatability_of_seeded_runs(R):
+    """tests/16_determinism.dream's property on this path: two identical
+    seeded runs of matmul (+ its backward) and flash attention (+ backward)
+    give byte-identical results. Everything is reproducible bit for bit
+    except flash dQ over more than one key tile: its fp32 partial sums from
+    the key tiles' CTAs land by L2 reduce-add in whatever order the CTAs
+    finish, so there the two runs agree to fp32 rounding, which can flip
+    the bf16 rounding of a few elements (checked: within one bf16 step of
+    the largest value)."""
+    def run_once():
+        R.call("dream_set_seed", R.scalar(31337))
+        A = R.call("dream_randn", R.scalar(160), R.scalar(160))
+        W = R.call("dream_randn", R.scalar(160), R.scalar(160))
+        h = R.call("tensor_matmul", A, W)
+        q = R.call("dream_randn", R.scalar(2), R.scalar(384 * 64))
+        k = R.call("dream_randn", R.scalar(2), R.scalar(384 * 64))
+        v = R.call("dream_randn", R.scalar(2), R.scalar(384 * 64))
+        o = R.call("dream_flash_attention", q, k, v, *(R.scalar(x) for x in (2, 384, 64, 64)))
+        R.call("backward", R.call("sum", R.call("tensor_mul", h, h)))
+        R.call("backward", R.call("sum", o))
+        return [R.data(h), R.grad(A), R.grad(W), R.data(o), R.grad(k), R.grad(v)], R.grad(q)
+    exact1, dq1 = run_once()
+    exact2, dq2 = run_once()
+    for a, b in zip(exact1, exact2):
+        assert np.array_equal(a, b)
+    assert np.abs(dq1 - dq2).max() <= 2.0 ** -7 * np.abs(dq1).max()
