@@ -332,3 +332,22 @@ def test_bmm_broadcast_operand_and_overlap_rejected(dgx):
     A = torch.zeros(2, 4, 4, device="cuda")
     with pytest.raises(dgx.DgxError):
         dgx.gemm_batched(A, A, out=torch.zeros(1, 4, 4, device="cuda").expand(2, 4, 4))
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 128, 256), (300, 200, 257), (512, 64, 300), (8, 16, 16), (7, 15, 13),
+                                   (9, 8, 17), (1, 4, 1), (16, 32, 24), (32, 16, 32)])
+def test_reference_selftest_shapes(dgx, orc, M, K, N):
+    """The shapes of the reference's gpu_selftest (runtime/ops/elementwise.inc:
+    821: the GPU matmul against the CPU GEMM, uniform(-1, 1) inputs, pass at
+    |d| <= sqrt(K)*1e-4 elementwise) and of its packed-f32 check (:939-941),
+    on the 3xTF32 path: the reference's elementwise criterion and the
+    normwise 1e-4 gate both hold."""
+    rng = np.random.default_rng(20260708 + M + K + N)
+    A = rng.uniform(-1, 1, (M, K))
+    B = rng.uniform(-1, 1, (K, N))
+    C = dgx.gemm(cuda(A), cuda(B))
+    dgx.sync_check()
+    ref = orc.gemm_f64(A.astype(np.float32).astype(np.float64), B.astype(np.float32).astype(np.float64))
+    got = C.cpu().numpy().astype(np.float64)
+    assert np.abs(got - ref).max() <= np.sqrt(K) * 1e-4
+    assert normwise(got, ref) < F32_TOL
