@@ -76,7 +76,8 @@ template <bool TF32, bool A_MN, bool B_MN, int BN_>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                   const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ ExtraOutMaps tmX,
+                   GemmArgs args) {
   using Cfg = GemmCfg<TF32, BN_>;
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -239,7 +240,10 @@ __global__ void __launch_bounds__(192, 1)
     // issues one TMA store / reduce-add per chunk.
     uint8_t* my_stage = out_stage + (warp - 2) * 8192;
     uint32_t issued = 0;  // stores issued by this warp: buffer = issued & 1
-    if (args.tma_out && lane == 0) tma_prefetch_desc(&tmC);
+    if (args.tma_out && lane == 0) {
+      tma_prefetch_desc(&tmC);
+      for (int e = 0; e < args.n_extra; ++e) tma_prefetch_desc(&tmX.m[e]);
+    }
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++use) {
       const int buf = use & 1;
       if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
@@ -307,9 +311,11 @@ __global__ void __launch_bounds__(192, 1)
               tma_store_3d(&tmC, st, n0, tm * BM + q * 32, t % splits);
             else if (args.tma_out == 2)
               tma_reduce_add_3d(&tmC, st, n0, tm * BM + q * 32, bz);
-            else
+            else {
               tma_store_3d(&tmC, st, n0, tm * BM + q * 32, bz);
-            bulk_commit();
+              for (int e = 0; e < args.n_extra; ++e) tma_store_3d(&tmX.m[e], st, n0, tm * BM + q * 32, bz);
+            }
+            bulk_commit();  // one group per staged buffer, all its destinations
           }
           ++issued;
         }
@@ -572,6 +578,7 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   }
   // Epilogue path (see GemmArgs::tma_out).
   CUtensorMap mc{};
+  ExtraOutMaps mx{};
   if (a.splits > 1) {
     auto enc = get_tensor_map_encoder();
     const cuuint64_t dims[3] = {(cuuint64_t)a.N, (cuuint64_t)a.M, (cuuint64_t)a.splits};
@@ -588,16 +595,20 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
     const bool aligned = ((uintptr_t)a.C & 15) == 0 && ((long long)a.ldc * esz) % 16 == 0 &&
                          (nb == 1 || (a.sC * esz) % 16 == 0);
     int mode = 0;
-    if (a.n_extra == 0 && aligned) {
+    if (aligned && extras_tma_aligned(a)) {
       if (a.beta == 0.f)
         mode = 1;
-      else if (a.beta == 1.f && !a.c_bf16 && !a.relu)
+      else if (a.n_extra == 0 && a.beta == 1.f && !a.c_bf16 && !a.relu)
         mode = 2;
     }
-    if (mode && !encode_3d(&mc, a.C, a.c_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                           (uint64_t)a.N, (uint64_t)a.M, nb, (uint64_t)a.ldc * esz, (uint64_t)a.sC * esz,
-                           128 / esz, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
+    const CUtensorMapDataType cdt = a.c_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if (mode && !encode_3d(&mc, a.C, cdt, (uint64_t)a.N, (uint64_t)a.M, nb, (uint64_t)a.ldc * esz,
+                           (uint64_t)a.sC * esz, 128 / esz, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
       mode = 0;
+    for (int e = 0; mode && e < a.n_extra; ++e)  // every extra destination, same box
+      if (!encode_3d(&mx.m[e], a.C_extra[e], cdt, (uint64_t)a.N, (uint64_t)a.M, nb, (uint64_t)a.ldc * esz,
+                     (uint64_t)a.sC * esz, 128 / esz, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
+        mode = 0;
     a.tma_out = mode;
     if (!mode) mc = ma;  // unused
   }
@@ -612,7 +623,7 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   const int grid = units < num_sms() ? (int)units : num_sms();
   {
     TimerScope timer(stream);
-    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, mc, a);
+    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, mc, mx, a);
   }
   if (a.splits > 1) {
     const long long quads = (long long)a.M * ((a.N + 3) / 4);

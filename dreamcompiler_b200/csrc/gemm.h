@@ -24,6 +24,8 @@ struct GemmArgs {
   // Extra destinations with C's layout (pitch ldc) that receive the same
   // output, e.g. other GPUs' buffers through NVLink peer mappings (the
   // tensor-parallel all-gather fused into the epilogue). beta must be 0.
+  // They take the TMA-store epilogue when C and every extra pointer are
+  // 16-byte aligned (ExtraOutMaps), else per-thread stores.
   void* C_extra[7];
   int n_extra;
   // Output path of the epilogue: 0 per-thread stores (any layout, beta, extra
@@ -39,6 +41,21 @@ struct GemmArgs {
   int batch;
   long long sA, sB, sC;
 };
+
+// TMA maps of the extra destinations (GemmArgs::C_extra[e], C's geometry).
+// With the TMA-store epilogue (tma_out 1) every staged box goes to C and then
+// to each extra destination from the same shared-memory buffer: whole
+// 128-byte rows per copy, the write size NVLink peer stores want.
+struct ExtraOutMaps {
+  CUtensorMap m[7];
+};
+
+// Whether every extra destination can take TMA stores (16-byte aligned).
+inline bool extras_tma_aligned(const GemmArgs& a) {
+  for (int e = 0; e < a.n_extra; ++e)
+    if (reinterpret_cast<uintptr_t>(a.C_extra[e]) & 15) return false;
+  return true;
+}
 
 // 2-SM bf16 kernel (gemm2.cu) and the algorithm switch.
 bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B);

@@ -110,7 +110,8 @@ struct Sched2 {
 template <bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ ExtraOutMaps tmX,
+                 GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* out_stage = smem + G2_STAGES * G2_STAGE;
@@ -229,7 +230,10 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;
     uint8_t* my_stage = out_stage + (warp - 2) * 8192;
     uint32_t issued = 0, use = 0;
-    if (lane == 0) tma_prefetch_desc(&tmC);
+    if (lane == 0) {
+      tma_prefetch_desc(&tmC);
+      for (int e = 0; e < args.n_extra; ++e) tma_prefetch_desc(&tmX.m[e]);
+    }
     for (int t = pair; t < num_tiles; t += npairs, ++use) {
       const int buf = use & 1;
       if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
@@ -293,9 +297,11 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) {
           if (args.tma_out == 2)
             tma_reduce_add_2d(&tmC, st, n0, row0);
-          else
+          else {
             tma_store_2d(&tmC, st, n0, row0);
-          bulk_commit();
+            for (int e = 0; e < args.n_extra; ++e) tma_store_2d(&tmX.m[e], st, n0, row0);
+          }
+          bulk_commit();  // one group per staged buffer, all its destinations
         }
         ++issued;
       }
@@ -330,12 +336,13 @@ bool encode_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
 }  // namespace
 
 // Whether the 2-SM kernel serves this bf16 GEMM: A K-major, one output with a
-// TMA-storable layout (beta 0, or 1 with fp32 C), no extra destinations,
-// enough 256 x 256 tiles to occupy the GPU's SM pairs, and K >= 1024 (below
+// TMA-storable layout (beta 0, or 1 with fp32 C), extra destinations only
+// with beta 0 and 16-byte aligned (each staged box is stored to all), enough 256 x 256 tiles to occupy the GPU's SM pairs, and K >= 1024 (below
 // that the single-CTA 128 x 256 tiles measured faster on this GPU: more tiles
 // for the short main loops).
 bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B) {
-  if (a.transA || a.n_extra || a.batch > 1) return false;
+  if (a.transA || a.batch > 1) return false;
+  if (a.n_extra && (a.beta != 0.f || !extras_tma_aligned(a))) return false;
   const int esz = a.c_bf16 ? 2 : 4;
   if ((((uintptr_t)a.C | (uintptr_t)A | (uintptr_t)B) & 15) || ((long long)a.ldc * esz) % 16) return false;
   if (((long long)a.lda * 2) % 16 || ((long long)a.ldb * 2) % 16) return false;
@@ -347,6 +354,7 @@ bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B) {
 cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cudaStream_t stream) {
   const bool b_mn = args.transB == 0;
   CUtensorMap ma{}, mb{}, mc{};
+  ExtraOutMaps mx{};
   if (!encode_2d_bf16(&ma, A, (uint64_t)args.K, (uint64_t)args.M, (uint64_t)args.lda * 2, G2_BK, G2_BM))
     return cudaErrorInvalidValue;
   if (b_mn) {  // B stored [K][N]: boxes of 64 columns x 64 K rows
@@ -369,10 +377,13 @@ cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cud
     const cuuint64_t strides[1] = {(cuuint64_t)a.ldc * esz};
     const cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32};
     const cuuint32_t estr[2] = {1, 1};
-    if (!enc || enc(&mc, a.c_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.C, dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
+    const CUtensorMapDataType cdt = a.c_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if (!enc) return cudaErrorInvalidValue;
+    for (int e = -1; e < a.n_extra; ++e)  // C, then every extra destination
+      if (enc(e < 0 ? &mc : &mx.m[e], cdt, 2, e < 0 ? a.C : a.C_extra[e], dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
   }
   auto kern = b_mn ? gemm2_kernel<true> : gemm2_kernel<false>;
   static bool attr_done[2] = {false, false};
@@ -396,7 +407,7 @@ cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cud
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   TimerScope timer(stream);
-  return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a);
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mx, a);
 }
 
 }  // namespace dgx

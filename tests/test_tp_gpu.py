@@ -38,15 +38,34 @@ def _worker(rank, world, port, mode, out):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     result = {"rank": rank}
     try:
-        M, N, K = 512, 1000, 384
-        orc.set_seed(3)
+        if mode == "wide":
+            # bf16 C with shards wide enough for the 2-SM kernel at 2 ranks
+            # (1-SM tiles beyond): every staged output box goes to all ranks
+            # by TMA stores; 64 sampled rows against the oracle, and every
+            # rank's C byte-identical
+            M, N, K = 4096, 4096, 1024
+            orc.set_seed(4)
+            out_dtype = torch.bfloat16
+        else:
+            M, N, K = 512, 1000, 384
+            orc.set_seed(3)
+            out_dtype = torch.float32
         A = orc.randn(M, K)
         B = orc.randn(K, N)
-        ref = orc.gemm_f64(orc.round_bf16(A).astype(np.float64), orc.round_bf16(B).astype(np.float64))
-        g = tp.ColumnParallelGemm(M, N, K, rank, world, out_dtype=torch.float32)
+        g = tp.ColumnParallelGemm(M, N, K, rank, world, out_dtype=out_dtype)
         Ad = torch.from_numpy(A).cuda().bfloat16()
         Bs = torch.from_numpy(B[:, g.col0:g.col0 + g.ncol].copy()).cuda().bfloat16()
-        if mode == "ok":
+        if mode == "wide":
+            import hashlib
+            for _ in range(2):
+                Cb = g(Ad, Bs)
+            dgx.sync_check()
+            rows = np.random.default_rng(5).choice(M, 64, replace=False)
+            ref = orc.gemm_f64(orc.round_bf16(A[rows]).astype(np.float64), orc.round_bf16(B).astype(np.float64))
+            result["err"] = normwise(Cb.float().cpu().numpy()[rows], ref)
+            result["digest"] = hashlib.sha1(Cb.view(torch.int16).cpu().numpy().tobytes()).hexdigest()
+        elif mode == "ok":
+            ref = orc.gemm_f64(orc.round_bf16(A).astype(np.float64), orc.round_bf16(B).astype(np.float64))
             for _ in range(3):
                 Cf = g(Ad, Bs)
             dgx.sync_check()
@@ -89,6 +108,13 @@ def test_fused_allgather_matches_oracle():
     world, res = _run("ok")
     for r in res:
         assert r["err"] < 1e-2, r
+
+
+def test_fused_allgather_tma_store_path():
+    world, res = _run("wide")
+    for r in res:
+        assert r["err"] < 1e-2, r
+    assert len({r["digest"] for r in res}) == 1, "ranks disagree on C"
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
