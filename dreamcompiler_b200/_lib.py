@@ -62,7 +62,6 @@ SIGNATURES = {
     "dgx_layernorm_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "dgx_layernorm_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "dgx_gemm_gelu": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
-    "dgx_gemm_residual": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp]),
     "dgx_gelu_fwd": (_i, [_vp, _i, _vp, C.c_longlong, _vp]),
     "dgx_gelu_bwd": (_i, [_vp, _i, _vp, _i, _vp, C.c_longlong, _vp]),
     "dgx_embedding_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),

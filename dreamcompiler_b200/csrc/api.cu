@@ -244,36 +244,6 @@ dgx_status dgx_gemm_gelu(const void* A, const void* B, void* C, void* G_or_U, in
   return cuda_status(gemm_bf16_tc(a, A, B, (cudaStream_t)stream), "dgx_gemm_gelu");
 }
 
-dgx_status dgx_gemm_residual(const void* A, const void* B, const float* R, float* C, int M, int N, int K, int lda,
-                             int ldb, int ldc, int transA, int transB, const float* bias, void* stream) {
-  if (M < 0 || N < 0 || K <= 0) return set_error(DGX_EINVAL, "dgx_gemm_residual: size %dx%dx%d", M, N, K);
-  if (M == 0 || N == 0) return DGX_OK;
-  if (!A || !B || !C || !R) return set_error(DGX_EINVAL, "dgx_gemm_residual: null operand");
-  const int min_lda = transA ? M : K, min_ldb = transB ? K : N;
-  if (lda < min_lda || ldb < min_ldb || ldc < N)
-    return set_error(DGX_EINVAL, "dgx_gemm_residual: leading dimension too small (lda %d ldb %d ldc %d)", lda, ldb,
-                     ldc);
-  const size_t span = ((size_t)(M - 1) * ldc + N) * sizeof(float);
-  if ((const char*)R < (const char*)C + span && (const char*)C < (const char*)R + span)
-    return set_error(DGX_EINVAL, "dgx_gemm_residual: R overlaps C");
-  GemmArgs a{};
-  a.M = M;
-  a.N = N;
-  a.K = K;
-  a.lda = lda;
-  a.ldb = ldb;
-  a.ldc = ldc;
-  a.transA = transA ? 1 : 0;
-  a.transB = transB ? 1 : 0;
-  a.C = C;
-  a.bias = bias;
-  a.err = device_error_word();
-  a.resid = R;
-  if (((uintptr_t)C | (uintptr_t)R) & 15 || ((long long)ldc * 4) % 16 || !gemm_tc_supported(a, 2, A, B))
-    return set_error(DGX_EUNSUPPORTED, "dgx_gemm_residual: needs 16-byte aligned operands and pitches");
-  return cuda_status(gemm_bf16_tc(a, A, B, (cudaStream_t)stream), "dgx_gemm_residual");
-}
-
 }  // extern "C"
 
 namespace dgx {

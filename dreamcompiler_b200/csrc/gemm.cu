@@ -280,23 +280,6 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[64];
           tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           if (cw == 64) tmem_ld32(taddr + c + CW32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-          float4 rr[8];  // residual source: this row's 32 fp32 values (loads overlap the TMEM load)
-          if (args.resid) {
-            const float* rrow = args.resid + (long long)m * args.ldc;
-            const int nb0 = tn * BN + c;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int n = nb0 + 4 * k;
-              if (m < args.M && n + 4 <= args.N) {
-                rr[k] = __ldg(reinterpret_cast<const float4*>(rrow + n));
-              } else {
-                float t[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) t[i] = (m < args.M && n + i < args.N) ? rrow[n + i] : 0.f;
-                rr[k] = make_float4(t[0], t[1], t[2], t[3]);
-              }
-            }
-          }
           uint4 uu[8];  // GELU backward: this row's 64 pre-activations (loads overlap the TMEM load)
           if (args.gelu == 2) {
             const __nv_bfloat16* urow = reinterpret_cast<const __nv_bfloat16*>(args.gelu_u) + (long long)m * args.ldc;
@@ -344,10 +327,6 @@ __global__ void __launch_bounds__(192, 1)
               float v = __uint_as_float(r[j]);
               if (args.bias) v += n0 + j < args.N ? args.bias[n0 + j] : 0.f;
               if (args.relu) v = fmaxf(v, 0.f);
-              if (args.resid) {  // R + value: the sum the reduce-add of value into a copy of R gives
-                const float4 q4 = rr[j / 4];
-                v += (j & 3) == 0 ? q4.x : (j & 3) == 1 ? q4.y : (j & 3) == 2 ? q4.z : q4.w;
-              }
               w[j] = __float_as_uint(v);
             }
           }
@@ -639,7 +618,7 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   {
     const int tiles = a.tiles_m * a.tiles_n;
     const int nk_all = (args.K + Cfg::BK - 1) / Cfg::BK;
-    if (a.n_extra == 0 && a.gelu == 0 && !a.resid && nb == 1 && tiles * 2 <= num_sms() && nk_all >= 16) {
+    if (a.n_extra == 0 && a.gelu == 0 && nb == 1 && tiles * 2 <= num_sms() && nk_all >= 16) {
       const int sp = std::min(std::min(num_sms() / tiles, nk_all / 8), 16);
       ldw = (a.N + 3) & ~3;
       if (sp >= 2 && (ws = (float*)library_scratch_slot(kScratchSplitK, (size_t)sp * a.M * ldw * sizeof(float), stream)) !=
@@ -681,8 +660,7 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
                      (uint64_t)a.sC * esz, 128 / esz, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
         mode = 0;
     a.tma_out = mode;
-    // the GELU and residual epilogues exist on the TMA-store path only
-    if ((a.gelu || a.resid) && mode != 1) return cudaErrorInvalidValue;
+    if (a.gelu && mode != 1) return cudaErrorInvalidValue;  // the GELU epilogue exists on the TMA-store path only
     if (!mode) mc = ma;  // unused
   }
   auto kern = gemm_tc_kernel<TF32, A_MN, B_MN, BN_>;

@@ -46,9 +46,6 @@ struct GemmArgs {
   // bf16 [M][ldc] pre-activation.
   int gelu;
   const void* gelu_u;
-  // Residual source (fp32 C, beta 0, single product, TMA stores; 1-SM
-  // kernel): C = resid + value, resid [M][ldc] fp32 (may not alias C).
-  const float* resid;
 };
 
 // TMA maps of the extra destinations (GemmArgs::C_extra[e], C's geometry).

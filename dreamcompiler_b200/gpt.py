@@ -26,7 +26,7 @@ from typing import Dict
 import torch
 
 from . import _lib as L
-from .ops import _stream, flash_bwd_workspace_size, gemm, gemm_gelu, gemm_residual
+from .ops import _stream, flash_bwd_workspace_size, gemm, gemm_gelu
 
 
 @dataclass
@@ -180,12 +180,14 @@ class GPT:
             qp = qkv.data_ptr()
             _c("dgx_flash_fwd_rows", qp, 3 * d, qp + 2 * d, 3 * d, qp + 4 * d, 3 * d, self.att16[l].data_ptr(), d,
                self.lse[l].data_ptr(), B, H, S, hd, hd ** -0.5, 1, s)
-            gemm_residual(self.att16[l], w[f"Wo{l}"], x0, x1, transB=True, bias=p[f"bo{l}"])  # x1 = x0 + att Wo^T + bo
+            x1.copy_(x0)
+            gemm(self.att16[l], w[f"Wo{l}"], transB=True, out=x1, bias=p[f"bo{l}"], beta=1.0)  # x1 = x0 + att Wo^T + bo
             _c("dgx_layernorm_fwd", x1.data_ptr(), h2.data_ptr(), self.mu[2 * l + 1].data_ptr(),
                self.rs[2 * l + 1].data_ptr(), R, d, s)
             # u = h2 W1^T + b1 (kept for the backward) and g = gelu(u), one kernel
             gemm_gelu(h2, w[f"W1{l}"], self.u16[l], self.g16[l], mode=L.DGX_GELU_FWD, transB=True, bias=p[f"b1{l}"])
-            gemm_residual(self.g16[l], w[f"W2{l}"], x1, x2, transB=True, bias=p[f"b2{l}"])  # x2 = x1 + g W2^T + b2
+            x2.copy_(x1)
+            gemm(self.g16[l], w[f"W2{l}"], transB=True, out=x2, bias=p[f"b2{l}"], beta=1.0)
         xL, hf = self.x[2 * c.n_layer], self.h16[2 * c.n_layer]
         _c("dgx_layernorm_fwd", xL.data_ptr(), hf.data_ptr(), self.mu[-1].data_ptr(), self.rs[-1].data_ptr(), R, d, s)
         gemm(hf, w["Wout"], transB=True, out=self.logits, bias=p["bout"])

@@ -87,22 +87,6 @@ def gemm_gelu(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, aux: torch.Te
     return out
 
 
-def gemm_residual(A: torch.Tensor, B: torch.Tensor, R: torch.Tensor, out: torch.Tensor, *, transA: bool = False,
-                  transB: bool = False, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """out = R + op(A) @ op(B) (+bias) (dgx_gemm_residual): bf16 A, B; fp32 R
-    and out [M, N] with one pitch, not overlapping."""
-    assert A.dtype == B.dtype == torch.bfloat16 and R.dtype == out.dtype == torch.float32
-    assert A.stride(1) == 1 and B.stride(1) == 1 and out.stride(1) == 1 and R.stride(1) == 1
-    M, K = (A.shape[1], A.shape[0]) if transA else (A.shape[0], A.shape[1])
-    N = B.shape[0] if transB else B.shape[1]
-    assert out.shape == (M, N) and R.shape == (M, N) and R.stride(0) == out.stride(0)
-    if bias is not None:
-        assert bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == N
-    L.call("dgx_gemm_residual", A.data_ptr(), B.data_ptr(), R.data_ptr(), out.data_ptr(), M, N, K, A.stride(0),
-           B.stride(0), out.stride(0), int(transA), int(transB), _ptr(bias), _stream(A))
-    return out
-
-
 def bmm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     assert A.dim() == 3 and B.dim() == 3 and A.is_contiguous() and B.is_contiguous()
     batch, M, K = A.shape

@@ -283,17 +283,6 @@ dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rst
 enum { DGX_GELU_FWD = 1, DGX_GELU_BWD = 2 };
 dgx_status dgx_gemm_gelu(const void* A, const void* B, void* C, void* G_or_U, int M, int N, int K, int lda, int ldb,
                          int ldc, int transA, int transB, const float* bias, int mode, void* stream);
-/*
- * Residual linear: C = R + op(A).op(B) (+ bias), bf16 A and B, fp32 R and C
- * [M][ldc] (R may not overlap C). The pre-LN block's `x + linear(h)`
- * (the reference's tensor add of a dream_linear result,
- * runtime/ops/elementwise.inc:1432-1521) in one kernel: the residual is read
- * in the epilogue instead of first copying R into C and accumulating with
- * beta = 1 (same fp32 sum). Needs the tensor-core path (16-byte aligned
- * pointers and pitches; DGX_EUNSUPPORTED otherwise).
- */
-dgx_status dgx_gemm_residual(const void* A, const void* B, const float* R, float* C, int M, int N, int K, int lda,
-                             int ldb, int ldc, int transA, int transB, const float* bias, void* stream);
 /* y16 = bf16(gelu(x)), tanh form (runtime/io/builtins.inc:548-560); x DGX_F32 or DGX_BF16. */
 dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream);
 /* dx16 = bf16(gelu'(x) * dy) (runtime/ops/autograd.inc:293-303); x, dy DGX_F32 or DGX_BF16. */

@@ -134,7 +134,7 @@ def test_gelu_kernels_against_oracle(dgx, n):
     assert nw(dx.double().cpu().numpy(), rdx) < 1e-2
 
 
-@pytest.mark.parametrize("M,N,K,bias", [(2048, 1536, 384, True), (8192, 384, 1536, False), (300, 200, 136, True)])
+@pytest.mark.parametrize("M,N,K,bias", [(2048, 1536, 384, True), (2048, 384, 1536, False), (300, 200, 136, True)])
 def test_gemm_gelu_epilogue_matches_separate_passes(dgx, M, N, K, bias):
     """dgx_gemm_gelu: the MLP GEMM with GELU in its epilogue equals dgx_gemm
     followed by dgx_gelu_fwd / dgx_gelu_bwd on the bf16 tensors: the
@@ -170,24 +170,6 @@ def test_gemm_gelu_epilogue_matches_separate_passes(dgx, M, N, K, bias):
     # and against the f64 oracle's GELU of the same bf16 pre-activations
     uf = u.double().cpu().numpy()
     assert np.abs(gl.double().cpu().numpy() - G.gelu(uf)).max() / np.abs(G.gelu(uf)).max() < 1e-2
-
-
-@pytest.mark.parametrize("M,N,K,bias", [(8192, 384, 1536, True), (8192, 384, 384, False), (300, 200, 136, True)])
-def test_gemm_residual_matches_copy_and_accumulate(dgx, M, N, K, bias):
-    """dgx_gemm_residual (x + linear(h) in one kernel) equals copying R into C
-    and accumulating with beta = 1, bit for bit (the same fp32 sum), on full
-    and ragged tiles (shapes with enough tiles that neither call splits K)."""
-    g = torch.Generator(device="cuda").manual_seed(7 * M + N + K)
-    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
-    b = torch.randn(N, device="cuda", generator=g) if bias else None
-    R = torch.randn(M, N, device="cuda", generator=g)
-    out = torch.full((M, N), float("nan"), device="cuda")
-    dgx.gemm_residual(A, W, R, out, transB=True, bias=b)
-    ref = R.clone()
-    dgx.gemm(A, W, transB=True, out=ref, bias=b, beta=1.0)
-    dgx.sync_check()
-    assert torch.equal(out, ref)
 
 
 @pytest.mark.parametrize("dtype,R,N", [("bf16", 16384, 1536), ("bf16", 16384, 384), ("f32", 16384, 65),
