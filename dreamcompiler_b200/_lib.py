@@ -17,7 +17,6 @@ DGX_OK, DGX_EINVAL, DGX_ECUDA, DGX_ENCCL, DGX_ETIMEOUT, DGX_EUNSUPPORTED, DGX_EN
 DGX_F32, DGX_BF16, DGX_I8, DGX_F64 = 0, 1, 2, 3
 DGX_EPI_NONE, DGX_EPI_BIAS, DGX_EPI_BIAS_RELU, DGX_EPI_RELU = 0, 1, 2, 3
 DGX_F32_3XTF32, DGX_F32_FFMA = 0, 1
-DGX_GELU_FWD, DGX_GELU_BWD = 1, 2
 
 STATUS_NAMES = {0: "DGX_OK", 1: "DGX_EINVAL", 2: "DGX_ECUDA", 3: "DGX_ENCCL", 4: "DGX_ETIMEOUT",
                 5: "DGX_EUNSUPPORTED", 6: "DGX_ENOMEM"}
@@ -61,7 +60,6 @@ SIGNATURES = {
     "dgx_quantize_rows_i8": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "dgx_layernorm_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "dgx_layernorm_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
-    "dgx_gemm_gelu": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
     "dgx_gelu_fwd": (_i, [_vp, _i, _vp, C.c_longlong, _vp]),
     "dgx_gelu_bwd": (_i, [_vp, _i, _vp, _i, _vp, C.c_longlong, _vp]),
     "dgx_embedding_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),

@@ -210,40 +210,6 @@ dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, 
   return gemm_run(a, A, B, ab_type, f32_mode, workspace, workspace_bytes, s);
 }
 
-dgx_status dgx_gemm_gelu(const void* A, const void* B, void* C, void* G_or_U, int M, int N, int K, int lda, int ldb,
-                         int ldc, int transA, int transB, const float* bias, int mode, void* stream) {
-  if (M < 0 || N < 0 || K <= 0) return set_error(DGX_EINVAL, "dgx_gemm_gelu: size %dx%dx%d", M, N, K);
-  if (M == 0 || N == 0) return DGX_OK;
-  if (!A || !B || !C || !G_or_U) return set_error(DGX_EINVAL, "dgx_gemm_gelu: null operand");
-  if (mode != DGX_GELU_FWD && mode != DGX_GELU_BWD) return set_error(DGX_EINVAL, "dgx_gemm_gelu: mode %d", mode);
-  const int min_lda = transA ? M : K, min_ldb = transB ? K : N;
-  if (lda < min_lda || ldb < min_ldb || ldc < N)
-    return set_error(DGX_EINVAL, "dgx_gemm_gelu: leading dimension too small (lda %d ldb %d ldc %d)", lda, ldb, ldc);
-  GemmArgs a{};
-  a.M = M;
-  a.N = N;
-  a.K = K;
-  a.lda = lda;
-  a.ldb = ldb;
-  a.ldc = ldc;
-  a.transA = transA ? 1 : 0;
-  a.transB = transB ? 1 : 0;
-  a.C = C;
-  a.c_bf16 = 1;
-  a.bias = bias;
-  a.err = device_error_word();
-  a.gelu = mode;
-  if (mode == DGX_GELU_FWD) {
-    a.C_extra[0] = G_or_U;
-    a.n_extra = 1;
-  } else {
-    a.gelu_u = G_or_U;
-  }
-  if (((uintptr_t)C | (uintptr_t)G_or_U) & 15 || ((long long)ldc * 2) % 16 || !gemm_tc_supported(a, 2, A, B))
-    return set_error(DGX_EUNSUPPORTED, "dgx_gemm_gelu: needs 16-byte aligned operands and pitches");
-  return cuda_status(gemm_bf16_tc(a, A, B, (cudaStream_t)stream), "dgx_gemm_gelu");
-}
-
 }  // extern "C"
 
 namespace dgx {

@@ -21,7 +21,6 @@
 #include <algorithm>
 
 #include "sm100.cuh"
-#include "gelu.cuh"
 #include "gemm.h"
 
 namespace dgx {
@@ -71,24 +70,6 @@ __device__ __forceinline__ uint32_t kstep_offset(int kk) {
   // K-major: advance 32 bytes inside the 128-byte swizzled row.
   // MN-major: advance (32/ESZ) K rows of 128 bytes each.
   return MN ? (uint32_t)kk * (32 / ESZ) * 128 : (uint32_t)kk * 32;
-}
-
-__device__ __forceinline__ uint32_t u4_word(const uint4& v, int i) {
-  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
-// Eight bf16 values of row `row` from column n (zero past n_end), 16-byte
-// load when all eight are in range.
-__device__ __forceinline__ uint4 ld_bf16x8_guarded(const __nv_bfloat16* row, int n, int n_end) {
-  if (n + 8 <= n_end) return __ldg(reinterpret_cast<const uint4*>(row + n));
-  uint32_t w[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    if (n + i < n_end) {
-      const uint32_t b = __bfloat16_as_ushort(row[n + i]);
-      w[i / 2] |= (i & 1) ? (b << 16) : b;
-    }
-  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <bool TF32, bool A_MN, bool B_MN, int BN_>
@@ -280,13 +261,6 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[64];
           tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           if (cw == 64) tmem_ld32(taddr + c + CW32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-          uint4 uu[8];  // GELU backward: this row's 64 pre-activations (loads overlap the TMEM load)
-          if (args.gelu == 2) {
-            const __nv_bfloat16* urow = reinterpret_cast<const __nv_bfloat16*>(args.gelu_u) + (long long)m * args.ldc;
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              uu[k] = m < args.M ? ld_bf16x8_guarded(urow, tn * BN + c + 8 * k, args.N) : make_uint4(0, 0, 0, 0);
-          }
           tmem_ld_wait();
           if (c + cw >= BN) {  // last loads of this accumulator: hand it back to the MMA warp
             tc_fence_before();
@@ -314,11 +288,6 @@ __global__ void __launch_bounds__(192, 1)
                 v0 = fmaxf(v0, 0.f);
                 v1 = fmaxf(v1, 0.f);
               }
-              if (args.gelu == 2) {  // gelu'(u) * bf16(value), as the separate pass on a bf16 gradient
-                const uint32_t uw = u4_word(uu[j / 8], (j / 2) & 3);
-                v0 = gelu_grad_fast(bf_lo(uw)) * __bfloat162float(__float2bfloat16_rn(v0));
-                v1 = gelu_grad_fast(bf_hi(uw)) * __bfloat162float(__float2bfloat16_rn(v1));
-              }
               w[j / 2] = pack_bf16x2(v0, v1);
             }
           } else {
@@ -344,30 +313,11 @@ __global__ void __launch_bounds__(192, 1)
               tma_reduce_add_3d(&tmC, st, n0, tm * BM + q * 32, bz);
             else {
               tma_store_3d(&tmC, st, n0, tm * BM + q * 32, bz);
-              for (int e = args.gelu == 1 ? 1 : 0; e < args.n_extra; ++e)
-                tma_store_3d(&tmX.m[e], st, n0, tm * BM + q * 32, bz);
+              for (int e = 0; e < args.n_extra; ++e) tma_store_3d(&tmX.m[e], st, n0, tm * BM + q * 32, bz);
             }
             bulk_commit();  // one group per staged buffer, all its destinations
           }
           ++issued;
-          if (args.gelu == 1) {  // GELU forward: gelu(bf16 value) to the first extra destination
-            uint8_t* st2 = my_stage + (issued & 1) * 4096;
-            if (lane == 0 && issued >= 2) bulk_wait_read1();
-            __syncwarp();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = pack_bf16x2(gelu_fast(bf_lo(w[i])), gelu_fast(bf_hi(w[i])));
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              *reinterpret_cast<uint4*>(st2 + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-                  make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_3d(&tmX.m[0], st2, n0, tm * BM + q * 32, bz);
-              bulk_commit();
-            }
-            ++issued;
-          }
         }
         (void)m;
       } else {
@@ -618,7 +568,7 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   {
     const int tiles = a.tiles_m * a.tiles_n;
     const int nk_all = (args.K + Cfg::BK - 1) / Cfg::BK;
-    if (a.n_extra == 0 && a.gelu == 0 && nb == 1 && tiles * 2 <= num_sms() && nk_all >= 16) {
+    if (a.n_extra == 0 && nb == 1 && tiles * 2 <= num_sms() && nk_all >= 16) {
       const int sp = std::min(std::min(num_sms() / tiles, nk_all / 8), 16);
       ldw = (a.N + 3) & ~3;
       if (sp >= 2 && (ws = (float*)library_scratch_slot(kScratchSplitK, (size_t)sp * a.M * ldw * sizeof(float), stream)) !=
@@ -660,7 +610,6 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
                      (uint64_t)a.sC * esz, 128 / esz, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
         mode = 0;
     a.tma_out = mode;
-    if (a.gelu && mode != 1) return cudaErrorInvalidValue;  // the GELU epilogue exists on the TMA-store path only
     if (!mode) mc = ma;  // unused
   }
   auto kern = gemm_tc_kernel<TF32, A_MN, B_MN, BN_>;

@@ -40,12 +40,6 @@ struct GemmArgs {
   // a single product.
   int batch;
   long long sA, sB, sC;
-  // GELU epilogue of the GPT step's MLP GEMMs (bf16 C, single product, TMA
-  // stores; 1-SM kernel): 1 = C gets the value and C_extra[0] (n_extra 1)
-  // gets gelu(bf16 value); 2 = C gets gelu'(gelu_u) * bf16(value), gelu_u a
-  // bf16 [M][ldc] pre-activation.
-  int gelu;
-  const void* gelu_u;
 };
 
 // TMA maps of the extra destinations (GemmArgs::C_extra[e], C's geometry).

@@ -341,7 +341,7 @@ bool encode_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
 // that the single-CTA 128 x 256 tiles measured faster on this GPU: more tiles
 // for the short main loops).
 bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B) {
-  if (a.transA || a.batch > 1 || a.gelu) return false;
+  if (a.transA || a.batch > 1) return false;
   if (a.n_extra && (a.beta != 0.f || !extras_tma_aligned(a))) return false;
   const int esz = a.c_bf16 ? 2 : 4;
   if ((((uintptr_t)a.C | (uintptr_t)A | (uintptr_t)B) & 15) || ((long long)a.ldc * esz) % 16) return false;

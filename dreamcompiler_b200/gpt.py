@@ -4,12 +4,11 @@ The model is the one a Dream program builds from the reference ops (see the
 restatement in oracle/gpt_oracle.py): token + position embedding, L pre-LN
 blocks of causal multi-head attention and a 4x GELU(tanh) MLP, a final
 layer_norm, a linear head, log_softmax + nll_loss, and AdamW. Every `linear`
-runs on dgx_gemm (bf16 operands, fp32 accumulate and bias epilogue; the
-MLP's first linear and its gradient on dgx_gemm_gelu, GELU in the epilogue), the
+runs on dgx_gemm (bf16 operands, fp32 accumulate and bias epilogue), the
 attention on dgx_flash_fwd_rows / dgx_flash_bwd_rows (heads read from and
 written to token rows), everything else on the libdgx
-device ops (dgx_layernorm_*, dgx_embedding_*, dgx_softmax_nll, dgx_colsum,
-dgx_adamw). Parameters, gradients and
+device ops (dgx_layernorm_*, dgx_gelu_*, dgx_embedding_*, dgx_softmax_nll,
+dgx_colsum, dgx_adamw, the head layout permutes). Parameters, gradients and
 AdamW state are fp32; the GEMMs read bf16 copies of the weights refreshed
 after each update. The residual stream and its gradient stay fp32; tensors
 whose only consumers read bf16 (the QKV projection, the MLP pre-activation
@@ -26,7 +25,7 @@ from typing import Dict
 import torch
 
 from . import _lib as L
-from .ops import _stream, flash_bwd_workspace_size, gemm, gemm_gelu
+from .ops import _stream, flash_bwd_workspace_size, gemm
 
 
 @dataclass
@@ -127,6 +126,7 @@ class GPT:
         self.dx = torch.empty(R, d, device=dev, dtype=f32)
         self.dx16 = torch.empty(R, d, device=dev, dtype=bf16)
         self.dh = torch.empty(R, d, device=dev, dtype=f32)
+        self.dg16 = torch.empty(R, 4 * d, device=dev, dtype=bf16)
         self.du16 = torch.empty(R, 4 * d, device=dev, dtype=bf16)
         self.dqkv16 = torch.empty(R, 3 * d, device=dev, dtype=bf16)
         self.datt16 = torch.empty(R, d, device=dev, dtype=bf16)
@@ -184,8 +184,8 @@ class GPT:
             gemm(self.att16[l], w[f"Wo{l}"], transB=True, out=x1, bias=p[f"bo{l}"], beta=1.0)  # x1 = x0 + att Wo^T + bo
             _c("dgx_layernorm_fwd", x1.data_ptr(), h2.data_ptr(), self.mu[2 * l + 1].data_ptr(),
                self.rs[2 * l + 1].data_ptr(), R, d, s)
-            # u = h2 W1^T + b1 (kept for the backward) and g = gelu(u), one kernel
-            gemm_gelu(h2, w[f"W1{l}"], self.u16[l], self.g16[l], mode=L.DGX_GELU_FWD, transB=True, bias=p[f"b1{l}"])
+            gemm(h2, w[f"W1{l}"], transB=True, out=self.u16[l], bias=p[f"b1{l}"])
+            _c("dgx_gelu_fwd", self.u16[l].data_ptr(), L.DGX_BF16, self.g16[l].data_ptr(), self.u16[l].numel(), s)
             x2.copy_(x1)
             gemm(self.g16[l], w[f"W2{l}"], transB=True, out=x2, bias=p[f"b2{l}"], beta=1.0)
         xL, hf = self.x[2 * c.n_layer], self.h16[2 * c.n_layer]
@@ -206,9 +206,11 @@ class GPT:
             h, h2 = self.h16[2 * l], self.h16[2 * l + 1]
             # MLP: x2 = x1 + gelu(h2 W1^T + b1) W2^T + b2
             conv16(self.dx, self.dx16)
-            gemm_gelu(self.dx16, w[f"W2{l}"], self.du16, self.u16[l], mode=L.DGX_GELU_BWD)  # du = gelu'(u) * dx W2
+            gemm(self.dx16, w[f"W2{l}"], out=self.dg16)                   # dg = dx W2
             gemm(self.dx16, self.g16[l], transA=True, out=g[f"W2{l}"])     # dW2 = dx^T g
             _c("dgx_colsum", self.dx.data_ptr(), L.DGX_F32, g[f"b2{l}"].data_ptr(), R, d, 0, s)
+            _c("dgx_gelu_bwd", self.u16[l].data_ptr(), L.DGX_BF16, self.dg16.data_ptr(), L.DGX_BF16,
+               self.du16.data_ptr(), self.du16.numel(), s)
             gemm(self.du16, w[f"W1{l}"], out=self.dh)                     # dh2 = du W1
             gemm(self.du16, h2, transA=True, out=g[f"W1{l}"])              # dW1 = du^T h2
             _c("dgx_colsum", self.du16.data_ptr(), L.DGX_BF16, g[f"b1{l}"].data_ptr(), R, 4 * d, 0, s)

@@ -69,24 +69,6 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, transA: bool = False, transB: bool
     return out
 
 
-def gemm_gelu(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, aux: torch.Tensor, *, mode: int,
-              transA: bool = False, transB: bool = False, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """bf16 GEMM with the MLP's GELU in the epilogue (dgx_gemm_gelu).
-    mode DGX_GELU_FWD: out = op(A) @ op(B) (+bias), aux = gelu(out).
-    mode DGX_GELU_BWD: out = gelu'(aux) * (op(A) @ op(B) (+bias)), aux the
-    forward's pre-activation. out and aux are bf16 [M, N] with one pitch."""
-    assert A.dtype == B.dtype == out.dtype == aux.dtype == torch.bfloat16
-    assert A.stride(1) == 1 and B.stride(1) == 1 and out.stride(1) == 1 and aux.stride(1) == 1
-    M, K = (A.shape[1], A.shape[0]) if transA else (A.shape[0], A.shape[1])
-    N = B.shape[0] if transB else B.shape[1]
-    assert out.shape == (M, N) and aux.shape == (M, N) and aux.stride(0) == out.stride(0)
-    if bias is not None:
-        assert bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == N
-    L.call("dgx_gemm_gelu", A.data_ptr(), B.data_ptr(), out.data_ptr(), aux.data_ptr(), M, N, K, A.stride(0),
-           B.stride(0), out.stride(0), int(transA), int(transB), _ptr(bias), int(mode), _stream(A))
-    return out
-
-
 def bmm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     assert A.dim() == 3 and B.dim() == 3 and A.is_contiguous() and B.is_contiguous()
     batch, M, K = A.shape

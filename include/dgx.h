@@ -264,25 +264,6 @@ dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd
  * (runtime/ops/autograd.inc:453-470); accumulate = 1 adds into dx. */
 dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rstd, const float* dy, float* dx, int R,
                              int C, int accumulate, void* stream);
-/*
- * bf16 GEMM with the GELU of an MLP layer in its epilogue (the GPT step's
- * linear -> gelu -> linear, runtime/io/builtins.inc:548-560, and the "gelu"
- * backward branch, runtime/ops/autograd.inc:293-303), so neither direction
- * runs a separate element-wise pass. A, B, C, G_or_U are bf16 with the
- * dgx_gemm meaning of lda/ldb/ldc and transA/transB; bias is optional (fp32
- * [N]); beta is 0.
- *   mode DGX_GELU_FWD: C = bf16(op(A).op(B) + bias) (the pre-activation the
- *       backward needs) and G = bf16(gelu(C)) (pitch ldc), one kernel.
- *   mode DGX_GELU_BWD: C = bf16(gelu'(U) * bf16(op(A).op(B) + bias)), U the
- *       forward's pre-activation (pitch ldc): the gradient of the MLP's first
- *       GEMM output straight from dY.W2.
- * Same values as dgx_gemm followed by dgx_gelu_fwd / dgx_gelu_bwd on bf16
- * tensors. Needs the tensor-core path: 16-byte aligned pointers and pitches
- * (DGX_EUNSUPPORTED otherwise).
- */
-enum { DGX_GELU_FWD = 1, DGX_GELU_BWD = 2 };
-dgx_status dgx_gemm_gelu(const void* A, const void* B, void* C, void* G_or_U, int M, int N, int K, int lda, int ldb,
-                         int ldc, int transA, int transB, const float* bias, int mode, void* stream);
 /* y16 = bf16(gelu(x)), tanh form (runtime/io/builtins.inc:548-560); x DGX_F32 or DGX_BF16. */
 dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream);
 /* dx16 = bf16(gelu'(x) * dy) (runtime/ops/autograd.inc:293-303); x, dy DGX_F32 or DGX_BF16. */

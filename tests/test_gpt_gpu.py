@@ -134,44 +134,6 @@ def test_gelu_kernels_against_oracle(dgx, n):
     assert nw(dx.double().cpu().numpy(), rdx) < 1e-2
 
 
-@pytest.mark.parametrize("M,N,K,bias", [(2048, 1536, 384, True), (2048, 384, 1536, False), (300, 200, 136, True)])
-def test_gemm_gelu_epilogue_matches_separate_passes(dgx, M, N, K, bias):
-    """dgx_gemm_gelu: the MLP GEMM with GELU in its epilogue equals dgx_gemm
-    followed by dgx_gelu_fwd / dgx_gelu_bwd on the bf16 tensors: the
-    pre-activation bit for bit, gelu(u) and gelu'(u) * bf16(dY.W) within one
-    bf16 ulp (same formula, evaluated in another kernel); ragged shapes take
-    the guarded loads and clipped TMA stores."""
-    from dreamcompiler_b200 import _lib as L
-    g = torch.Generator(device="cuda").manual_seed(M + N + K)
-    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
-    b = torch.randn(N, device="cuda", generator=g) if bias else None
-    s = torch.cuda.current_stream().cuda_stream
-    one_ulp = lambda got, ref: bool(((got.float() - ref.float()).abs() <= ref.float().abs() * 2 ** -7 + 1e-30).all())
-    # forward: u = A W^T + b, g = gelu(u)
-    u, gl = (torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for _ in range(2))
-    dgx.gemm_gelu(A, W, u, gl, mode=L.DGX_GELU_FWD, transB=True, bias=b)
-    u_ref = dgx.gemm(A, W, transB=True, bias=b, out_dtype=torch.bfloat16)
-    g_ref = torch.empty_like(u_ref)
-    L.call("dgx_gelu_fwd", u_ref.data_ptr(), L.DGX_BF16, g_ref.data_ptr(), u_ref.numel(), s)
-    dgx.sync_check()
-    assert torch.equal(u, u_ref)
-    assert one_ulp(gl, g_ref)
-    # backward: du = gelu'(u) * bf16(dY W2), dY [M][K'] with W2 [K'][N]
-    dY = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    W2 = (torch.randn(K, N, device="cuda", generator=g) / K ** 0.5).bfloat16()
-    du = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    dgx.gemm_gelu(dY, W2, du, u, mode=L.DGX_GELU_BWD)
-    dg_ref = dgx.gemm(dY, W2, out_dtype=torch.bfloat16)
-    du_ref = torch.empty_like(dg_ref)
-    L.call("dgx_gelu_bwd", u.data_ptr(), L.DGX_BF16, dg_ref.data_ptr(), L.DGX_BF16, du_ref.data_ptr(), du.numel(), s)
-    dgx.sync_check()
-    assert one_ulp(du, du_ref)
-    # and against the f64 oracle's GELU of the same bf16 pre-activations
-    uf = u.double().cpu().numpy()
-    assert np.abs(gl.double().cpu().numpy() - G.gelu(uf)).max() / np.abs(G.gelu(uf)).max() < 1e-2
-
-
 @pytest.mark.parametrize("dtype,R,N", [("bf16", 16384, 1536), ("bf16", 16384, 384), ("f32", 16384, 65),
                                        ("f32", 1000, 384), ("bf16", 77, 24)])
 def test_colsum_kernels(dgx, dtype, R, N):
