@@ -72,7 +72,9 @@ __device__ __forceinline__ uint32_t kstep_offset(int kk) {
   return MN ? (uint32_t)kk * (32 / ESZ) * 128 : (uint32_t)kk * 32;
 }
 
-template <bool TF32, bool A_MN, bool B_MN, int BN_>
+// EXTRA: the TMA-store epilogue also stores every staged box to the extra
+// destinations (tmX); plain instantiations carry none of that code.
+template <bool TF32, bool A_MN, bool B_MN, int BN_, bool EXTRA = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
@@ -242,7 +244,8 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t issued = 0;  // stores issued by this warp: buffer = issued & 1
     if (args.tma_out && lane == 0) {
       tma_prefetch_desc(&tmC);
-      for (int e = 0; e < args.n_extra; ++e) tma_prefetch_desc(&tmX.m[e]);
+      if (EXTRA)
+        for (int e = 0; e < args.n_extra; ++e) tma_prefetch_desc(&tmX.m[e]);
     }
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++use) {
       const int buf = use & 1;
@@ -313,7 +316,8 @@ __global__ void __launch_bounds__(192, 1)
               tma_reduce_add_3d(&tmC, st, n0, tm * BM + q * 32, bz);
             else {
               tma_store_3d(&tmC, st, n0, tm * BM + q * 32, bz);
-              for (int e = 0; e < args.n_extra; ++e) tma_store_3d(&tmX.m[e], st, n0, tm * BM + q * 32, bz);
+              if (EXTRA)
+                for (int e = 0; e < args.n_extra; ++e) tma_store_3d(&tmX.m[e], st, n0, tm * BM + q * 32, bz);
             }
             bulk_commit();  // one group per staged buffer, all its destinations
           }
@@ -595,7 +599,10 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
     const bool aligned = ((uintptr_t)a.C & 15) == 0 && ((long long)a.ldc * esz) % 16 == 0 &&
                          (nb == 1 || (a.sC * esz) % 16 == 0);
     int mode = 0;
-    if (aligned && extras_tma_aligned(a)) {
+    // TMA stores to extra destinations: bf16 operands with A K-major only
+    // (the column-parallel GEMM); other extras take per-thread stores.
+    const bool extra_ok = a.n_extra == 0 || (!TF32 && !A_MN && extras_tma_aligned(a));
+    if (aligned && extra_ok) {
       if (a.beta == 0.f)
         mode = 1;
       else if (a.n_extra == 0 && a.beta == 1.f && !a.c_bf16 && !a.relu)
@@ -612,12 +619,16 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
     a.tma_out = mode;
     if (!mode) mc = ma;  // unused
   }
-  auto kern = gemm_tc_kernel<TF32, A_MN, B_MN, BN_>;
-  static bool attr_done = false;  // per template instantiation
-  if (!attr_done) {
+  auto kern = gemm_tc_kernel<TF32, A_MN, B_MN, BN_, false>;
+  const bool extra = a.tma_out == 1 && a.n_extra > 0;
+  if constexpr (!TF32 && !A_MN) {
+    if (extra) kern = gemm_tc_kernel<TF32, A_MN, B_MN, BN_, true>;
+  }
+  static bool attr_done[2] = {false, false};  // per template instantiation
+  if (!attr_done[extra]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_done[extra] = true;
   }
   const long long units = (long long)a.tiles_m * a.tiles_n * a.splits * nb;
   const int grid = units < num_sms() ? (int)units : num_sms();

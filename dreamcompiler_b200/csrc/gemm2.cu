@@ -107,7 +107,8 @@ struct Sched2 {
   }
 };
 
-template <bool B_MN>
+// EXTRA: every staged box also goes to the extra destinations (tmX).
+template <bool B_MN, bool EXTRA>
 __global__ void __launch_bounds__(192, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ ExtraOutMaps tmX,
@@ -232,7 +233,8 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t issued = 0, use = 0;
     if (lane == 0) {
       tma_prefetch_desc(&tmC);
-      for (int e = 0; e < args.n_extra; ++e) tma_prefetch_desc(&tmX.m[e]);
+      if (EXTRA)
+        for (int e = 0; e < args.n_extra; ++e) tma_prefetch_desc(&tmX.m[e]);
     }
     for (int t = pair; t < num_tiles; t += npairs, ++use) {
       const int buf = use & 1;
@@ -299,7 +301,8 @@ __global__ void __launch_bounds__(192, 1)
             tma_reduce_add_2d(&tmC, st, n0, row0);
           else {
             tma_store_2d(&tmC, st, n0, row0);
-            for (int e = 0; e < args.n_extra; ++e) tma_store_2d(&tmX.m[e], st, n0, row0);
+            if (EXTRA)
+              for (int e = 0; e < args.n_extra; ++e) tma_store_2d(&tmX.m[e], st, n0, row0);
           }
           bulk_commit();  // one group per staged buffer, all its destinations
         }
@@ -337,12 +340,13 @@ bool encode_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
 
 // Whether the 2-SM kernel serves this bf16 GEMM: A K-major, one output with a
 // TMA-storable layout (beta 0, or 1 with fp32 C), extra destinations only
-// with beta 0 and 16-byte aligned (each staged box is stored to all), enough 256 x 256 tiles to occupy the GPU's SM pairs, and K >= 1024 (below
-// that the single-CTA 128 x 256 tiles measured faster on this GPU: more tiles
-// for the short main loops).
+// with beta 0, B stored [K][N] and 16-byte aligned pointers (each staged box
+// is stored to all), enough 256 x 256 tiles to occupy the GPU's SM pairs, and
+// K >= 1024 (below that the single-CTA 128 x 256 tiles measured faster on
+// this GPU: more tiles for the short main loops).
 bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B) {
   if (a.transA || a.batch > 1) return false;
-  if (a.n_extra && (a.beta != 0.f || !extras_tma_aligned(a))) return false;
+  if (a.n_extra && (a.beta != 0.f || a.transB || !extras_tma_aligned(a))) return false;
   const int esz = a.c_bf16 ? 2 : 4;
   if ((((uintptr_t)a.C | (uintptr_t)A | (uintptr_t)B) & 15) || ((long long)a.ldc * esz) % 16) return false;
   if (((long long)a.lda * 2) % 16 || ((long long)a.ldb * 2) % 16) return false;
@@ -385,12 +389,14 @@ cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cud
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
   }
-  auto kern = b_mn ? gemm2_kernel<true> : gemm2_kernel<false>;
-  static bool attr_done[2] = {false, false};
-  if (!attr_done[b_mn]) {
+  const bool extra = a.n_extra > 0;  // B stored [K][N] (gemm2_eligible)
+  auto kern = extra ? gemm2_kernel<true, true> : b_mn ? gemm2_kernel<true, false> : gemm2_kernel<false, false>;
+  const int variant = extra ? 2 : b_mn;
+  static bool attr_done[3] = {false, false, false};
+  if (!attr_done[variant]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM);
     if (e != cudaSuccess) return e;
-    attr_done[b_mn] = true;
+    attr_done[variant] = true;
   }
   const int tiles = a.tiles_m * a.tiles_n;
   const int pairs = std::min(tiles, num_sms() / 2);
