@@ -315,6 +315,7 @@ __global__ void colsum_partial_vec_kernel(const T* __restrict__ dy, float* __res
 #pragma unroll
   for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
   if (cv * VEC < N)
+#pragma unroll 4
     for (int r = r0 + ty; r < r1; r += 8) {
       const uint4 w = __ldg(reinterpret_cast<const uint4*>(dy + (size_t)r * N) + cv);
       if constexpr (sizeof(T) == 2) {
@@ -345,11 +346,32 @@ __global__ void colsum_partial_vec_kernel(const T* __restrict__ dy, float* __res
   }
 }
 
+// db[c] (+)= sum over slices of part[k][c]. A block of 8 warps owns 32
+// columns: warp w sums slices w, w+8, ... (four independent partial sums so
+// four loads are in flight), then warp 0 adds the 8 warp sums in order. The
+// order is fixed, so the result is the same on every run.
 __global__ void colsum_final_kernel(const float* __restrict__ part, float* __restrict__ db, int N, int accumulate,
                                     int slices) {
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < N; c += gridDim.x * blockDim.x) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (c < N) {
+    int k = w;
+    for (; k + 24 < slices; k += 32) {
+      s0 += part[(size_t)k * N + c];
+      s1 += part[(size_t)(k + 8) * N + c];
+      s2 += part[(size_t)(k + 16) * N + c];
+      s3 += part[(size_t)(k + 24) * N + c];
+    }
+    for (; k < slices; k += 8) s0 += part[(size_t)k * N + c];
+  }
+  red[w][lane] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (w == 0 && c < N) {
     float s = 0.f;
-    for (int k = 0; k < slices; ++k) s += part[(size_t)k * N + c];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += red[j][lane];
     db[c] = accumulate ? db[c] + s : s;
   }
 }
@@ -558,7 +580,7 @@ dgx_status dgx_colsum(const void* dy, int dy_type, float* db, int R, int N, int 
     else
       colsum_partial_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part, R, N);
   }
-  colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(part, db, N, accumulate, slices);
+  colsum_final_kernel<<<(N + 31) / 32, 256, 0, s>>>(part, db, N, accumulate, slices);
   return cuda_status(cudaGetLastError(), "dgx_colsum");
 }
 
