@@ -249,11 +249,12 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++use) {
       const int buf = use & 1;
-      if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
-      tc_fence_after();
       int tm, tn;
       const int bz = t / per_batch;
       sched.coords((t - bz * per_batch) / splits, tm, tn);
+      if (args.tma_out && args.tma_out != 3) prefetch_bias_l1(args.bias, tn * BN, BN, args.N, lane);
+      if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
+      tc_fence_after();
       const int m = tm * BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       if (args.tma_out) {
@@ -281,25 +282,35 @@ __global__ void __launch_bounds__(192, 1)
             for (int j = 0; j < 32; ++j) w[j] = r[j];
           } else if (args.c_bf16) {
 #pragma unroll
-            for (int j = 0; j < 64; j += 2) {
-              float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
-              if (args.bias) {
-                v0 += n0 + j < args.N ? args.bias[n0 + j] : 0.f;
-                v1 += n0 + j + 1 < args.N ? args.bias[n0 + j + 1] : 0.f;
+            for (int j8 = 0; j8 < 64; j8 += 8) {
+              float bv[8];
+              if (args.bias) load_bias8(args.bias, n0 + j8, args.N, bv);
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                float v0 = __uint_as_float(r[j8 + i]), v1 = __uint_as_float(r[j8 + i + 1]);
+                if (args.bias) {
+                  v0 += bv[i];
+                  v1 += bv[i + 1];
+                }
+                if (args.relu) {
+                  v0 = fmaxf(v0, 0.f);
+                  v1 = fmaxf(v1, 0.f);
+                }
+                w[(j8 + i) / 2] = pack_bf16x2(v0, v1);
               }
-              if (args.relu) {
-                v0 = fmaxf(v0, 0.f);
-                v1 = fmaxf(v1, 0.f);
-              }
-              w[j / 2] = pack_bf16x2(v0, v1);
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float v = __uint_as_float(r[j]);
-              if (args.bias) v += n0 + j < args.N ? args.bias[n0 + j] : 0.f;
-              if (args.relu) v = fmaxf(v, 0.f);
-              w[j] = __float_as_uint(v);
+            for (int j8 = 0; j8 < 32; j8 += 8) {
+              float bv[8];
+              if (args.bias) load_bias8(args.bias, n0 + j8, args.N, bv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float v = __uint_as_float(r[j8 + i]);
+                if (args.bias) v += bv[i];
+                if (args.relu) v = fmaxf(v, 0.f);
+                w[j8 + i] = __float_as_uint(v);
+              }
             }
           }
 #pragma unroll

@@ -62,6 +62,27 @@ bool gemm2_eligible(const GemmArgs& a, const void* A, const void* B);
 cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cudaStream_t stream);
 void gemm_set_algo(int algo);
 
+// Bias of the 8 columns n..n+7 (zero past N): two 16-byte loads when the
+// slice is whole and aligned, else guarded scalar loads.
+__device__ __forceinline__ void load_bias8(const float* bias, int n, int N, float (&b)[8]) {
+  if (n + 8 <= N && (reinterpret_cast<uintptr_t>(bias + n) & 15) == 0) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(bias + n));
+    const float4 y = __ldg(reinterpret_cast<const float4*>(bias + n + 4));
+    b[0] = x.x; b[1] = x.y; b[2] = x.z; b[3] = x.w;
+    b[4] = y.x; b[5] = y.y; b[6] = y.z; b[7] = y.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = n + i < N ? bias[n + i] : 0.f;
+  }
+}
+// Bring the bias columns [n0, n0 + width) of a tile into L1 (one 128-byte
+// line per lane) while the epilogue still waits for the accumulator, so the
+// per-chunk bias loads hit L1 instead of waiting on L2.
+__device__ __forceinline__ void prefetch_bias_l1(const float* bias, int n0, int width, int N, int lane) {
+  const int n = n0 + lane * 32;
+  if (bias && lane * 32 < width && n < N) asm volatile("prefetch.global.L1 [%0];" ::"l"(bias + n));
+}
+
 __device__ __forceinline__ float gemm_finish(const GemmArgs& a, int n, float acc, float old) {
   float v = acc;
   if (a.beta != 0.f) v = fmaf(a.beta, old, v);

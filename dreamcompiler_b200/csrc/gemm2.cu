@@ -238,10 +238,11 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int t = pair; t < num_tiles; t += npairs, ++use) {
       const int buf = use & 1;
-      if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
-      tc_fence_after();
       int tm, tn;
       sched.coords(t, tm, tn);
+      prefetch_bias_l1(args.bias, tn * G2_BN, G2_BN, args.N, lane);
+      if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
+      tc_fence_after();
       const int row0 = tm * 2 * G2_BM + (int)rank * G2_BM + q * 32;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * G2_BN;
       const int cw = args.c_bf16 ? 64 : 32;
@@ -269,25 +270,35 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t w[32];
         if (args.c_bf16) {
 #pragma unroll
-          for (int j = 0; j < 64; j += 2) {
-            float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
-            if (args.bias) {
-              v0 += n0 + j < args.N ? args.bias[n0 + j] : 0.f;
-              v1 += n0 + j + 1 < args.N ? args.bias[n0 + j + 1] : 0.f;
+          for (int j8 = 0; j8 < 64; j8 += 8) {
+            float bv[8];
+            if (args.bias) load_bias8(args.bias, n0 + j8, args.N, bv);
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+              float v0 = __uint_as_float(r[j8 + i]), v1 = __uint_as_float(r[j8 + i + 1]);
+              if (args.bias) {
+                v0 += bv[i];
+                v1 += bv[i + 1];
+              }
+              if (args.relu) {
+                v0 = fmaxf(v0, 0.f);
+                v1 = fmaxf(v1, 0.f);
+              }
+              w[(j8 + i) / 2] = pack_bf16x2(v0, v1);
             }
-            if (args.relu) {
-              v0 = fmaxf(v0, 0.f);
-              v1 = fmaxf(v1, 0.f);
-            }
-            w[j / 2] = pack_bf16x2(v0, v1);
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float v = __uint_as_float(r[j]);
-            if (args.bias) v += n0 + j < args.N ? args.bias[n0 + j] : 0.f;
-            if (args.relu) v = fmaxf(v, 0.f);
-            w[j] = __float_as_uint(v);
+          for (int j8 = 0; j8 < 32; j8 += 8) {
+            float bv[8];
+            if (args.bias) load_bias8(args.bias, n0 + j8, args.N, bv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float v = __uint_as_float(r[j8 + i]);
+              if (args.bias) v += bv[i];
+              if (args.relu) v = fmaxf(v, 0.f);
+              w[j8 + i] = __float_as_uint(v);
+            }
           }
         }
 #pragma unroll
