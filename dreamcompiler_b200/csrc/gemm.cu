@@ -265,6 +265,17 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[64];
           tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           if (cw == 64) tmem_ld32(taddr + c + CW32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          float bq[64];  // this chunk's bias: the loads overlap the TMEM load
+          if (args.bias && args.tma_out != 3) {
+#pragma unroll
+            for (int j8 = 0; j8 < 64; j8 += 8)
+              if (j8 < cw) {
+                float b8[8];
+                load_bias8(args.bias, tn * BN + c + j8, args.N, b8);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) bq[j8 + i] = b8[i];
+              }
+          }
           tmem_ld_wait();
           if (c + cw >= BN) {  // last loads of this accumulator: hand it back to the MMA warp
             tc_fence_before();
@@ -283,14 +294,12 @@ __global__ void __launch_bounds__(192, 1)
           } else if (args.c_bf16) {
 #pragma unroll
             for (int j8 = 0; j8 < 64; j8 += 8) {
-              float bv[8];
-              if (args.bias) load_bias8(args.bias, n0 + j8, args.N, bv);
 #pragma unroll
               for (int i = 0; i < 8; i += 2) {
                 float v0 = __uint_as_float(r[j8 + i]), v1 = __uint_as_float(r[j8 + i + 1]);
                 if (args.bias) {
-                  v0 += bv[i];
-                  v1 += bv[i + 1];
+                  v0 += bq[j8 + i];
+                  v1 += bq[j8 + i + 1];
                 }
                 if (args.relu) {
                   v0 = fmaxf(v0, 0.f);
@@ -302,12 +311,10 @@ __global__ void __launch_bounds__(192, 1)
           } else {
 #pragma unroll
             for (int j8 = 0; j8 < 32; j8 += 8) {
-              float bv[8];
-              if (args.bias) load_bias8(args.bias, n0 + j8, args.N, bv);
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
                 float v = __uint_as_float(r[j8 + i]);
-                if (args.bias) v += bv[i];
+                if (args.bias) v += bq[j8 + i];
                 if (args.relu) v = fmaxf(v, 0.f);
                 w[j8 + i] = __float_as_uint(v);
               }
