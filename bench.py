@@ -356,8 +356,9 @@ def run_secondary(local_rank):
     after warm-up (rank 0 at N=1 only):
       configs[4]  int8 weight-only dense 4096x4096, B in {1, 16, 256}, both modes
       configs[0]  f32 GEMM 1024^3 + dA/dB backward (3xTF32 tcgen05)
-      configs[3]  bf16 GEMM 4096/8192/16384^3, single GPU
       configs[2]  char-level GPT training step (fwd + bwd + AdamW), tokens/s
+      configs[3]  bf16 GEMM 4096/8192/16384^3, single GPU (last: the 16384^3
+                  GEMMs leave the part power-capped for a while)
     Operands that fit in L2 are cycled through enough copies to exceed it.
     Each entry carries the median SM clock sampled over its timed replays
     (the latency-bound int8 layer runs first, before the GEMM sweeps)."""
@@ -435,19 +436,6 @@ def run_secondary(local_rank):
                                             "path": "3xTF32 on tcgen05 kind::tf32 (3 MMAs per K step)"}
     del sets, C, dA, dB, ws
 
-    # configs[3]: bf16 GEMM sweep, C bf16
-    sweep = {}
-    for n in (4096, 8192, 16384):
-        copies = 4 if n == 4096 else 1   # 4 x 64 MiB of operands > L2 at 4096
-        A = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
-        B = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
-        Cb = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
-        t = timed(lambda i: dgx.gemm(A[i % copies], B[i % copies], out=Cb), 20 if n < 16384 else 6)
-        sweep[str(n)] = {"ms": t * 1e3, "tflops": 2 * n ** 3 / t / 1e12, "sm_mhz": last_clk["sm_mhz"]}
-        del A, B, Cb
-        torch.cuda.empty_cache()
-    res["config4_bf16_gemm"] = sweep
-
     # char-level GPT training step (6 layers, d 384, 6 heads, seq 256,
     # batch 64, vocab 65): forward, backward and AdamW, synthetic uniform token ids
     from dreamcompiler_b200.gpt import GPT, GPTConfig
@@ -464,6 +452,20 @@ def run_secondary(local_rank):
                                      "precision": "bf16 GEMM/attention operands, fp32 master weights, grads, AdamW"}
     del model
     torch.cuda.empty_cache()
+
+    # configs[3]: bf16 GEMM sweep, C bf16
+    sweep = {}
+    for n in (4096, 8192, 16384):
+        copies = 4 if n == 4096 else 1   # 4 x 64 MiB of operands > L2 at 4096
+        A = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
+        B = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
+        Cb = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+        t = timed(lambda i: dgx.gemm(A[i % copies], B[i % copies], out=Cb), 20 if n < 16384 else 6)
+        sweep[str(n)] = {"ms": t * 1e3, "tflops": 2 * n ** 3 / t / 1e12, "sm_mhz": last_clk["sm_mhz"]}
+        del A, B, Cb
+        torch.cuda.empty_cache()
+    res["config4_bf16_gemm"] = sweep
+
     return res
 
 
@@ -531,8 +533,10 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     elapsed, e2e_s, bwd_kernel_s, clocks = run_ours(args, rank, world, local_rank)
-    tp_s, tp_steps = run_tp_gemm(args, rank, world, local_rank)
+    # the secondary configs (1 GPU) before the TP GEMM: its 16384^3 steps
+    # leave the part power-capped for a while
     secondary = run_secondary(local_rank) if world == 1 and not args.no_secondary else None
+    tp_s, tp_steps = run_tp_gemm(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
