@@ -8,6 +8,7 @@ two launches of each kernel).
     python -m dreamcompiler_b200.profile_case gemm_f32 --n 1024       # 3xTF32
     python -m dreamcompiler_b200.profile_case conv --batch 8          # 64 -> 128 channels, 3x3, 32x32
     python -m dreamcompiler_b200.profile_case gpt                     # one config-3 training step
+    python -m dreamcompiler_b200.profile_case linear                  # GPT MLP-up: 16384x1536x384 + bias
 """
 from __future__ import annotations
 
@@ -19,7 +20,7 @@ def main() -> None:
     import dreamcompiler_b200 as dgx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["flash", "gemm", "w8", "gemm_f32", "conv", "gpt"])
+    ap.add_argument("kind", choices=["flash", "gemm", "w8", "gemm_f32", "conv", "gpt", "linear"])
     ap.add_argument("--bh", type=int, default=16)
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--dim", type=int, default=64)
@@ -41,6 +42,13 @@ def main() -> None:
         C = torch.empty(a.n, a.n, device="cuda", dtype=torch.bfloat16)
         for _ in range(a.reps):
             dgx.gemm(A, B, out=C)
+    elif a.kind == "linear":  # X.W^T + b at the GPT step's MLP-up shape (bf16 out)
+        X = torch.randn(16384, 384, device="cuda", generator=g).bfloat16()
+        W = (torch.randn(1536, 384, device="cuda", generator=g) / 384 ** 0.5).bfloat16()
+        b = torch.randn(1536, device="cuda", generator=g)
+        Y = torch.empty(16384, 1536, device="cuda", dtype=torch.bfloat16)
+        for _ in range(a.reps):
+            dgx.gemm(X, W, transB=True, out=Y, bias=b)
     elif a.kind == "gemm_f32":
         A, B, dC = (torch.randn(a.n, a.n, device="cuda", generator=g) for _ in range(3))
         for _ in range(a.reps):
