@@ -9,9 +9,9 @@
 //
 // Design: one persistent CTA per SM. Warp 0 issues TMA tile loads into a
 // ring of shared-memory stages; warp 1 issues tcgen05.mma into one of two TMEM
-// accumulators; warps 2-5 drain the other accumulator (tcgen05.ld), apply the
-// epilogue and store, so the epilogue of tile i overlaps the main loop of
-// tile i+1. Transposed operands are handled by the shared-memory descriptor's
+// accumulators; warps 2-9 (two per TMEM lane quarter) drain the other
+// accumulator (tcgen05.ld), apply the epilogue and store, so the epilogue of
+// tile i overlaps the main loop of tile i+1. Transposed operands are handled by the shared-memory descriptor's
 // major-ness (K-major or MN-major), never by a copy.
 //
 // bf16 inputs run kind::f16 with fp32 accumulation. f32 inputs run the
@@ -44,8 +44,8 @@ struct GemmCfg {
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;                   // double-buffered accumulator
   static constexpr int CHUNK = 128 / ESZ;                    // MN elements per 128-byte chunk
-  // Epilogue staging for the TMA-store path: 4 warps x 2 buffers x (32 rows x 128 B).
-  static constexpr int OUT_STAGE_BYTES = 4 * 2 * 4096;
+  // Epilogue staging for the TMA-store path: 8 warps x (32 rows x 128 B).
+  static constexpr int OUT_STAGE_BYTES = 8 * 4096;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t FMT = TF32 ? 2u : 1u;
 };
@@ -74,8 +74,12 @@ __device__ __forceinline__ uint32_t kstep_offset(int kk) {
 
 // EXTRA: the TMA-store epilogue also stores every staged box to the extra
 // destinations (tmX); plain instantiations carry none of that code.
+// Warps: 0 TMA producer, 1 MMA issuer, 2..9 epilogue (two per TMEM lane
+// quarter, taking alternate column chunks of the accumulator).
+constexpr int kGemmThreads = 320;
+
 template <bool TF32, bool A_MN, bool B_MN, int BN_, bool EXTRA = false>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ ExtraOutMaps tmX,
@@ -103,7 +107,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], 4);
+      mbar_init(&acce_bar[b], 8);  // every epilogue warp releases the accumulator
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -232,16 +236,21 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    // Two warps per TMEM lane quarter: `half` 0 takes the even column chunks
+    // of the accumulator, 1 the odd ones, so the drain, the epilogue math
+    // and the stores of one tile run on 8 warps (at small K the epilogue,
+    // not the main loop, sets the tile period).
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     uint32_t use = 0;
     // TMA-store path: each warp stages its 32 rows x 128 bytes (32 fp32 or 64
-    // bf16 columns) in one of two shared-memory buffers with the 128-byte
-    // swizzle (16-byte unit u of row r at u ^ (r & 7): conflict-free) and
-    // issues one TMA store / reduce-add per chunk.
-    uint8_t* my_stage = out_stage + (warp - 2) * 8192;
-    uint32_t issued = 0;  // stores issued by this warp: buffer = issued & 1
+    // bf16 columns) in its shared-memory buffer with the 128-byte swizzle
+    // (16-byte unit u of row r at u ^ (r & 7): conflict-free) and issues one
+    // TMA store / reduce-add per chunk.
+    uint8_t* my_stage = out_stage + (warp - 2) * 4096;
+    uint32_t issued = 0;  // stores issued by this warp
     if (args.tma_out && lane == 0) {
       tma_prefetch_desc(&tmC);
       if (EXTRA)
@@ -260,8 +269,13 @@ __global__ void __launch_bounds__(192, 1)
       if (args.tma_out) {
         constexpr int CW32 = 32;  // fp32 columns per 32-column TMEM load
         const int cw = (args.c_bf16 && args.tma_out != 3) ? 64 : 32;  // columns per 128-byte staged row
+        if (half * cw >= BN) {  // no chunk for this warp (one-chunk tiles): release at once
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce_bar[buf]);
+        }
 #pragma unroll 1
-        for (int c = 0; c < BN; c += cw) {
+        for (int c = half * cw; c < BN; c += 2 * cw) {
           uint32_t r[64];
           tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           if (cw == 64) tmem_ld32(taddr + c + CW32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
@@ -277,15 +291,15 @@ __global__ void __launch_bounds__(192, 1)
               }
           }
           tmem_ld_wait();
-          if (c + cw >= BN) {  // last loads of this accumulator: hand it back to the MMA warp
+          if (c + 2 * cw >= BN) {  // this warp's last loads of the accumulator: release it
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce_bar[buf]);
           }
           const int n0 = tn * BN + c;
           if (n0 >= args.N) continue;
-          uint8_t* st = my_stage + (issued & 1) * 4096;
-          if (lane == 0 && issued >= 2) bulk_wait_read1();  // the store issued from this buffer has read it
+          uint8_t* st = my_stage;
+          if (lane == 0 && issued >= 1) bulk_wait_read0();  // the previous store has read the buffer
           __syncwarp();
           uint32_t w[32];
           if (args.tma_out == 3) {  // raw partial sums
@@ -344,7 +358,7 @@ __global__ void __launch_bounds__(192, 1)
         (void)m;
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * 32; c < BN; c += 64) {
           uint32_t r[32];
           tmem_ld32(taddr + c, r);
           tmem_ld_wait();
@@ -652,7 +666,7 @@ static cudaError_t launch_tc_bn(const GemmArgs& args, const void* A, const void*
   const int grid = units < num_sms() ? (int)units : num_sms();
   {
     TimerScope timer(stream);
-    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, mc, mx, a);
+    kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, mc, mx, a);
   }
   if (a.splits > 1) {
     const long long quads = (long long)a.M * ((a.N + 3) / 4);
