@@ -60,6 +60,7 @@ SIGNATURES = {
     "dgx_quantize_rows_i8": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "dgx_layernorm_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "dgx_layernorm_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "dgx_layernorm_bwd_x16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "dgx_gelu_fwd": (_i, [_vp, _i, _vp, C.c_longlong, _vp]),
     "dgx_gelu_bwd": (_i, [_vp, _i, _vp, _i, _vp, C.c_longlong, _vp]),
     "dgx_embedding_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),

@@ -55,10 +55,11 @@ __global__ void ln_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* __rest
   }
 }
 
-// dx (+)= rstd/C * (C*dy - sum(dy) - y*sum(dy*y)), y recomputed from x.
+// dx (+)= rstd/C * (C*dy - sum(dy) - y*sum(dy*y)), y recomputed from x;
+// dx16 (may be null) receives bf16(dx) as well, the operand of the next GEMMs.
 __global__ void ln_bwd_kernel(const float* __restrict__ x, const float* __restrict__ mean,
                               const float* __restrict__ rstd, const float* __restrict__ dy, float* __restrict__ dx,
-                              int R, int C, int accumulate) {
+                              __nv_bfloat16* __restrict__ dx16, int R, int C, int accumulate) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
@@ -78,7 +79,9 @@ __global__ void ln_bwd_kernel(const float* __restrict__ x, const float* __restri
   for (int j = lane; j < C; j += 32) {
     const float yv = (xr[j] - mu) * rs;
     const float v = a * (C * gr[j] - sg - yv * sgy);
-    dr[j] = accumulate ? dr[j] + v : v;
+    const float o = accumulate ? dr[j] + v : v;
+    dr[j] = o;
+    if (dx16) dx16[(size_t)row * C + j] = __float2bfloat16_rn(o);
   }
 }
 
@@ -446,8 +449,18 @@ dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rst
   if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_bwd: R=%d C=%d", R, C);
   if (R == 0) return DGX_OK;
   if (!x || !mean || !rstd || !dy || !dx) return set_error(DGX_EINVAL, "dgx_layernorm_bwd: null pointer");
-  ln_bwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, R, C, accumulate);
+  ln_bwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, nullptr, R, C, accumulate);
   return cuda_status(cudaGetLastError(), "dgx_layernorm_bwd");
+}
+
+dgx_status dgx_layernorm_bwd_x16(const float* x, const float* mean, const float* rstd, const float* dy, float* dx,
+                                 void* dx16, int R, int C, int accumulate, void* stream) {
+  if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_bwd_x16: R=%d C=%d", R, C);
+  if (R == 0) return DGX_OK;
+  if (!x || !mean || !rstd || !dy || !dx || !dx16) return set_error(DGX_EINVAL, "dgx_layernorm_bwd_x16: null pointer");
+  ln_bwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, (__nv_bfloat16*)dx16, R, C,
+                                                               accumulate);
+  return cuda_status(cudaGetLastError(), "dgx_layernorm_bwd_x16");
 }
 
 dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream) {

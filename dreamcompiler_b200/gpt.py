@@ -197,15 +197,13 @@ class GPT:
         gemm(self.dlogits, w["Wout"], out=self.dh)                        # dhf = dlogits Wout
         gemm(self.dlogits, hf, transA=True, out=g["Wout"])                # dWout = dlogits^T hf
         _c("dgx_colsum", self.dlogits.data_ptr(), L.DGX_BF16, g["bout"].data_ptr(), R, Vp, 0, s)
-        _c("dgx_layernorm_bwd", xL.data_ptr(), self.mu[-1].data_ptr(), self.rs[-1].data_ptr(), self.dh.data_ptr(),
-           self.dx.data_ptr(), R, d, 0, s)
-        conv16 = lambda src, dst: _c("dgx_convert", src.data_ptr(), L.DGX_F32, dst.data_ptr(), L.DGX_BF16,
-                                     src.numel(), 0, s)
+        # each layer-norm backward also leaves bf16(dx) in dx16 for the next GEMMs
+        _c("dgx_layernorm_bwd_x16", xL.data_ptr(), self.mu[-1].data_ptr(), self.rs[-1].data_ptr(),
+           self.dh.data_ptr(), self.dx.data_ptr(), self.dx16.data_ptr(), R, d, 0, s)
         for l in reversed(range(c.n_layer)):
             x0, x1 = self.x[2 * l], self.x[2 * l + 1]
             h, h2 = self.h16[2 * l], self.h16[2 * l + 1]
             # MLP: x2 = x1 + gelu(h2 W1^T + b1) W2^T + b2
-            conv16(self.dx, self.dx16)
             gemm(self.dx16, w[f"W2{l}"], out=self.dg16)                   # dg = dx W2
             gemm(self.dx16, self.g16[l], transA=True, out=g[f"W2{l}"])     # dW2 = dx^T g
             _c("dgx_colsum", self.dx.data_ptr(), L.DGX_F32, g[f"b2{l}"].data_ptr(), R, d, 0, s)
@@ -214,10 +212,9 @@ class GPT:
             gemm(self.du16, w[f"W1{l}"], out=self.dh)                     # dh2 = du W1
             gemm(self.du16, h2, transA=True, out=g[f"W1{l}"])              # dW1 = du^T h2
             _c("dgx_colsum", self.du16.data_ptr(), L.DGX_BF16, g[f"b1{l}"].data_ptr(), R, 4 * d, 0, s)
-            _c("dgx_layernorm_bwd", x1.data_ptr(), self.mu[2 * l + 1].data_ptr(), self.rs[2 * l + 1].data_ptr(),
-               self.dh.data_ptr(), self.dx.data_ptr(), R, d, 1, s)
+            _c("dgx_layernorm_bwd_x16", x1.data_ptr(), self.mu[2 * l + 1].data_ptr(), self.rs[2 * l + 1].data_ptr(),
+               self.dh.data_ptr(), self.dx.data_ptr(), self.dx16.data_ptr(), R, d, 1, s)
             # attention: x1 = x0 + merge(attn(split(h Wqkv^T + bqkv))) Wo^T + bo
-            conv16(self.dx, self.dx16)
             gemm(self.dx16, w[f"Wo{l}"], out=self.datt16)                 # datt = dx Wo (bf16 rows)
             gemm(self.dx16, self.att16[l], transA=True, out=g[f"Wo{l}"])   # dWo = dx^T att
             _c("dgx_colsum", self.dx.data_ptr(), L.DGX_F32, g[f"bo{l}"].data_ptr(), R, d, 0, s)
@@ -229,8 +226,12 @@ class GPT:
             gemm(self.dqkv16, w[f"Wqkv{l}"], out=self.dh)                 # dh = dqkv Wqkv
             gemm(self.dqkv16, h, transA=True, out=g[f"Wqkv{l}"])           # dWqkv = dqkv^T h
             _c("dgx_colsum", self.dqkv16.data_ptr(), L.DGX_BF16, g[f"bqkv{l}"].data_ptr(), R, 3 * d, 0, s)
-            _c("dgx_layernorm_bwd", x0.data_ptr(), self.mu[2 * l].data_ptr(), self.rs[2 * l].data_ptr(),
-               self.dh.data_ptr(), self.dx.data_ptr(), R, d, 1, s)
+            if l > 0:
+                _c("dgx_layernorm_bwd_x16", x0.data_ptr(), self.mu[2 * l].data_ptr(), self.rs[2 * l].data_ptr(),
+                   self.dh.data_ptr(), self.dx.data_ptr(), self.dx16.data_ptr(), R, d, 1, s)
+            else:  # the embedding backward reads dx in fp32 only
+                _c("dgx_layernorm_bwd", x0.data_ptr(), self.mu[2 * l].data_ptr(), self.rs[2 * l].data_ptr(),
+                   self.dh.data_ptr(), self.dx.data_ptr(), R, d, 1, s)
         g["W_tok"].zero_()
         g["P"].zero_()
         _c("dgx_embedding_bwd", self.tok.data_ptr(), self.dx.data_ptr(), g["W_tok"].data_ptr(), g["P"].data_ptr(),

@@ -264,6 +264,10 @@ dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd
  * (runtime/ops/autograd.inc:453-470); accumulate = 1 adds into dx. */
 dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rstd, const float* dy, float* dx, int R,
                              int C, int accumulate, void* stream);
+/* dgx_layernorm_bwd that also writes bf16(dx) into dx16 ([R][C]): the
+ * residual gradient and the bf16 operand of the next GEMMs in one pass. */
+dgx_status dgx_layernorm_bwd_x16(const float* x, const float* mean, const float* rstd, const float* dy, float* dx,
+                                 void* dx16, int R, int C, int accumulate, void* stream);
 /* y16 = bf16(gelu(x)), tanh form (runtime/io/builtins.inc:548-560); x DGX_F32 or DGX_BF16. */
 dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream);
 /* dx16 = bf16(gelu'(x) * dy) (runtime/ops/autograd.inc:293-303); x, dy DGX_F32 or DGX_BF16. */

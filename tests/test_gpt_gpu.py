@@ -134,6 +134,29 @@ def test_gelu_kernels_against_oracle(dgx, n):
     assert nw(dx.double().cpu().numpy(), rdx) < 1e-2
 
 
+@pytest.mark.parametrize("accumulate", [0, 1])
+def test_layernorm_bwd_x16_matches_separate_conversion(dgx, accumulate):
+    """dgx_layernorm_bwd_x16: the same fp32 dx as dgx_layernorm_bwd, plus
+    dx16 = bf16(dx) bit for bit (what converting dx afterwards gives)."""
+    from dreamcompiler_b200 import _lib as L
+    R, C = 1000, 384
+    g = torch.Generator(device="cuda").manual_seed(17 + accumulate)
+    x, dy, dx0 = (torch.randn(R, C, device="cuda", generator=g) for _ in range(3))
+    y16 = torch.empty(R, C, device="cuda", dtype=torch.bfloat16)
+    mu, rs = torch.empty(R, device="cuda"), torch.empty(R, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    L.call("dgx_layernorm_fwd", x.data_ptr(), y16.data_ptr(), mu.data_ptr(), rs.data_ptr(), R, C, s)
+    dx_a, dx_b = dx0.clone(), dx0.clone()
+    dx16 = torch.empty(R, C, device="cuda", dtype=torch.bfloat16)
+    L.call("dgx_layernorm_bwd", x.data_ptr(), mu.data_ptr(), rs.data_ptr(), dy.data_ptr(), dx_a.data_ptr(), R, C,
+           accumulate, s)
+    L.call("dgx_layernorm_bwd_x16", x.data_ptr(), mu.data_ptr(), rs.data_ptr(), dy.data_ptr(), dx_b.data_ptr(),
+           dx16.data_ptr(), R, C, accumulate, s)
+    dgx.sync_check()
+    assert torch.equal(dx_a, dx_b)
+    assert torch.equal(dx16, dx_a.bfloat16())
+
+
 @pytest.mark.parametrize("dtype,R,N", [("bf16", 16384, 1536), ("bf16", 16384, 384), ("f32", 16384, 65),
                                        ("f32", 1000, 384), ("bf16", 77, 24)])
 def test_colsum_kernels(dgx, dtype, R, N):
