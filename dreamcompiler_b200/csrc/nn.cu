@@ -55,6 +55,98 @@ __global__ void ln_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* __rest
   }
 }
 
+// Row-in-registers forms for C a multiple of 128 (C <= 128 * LN_MAXV) and
+// 16-byte aligned rows: lane l holds float4 groups l, l+32, ... of the row,
+// so every access is a 16-byte load or store and the row is read once.
+// Same two-pass statistics and formulas as the scalar kernels.
+constexpr int LN_MAXV = 8;
+
+__device__ __forceinline__ uint2 pack_bf16x4(float a, float b, float c, float d) {
+  return make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+}
+
+__global__ void ln_fwd_vec_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, float* __restrict__ mean,
+                                  float* __restrict__ rstd, int R, int C) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= R) return;
+  const int nv = C / 128;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * C);
+  float4 xv[LN_MAXV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i)
+    if (i < nv) {
+      xv[i] = __ldg(xr + lane + 32 * i);
+      s += (xv[i].x + xv[i].y) + (xv[i].z + xv[i].w);
+    }
+  const float mu = warp_sum(s) / C;
+  float v = 0.f;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i)
+    if (i < nv) {
+      const float a = xv[i].x - mu, b = xv[i].y - mu, c = xv[i].z - mu, d = xv[i].w - mu;
+      v = fmaf(a, a, v);
+      v = fmaf(b, b, v);
+      v = fmaf(c, c, v);
+      v = fmaf(d, d, v);
+    }
+  const float rs = rsqrtf(warp_sum(v) / C + kLnEps);
+  uint2* yr = reinterpret_cast<uint2*>(y + (size_t)row * C);
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i)
+    if (i < nv)
+      yr[lane + 32 * i] = pack_bf16x4((xv[i].x - mu) * rs, (xv[i].y - mu) * rs, (xv[i].z - mu) * rs,
+                                      (xv[i].w - mu) * rs);
+  if (lane == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+}
+
+__global__ void ln_bwd_vec_kernel(const float* __restrict__ x, const float* __restrict__ mean,
+                                  const float* __restrict__ rstd, const float* __restrict__ dy, float* __restrict__ dx,
+                                  __nv_bfloat16* __restrict__ dx16, int R, int C, int accumulate) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= R) return;
+  const int nv = C / 128;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * C);
+  const float4* gr = reinterpret_cast<const float4*>(dy + (size_t)row * C);
+  const float mu = mean[row], rs = rstd[row];
+  float4 yv[LN_MAXV], gv[LN_MAXV];
+  float sg = 0.f, sgy = 0.f;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i)
+    if (i < nv) {
+      const float4 xi = __ldg(xr + lane + 32 * i);
+      gv[i] = __ldg(gr + lane + 32 * i);
+      yv[i] = make_float4((xi.x - mu) * rs, (xi.y - mu) * rs, (xi.z - mu) * rs, (xi.w - mu) * rs);
+      sg += (gv[i].x + gv[i].y) + (gv[i].z + gv[i].w);
+      sgy = fmaf(gv[i].x, yv[i].x, sgy);
+      sgy = fmaf(gv[i].y, yv[i].y, sgy);
+      sgy = fmaf(gv[i].z, yv[i].z, sgy);
+      sgy = fmaf(gv[i].w, yv[i].w, sgy);
+    }
+  sg = warp_sum(sg);
+  sgy = warp_sum(sgy);
+  const float a = rs / C;
+  float4* dr = reinterpret_cast<float4*>(dx + (size_t)row * C);
+  uint2* d16 = reinterpret_cast<uint2*>(dx16 + (size_t)row * C);
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i)
+    if (i < nv) {
+      float4 o = make_float4(a * (C * gv[i].x - sg - yv[i].x * sgy), a * (C * gv[i].y - sg - yv[i].y * sgy),
+                             a * (C * gv[i].z - sg - yv[i].z * sgy), a * (C * gv[i].w - sg - yv[i].w * sgy));
+      if (accumulate) {
+        const float4 p = dr[lane + 32 * i];
+        o = make_float4(p.x + o.x, p.y + o.y, p.z + o.z, p.w + o.w);
+      }
+      dr[lane + 32 * i] = o;
+      if (dx16) d16[lane + 32 * i] = pack_bf16x4(o.x, o.y, o.z, o.w);
+    }
+}
+
 // dx (+)= rstd/C * (C*dy - sum(dy) - y*sum(dy*y)), y recomputed from x;
 // dx16 (may be null) receives bf16(dx) as well, the operand of the next GEMMs.
 __global__ void ln_bwd_kernel(const float* __restrict__ x, const float* __restrict__ mean,
@@ -434,13 +526,25 @@ int ew_grid(long long n) {
 
 using namespace dgx;
 
+namespace {
+// The row-in-registers layer-norm kernels apply: C a multiple of 128 up to
+// 128 * LN_MAXV, every row 16-byte aligned (bf16 rows: 8-byte aligned).
+bool ln_vec_ok(int C, const void* a, const void* b = nullptr, const void* c = nullptr, const void* d = nullptr) {
+  if (C % 128 || C > 128 * LN_MAXV) return false;
+  return ((((uintptr_t)a) | (uintptr_t)b | (uintptr_t)c | (uintptr_t)d) & 15) == 0;
+}
+}  // namespace
+
 extern "C" {
 
 dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd, int R, int C, void* stream) {
   if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_fwd: R=%d C=%d", R, C);
   if (R == 0) return DGX_OK;
   if (!x || !y16 || !mean || !rstd) return set_error(DGX_EINVAL, "dgx_layernorm_fwd: null pointer");
-  ln_fwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, (__nv_bfloat16*)y16, mean, rstd, R, C);
+  if (ln_vec_ok(C, x, y16))
+    ln_fwd_vec_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, (__nv_bfloat16*)y16, mean, rstd, R, C);
+  else
+    ln_fwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, (__nv_bfloat16*)y16, mean, rstd, R, C);
   return cuda_status(cudaGetLastError(), "dgx_layernorm_fwd");
 }
 
@@ -449,7 +553,10 @@ dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rst
   if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_bwd: R=%d C=%d", R, C);
   if (R == 0) return DGX_OK;
   if (!x || !mean || !rstd || !dy || !dx) return set_error(DGX_EINVAL, "dgx_layernorm_bwd: null pointer");
-  ln_bwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, nullptr, R, C, accumulate);
+  if (ln_vec_ok(C, x, dy, dx))
+    ln_bwd_vec_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, nullptr, R, C, accumulate);
+  else
+    ln_bwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, nullptr, R, C, accumulate);
   return cuda_status(cudaGetLastError(), "dgx_layernorm_bwd");
 }
 
@@ -458,8 +565,12 @@ dgx_status dgx_layernorm_bwd_x16(const float* x, const float* mean, const float*
   if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_bwd_x16: R=%d C=%d", R, C);
   if (R == 0) return DGX_OK;
   if (!x || !mean || !rstd || !dy || !dx || !dx16) return set_error(DGX_EINVAL, "dgx_layernorm_bwd_x16: null pointer");
-  ln_bwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, (__nv_bfloat16*)dx16, R, C,
-                                                               accumulate);
+  if (ln_vec_ok(C, x, dy, dx, dx16))
+    ln_bwd_vec_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, (__nv_bfloat16*)dx16, R,
+                                                                     C, accumulate);
+  else
+    ln_bwd_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, mean, rstd, dy, dx, (__nv_bfloat16*)dx16, R, C,
+                                                                 accumulate);
   return cuda_status(cudaGetLastError(), "dgx_layernorm_bwd_x16");
 }
 

@@ -134,6 +134,35 @@ def test_gelu_kernels_against_oracle(dgx, n):
     assert nw(dx.double().cpu().numpy(), rdx) < 1e-2
 
 
+@pytest.mark.parametrize("C", [384, 1024, 100])
+def test_layernorm_kernels_against_oracle(dgx, C):
+    """dgx_layernorm_fwd / dgx_layernorm_bwd (row-in-registers path for C a
+    multiple of 128, scalar path otherwise) against the f64 oracle's
+    layer_norm and its backward (runtime/io/builtins.inc:167-197,
+    runtime/ops/autograd.inc:453-470): y16 to the bf16 tolerance, mean,
+    rstd and dx to 1e-5 normwise."""
+    from dreamcompiler_b200 import _lib as L
+    R = 777
+    g = torch.Generator(device="cuda").manual_seed(C)
+    x = torch.randn(R, C, device="cuda", generator=g) * 2 + 0.5
+    dy = torch.randn(R, C, device="cuda", generator=g)
+    y16 = torch.empty(R, C, device="cuda", dtype=torch.bfloat16)
+    mu, rs = torch.empty(R, device="cuda"), torch.empty(R, device="cuda")
+    dx = torch.empty(R, C, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    L.call("dgx_layernorm_fwd", x.data_ptr(), y16.data_ptr(), mu.data_ptr(), rs.data_ptr(), R, C, s)
+    L.call("dgx_layernorm_bwd", x.data_ptr(), mu.data_ptr(), rs.data_ptr(), dy.data_ptr(), dx.data_ptr(), R, C, 0, s)
+    dgx.sync_check()
+    xf, dyf = x.double().cpu().numpy(), dy.double().cpu().numpy()
+    ry, inv = G.layer_norm(xf)
+    rdx = G.layer_norm_bwd(ry, inv, dyf)
+    nw = lambda a, r: np.abs(a - r).max() / np.abs(r).max()
+    assert nw(y16.double().cpu().numpy(), ry) < 1e-2
+    assert nw(rs.double().cpu().numpy(), np.asarray(inv).reshape(-1)) < 1e-5
+    assert nw(mu.double().cpu().numpy(), xf.mean(1)) < 1e-5
+    assert nw(dx.double().cpu().numpy(), rdx) < 1e-5
+
+
 @pytest.mark.parametrize("accumulate", [0, 1])
 def test_layernorm_bwd_x16_matches_separate_conversion(dgx, accumulate):
     """dgx_layernorm_bwd_x16: the same fp32 dx as dgx_layernorm_bwd, plus
