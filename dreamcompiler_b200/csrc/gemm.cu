@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int bz = t / per_batch;
       sched.coords((t - bz * per_batch) / splits, tm, tn);
       if (args.tma_out && args.tma_out != 3) prefetch_bias_l1(args.bias, tn * BN, BN, args.N, lane);
-      if (!mbar_wait_backoff(&accf_bar[buf], (use >> 1) & 1, wc)) break;
+      if (!mbar_wait(&accf_bar[buf], (use >> 1) & 1, wc)) break;
       tc_fence_after();
       const int m = tm * BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;

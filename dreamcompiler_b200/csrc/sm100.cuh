@@ -89,24 +89,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
-// mbar_wait for a role that waits about a whole main loop (the GEMM
-// epilogue's accumulator wait): a short sleep between polls leaves the
-// issue slots to the producer and MMA warps. Same bound and abort.
-__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
-  if (mbar_test(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (true) {
-    __nanosleep(64);
-    if (mbar_test(bar, parity)) return true;
-    if (*w.abort) return false;
-    if (clock64() - t0 > kWaitBudgetCycles) {
-      *w.abort = 1;
-      if (w.err) atomicOr(w.err, DGX_DEV_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 // Used only on the teardown path: wait for copies already in flight to land
 // before the CTA leaves (so no TMA write targets freed shared memory).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
