@@ -28,29 +28,6 @@
 #include "common.h"
 #include "flash.h"
 #include "sm100.cuh"
-#include "softmax_math.cuh"
-
-// Optional phase tracing for kernel tuning: built with -DDGX_TRACE, CTA 0
-// records clock64() into dgx_bwd_trace[tile * 16 + point] (tile = its n-th
-// Q tile), points: MMA warp 0-5 (wait p_ready, got it, S(i+1) issued, got
-// ds_ready, got dq_empty, dP(i+1) issued), compute warp 0: 6-11 (wait
-// s_full, got it, exps done, p_ready, got dp_full, ds_ready), dQ drain:
-// 12-14 (wait dq_full, got it, reduce issued). Read back with
-// dgx_bwd_trace_read. Compiled out otherwise.
-#ifdef DGX_TRACE
-__device__ unsigned long long dgx_bwd_trace[16384];
-#define BWD_TRACE(slot) \
-  do {                  \
-    if (blockIdx.x == 0) dgx_bwd_trace[(slot)] = clock64(); \
-  } while (0)
-extern "C" int dgx_bwd_trace_read(void* dst) {
-  return (int)cudaMemcpyFromSymbol(dst, dgx_bwd_trace, sizeof(dgx_bwd_trace));
-}
-#else
-#define BWD_TRACE(slot) \
-  do {                  \
-  } while (0)
-#endif
 
 namespace dgx {
 
@@ -248,9 +225,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int s1 = (gt + 1) % Q_STAGES;
           // p_ready of an item's first tile also means the compute warps have
           // read out the previous item's dV / dK, so dV(0) may overwrite them.
-          BWD_TRACE(gt * 16 + 0);
           if (!(ok = mbar_wait(&bars->p_ready, gt & 1, wc))) break;
-          BWD_TRACE(gt * 16 + 1);
           tc_fence_after();
           tmem_a_acc(tmem + T_DV, tmem + T_ST, do_s, it == 0);  // dV += P^T dO
           if (next) {
@@ -259,14 +234,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             kmajor_pair(tmem + T_ST, sK, sQ + s1 * TILE);  // S^T(i+1)
             tc_commit(&bars->s_full);
           }
-          BWD_TRACE(gt * 16 + 2);
           if (!(ok = mbar_wait(&bars->ds_ready, gt & 1, wc))) break;
-          BWD_TRACE(gt * 16 + 3);
           tc_fence_after();
           tmem_a_acc(tmem + T_DK, tmem + T_DPT, q_s, it == 0);  // dK += dS^T Q
           const int b = gt & 1;
           if (!(ok = mbar_wait(&bars->dq_empty[b], ((gt >> 1) & 1) ^ 1, wc))) break;
-          BWD_TRACE(gt * 16 + 4);
           tc_fence_after();
           {
             const uint64_t da = sw128_desc(sdS, BKV * 128, 1024), dk = sw128_desc(sK, DP * 128, 1024);
@@ -280,7 +252,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             kmajor_pair(tmem + T_DPT, sV, sdO + s1 * TILE);  // dP^T(i+1)
             tc_commit(&bars->dp_full);
           }
-          BWD_TRACE(gt * 16 + 5);
         }
         if (!ok) break;
         tc_commit(&bars->acc_done);    // dV, dK of this item complete
@@ -304,9 +275,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const Item I = item(w);
       for (int it = 0; it < I.n; ++it, ++gt) {
         const int b = gt & 1;
-        if (issuer) BWD_TRACE(gt * 16 + 12);
         if (!(ok = mbar_wait(&bars->dq_full[b], (gt >> 1) & 1, wc))) break;
-        if (issuer) BWD_TRACE(gt * 16 + 13);
         tc_fence_after();
         uint32_t v[DP];
         tmem_ld32(tmem + lane_off + T_DQ + 64 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
@@ -332,7 +301,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tma_reduce_add_3d(&tmdQacc, stage, 0, q0, I.bh);
           if (args.D > 32) tma_reduce_add_3d(&tmdQacc, stage + DQ_BOX, 32, q0, I.bh);
           bulk_commit();
-          BWD_TRACE(gt * 16 + 14);
         }
       }
     }
@@ -359,10 +327,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float* st = reinterpret_cast<const float*>(smem + SM_STAT + (gt % Q_STAGES) * STAT_BYTES);
         const float* Ls = st + 64 * h;
         const float* Ds = st + BQ + 64 * h;
-        const bool trc = warp == 0 && lane == 0;
-        if (trc) BWD_TRACE(gt * 16 + 6);
         if (!(ok = mbar_wait(&bars->s_full, gt & 1, wc))) break;
-        if (trc) BWD_TRACE(gt * 16 + 7);
         tc_fence_after();
         // Both 32-column loads in flight before one wait.
         float p[64];
@@ -380,7 +345,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
               static_for<0, 32, 1>([&](auto tt) {
                 constexpr int t = decltype(tt)::value;
-                p[cc + t] = ex2_col<t, DGX_EXP_EMU_BWD>(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
+                p[cc + t] = ex2(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
               });
             }
           } else {
@@ -391,7 +356,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
               static_for<0, 32, 1>([&](auto tt) {
                 constexpr int t = decltype(tt)::value;
-                const float e = ex2_col<t, DGX_EXP_EMU_BWD>(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
+                const float e = ex2(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
                 p[cc + t] = qt0 + 64 * h + cc + t < key ? 0.f : e;
               });
             }
@@ -405,17 +370,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int cc = 0; cc < 64; cc += 32) {
           uint32_t pk[16];
 #pragma unroll
-          for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2_fast(p[cc + 2 * t], p[cc + 2 * t + 1]);
+          for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(p[cc + 2 * t], p[cc + 2 * t + 1]);
           tmem_st16(tmem + lane_off + T_ST + 64 * h + cc / 2, pk);
         }
-        if (trc) BWD_TRACE(gt * 16 + 8);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_ready);
-        if (trc) BWD_TRACE(gt * 16 + 9);
         if (!(ok = mbar_wait(&bars->dp_full, gt & 1, wc))) break;
-        if (trc) BWD_TRACE(gt * 16 + 10);
         tc_fence_after();
 #pragma unroll
         for (int cc = 0; cc < 64; cc += 32) {
@@ -430,7 +392,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int t = 0; t < 32; t += 2) {
             const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - dd[t]);
             const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - dd[t + 1]);
-            pk[t / 2] = pack_bf16x2_fast(ds0, ds1);
+            pk[t / 2] = pack_bf16x2(ds0, ds1);
           }
           tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
           // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
@@ -447,7 +409,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->ds_ready);
-        if (trc) BWD_TRACE(gt * 16 + 11);
       }
       if (!ok) break;
       // ---------------------------------------------------------- item epilogue: dV (h=0), dK (h=1)

@@ -28,25 +28,6 @@
 #include "common.h"
 #include "flash.h"
 #include "sm100.cuh"
-#include "softmax_math.cuh"
-
-// Optional phase tracing for kernel tuning: built with -DDGX_TRACE, CTA 0
-// records clock64() at the marked points into dgx_fwd_trace (read back with
-// dgx_fwd_trace_read). Compiled out otherwise.
-#ifdef DGX_TRACE
-__device__ unsigned long long dgx_fwd_trace[16384];
-#define FWD_TRACE(slot) \
-  do {                  \
-    if (blockIdx.x == 0) dgx_fwd_trace[(slot)] = clock64(); \
-  } while (0)
-extern "C" int dgx_fwd_trace_read(void* dst) {
-  return (int)cudaMemcpyFromSymbol(dst, dgx_fwd_trace, sizeof(dgx_fwd_trace));
-}
-#else
-#define FWD_TRACE(slot) \
-  do {                  \
-  } while (0)
-#endif
 
 namespace dgx {
 
@@ -62,10 +43,7 @@ constexpr int NUM_THREADS = 384;  // WG0: softmax A, WG1: softmax B, WG2: TMA wa
 constexpr uint32_t REG_SOFTMAX = 224, REG_CTRL = 56;
 constexpr float RESCALE_LOG2 = 8.0f;
 // Exponential column after which a softmax group hands the MUFU turn over.
-#ifndef DGX_FWD_TURN_AT
-#define DGX_FWD_TURN_AT 80
-#endif
-constexpr int TURN_AT = DGX_FWD_TURN_AT;
+constexpr int TURN_AT = 80;
 
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int SM_Q = 0;                               // Q_A, Q_B (two buffers: next item's Q)
@@ -245,30 +223,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int j = 0; ok && j < I.nB; ++j) {
           const uint32_t kvi = gkv + j;
           const int s = kvi % KV_STAGES;
-          FWD_TRACE(8192 + j * 8 + 0);
           if (j + 1 < I.nB) {
             if (!(ok = mbar_wait(&bars->k_full[(kvi + 1) % KV_STAGES], ((kvi + 1) / KV_STAGES) & 1, wc))) break;
             if (j + 1 < I.nA) {
               if (!(ok = s_ready(0))) break;
               tc_fence_after();
-              FWD_TRACE(8192 + j * 8 + 1);
               issue_s(sq, 0, kvi + 1);
             }
             if (!(ok = s_ready(1))) break;
             tc_fence_after();
-            FWD_TRACE(8192 + j * 8 + 2);
             issue_s(sq, 1, kvi + 1);
           }
           if (!(ok = mbar_wait(&bars->v_full[s], (kvi / KV_STAGES) & 1, wc))) break;
           if (j < I.nA) {
             if (!(ok = mbar_wait(&bars->p_full[0], np[0] & 1, wc))) break;
             tc_fence_after();
-            FWD_TRACE(8192 + j * 8 + 3);
             issue_pv(0, kvi, j == 0);
           }
           if (!(ok = mbar_wait(&bars->p_full[1], np[1] & 1, wc))) break;
           tc_fence_after();
-          FWD_TRACE(8192 + j * 8 + 4);
           issue_pv(1, kvi, j == 0);
           tc_commit(&bars->kv_empty[s]);
         }
@@ -302,11 +275,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < n; ++j) {
         const uint32_t k = kbase + j;
-        const bool trc = (warp & 3) == 0 && lane == 0;
-        const int tb = x * 4096 + j * 8;
-        if (trc) FWD_TRACE(tb + 0);
         if (!(ok = mbar_wait(&bars->s_full[x], k & 1, wc))) break;
-        if (trc) FWD_TRACE(tb + 1);
         tc_fence_after();
         float s[BLOCK_N];
 #pragma unroll
@@ -343,14 +312,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (x == 0 ? j > 0 : j < I.nA) {
           if (!(ok = mbar_wait(&bars->turn[x], (x == 0 ? tbase + j - 1 : tbase + j) & 1, wc))) break;
         }
-        if (trc) FWD_TRACE(tb + 2);
         float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         uint32_t p[BLOCK_N / 2];
         auto step = [&](auto cc) {
           constexpr int c = decltype(cc)::value;
-          const float e0 = ex2_col<c, DGX_EXP_EMU_FWD>(fmaf(s[c], sl2, nmb)), e1 = ex2_col<c + 1, DGX_EXP_EMU_FWD>(fmaf(s[c + 1], sl2, nmb));
+          const float e0 = ex2(fmaf(s[c], sl2, nmb)), e1 = ex2(fmaf(s[c + 1], sl2, nmb));
           ps[(c >> 1) & 7] += e0 + e1;
-          p[c / 2] = pack_bf16x2_fast(e0, e1);
+          p[c / 2] = pack_bf16x2(e0, e1);
         };
         // Hand the turn to the other group (B only while A has tiles left)
         // before the last columns: the other group's wait ends while these
@@ -361,7 +329,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0 && (x == 0 || j + 1 < I.nA)) mbar_arrive(&bars->turn[x ^ 1]);
         static_for<TURN_AT, BLOCK_N, 2>(step);
         const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-        if (trc) FWD_TRACE(tb + 3);
         l_run = l_run * factor + rs;
         if (j > 0) {
           // PV(j-1) must be done: it reads the P buffer and accumulates O.
@@ -381,13 +348,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st_wait();
           }
         }
-        if (trc) FWD_TRACE(tb + 4);
         // P(j) overwrites P(j-1), which PV(j-1) (waited for above, or of the
         // previous item, which the epilogue waited for) has read.
 #pragma unroll
         for (int c = 0; c < BLOCK_N / 2; c += 16) tmem_st16(t_p + c, *reinterpret_cast<uint32_t(*)[16]>(&p[c]));
         tmem_st_wait();
-        if (trc) FWD_TRACE(tb + 5);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_full[x]);

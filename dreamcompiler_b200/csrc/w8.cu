@@ -14,7 +14,6 @@
 // The SIMT kernel below serves the other shapes: each warp owns two output
 // channels and reads their weight rows with 16-byte loads, fp32 products and
 // sums in mode 0, dp4a in mode 1.
-#include <mutex>
 
 #include "common.h"
 #include "w8.h"
@@ -256,14 +255,16 @@ using namespace dgx;
 
 extern "C" {
 
-dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, int K, void* stream) {
+dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, int K, void* stream) {  DGX_FAULT_POINT("dgx_quantize_rows_i8");
+
   if (B < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_quantize_rows_i8: negative size");
   if (B == 0) return DGX_OK;
   if (!X || !Xq || !sx) return set_error(DGX_EINVAL, "dgx_quantize_rows_i8: null pointer");
   return cuda_status(quantize_rows(X, Xq, sx, B, K, (cudaStream_t)stream), "dgx_quantize_rows_i8");
 }
 
-dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream) {
+dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream) {  DGX_FAULT_POINT("dgx_gemm_i8i32");
+
   if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: negative size");
   if (B == 0 || N == 0) return DGX_OK;
   if (!Xq || !W || !acc) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: null pointer");
@@ -304,7 +305,8 @@ static dgx_status w8_layer(const char* op, const float* X, const int8_t* W, cons
 extern "C" {
 
 dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y, int B,
-                       int N, int K, int mode, void* stream) {
+                       int N, int K, int mode, void* stream) {  DGX_FAULT_POINT("dgx_gemm_w8");
+
   if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_w8: negative size");
   if (mode != 0 && mode != 1) return set_error(DGX_EINVAL, "dgx_gemm_w8: mode %d", mode);
   if (B == 0 || N == 0) return DGX_OK;
@@ -314,7 +316,8 @@ dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, cons
 }
 
 dgx_status dgx_dense_q(const float* X, const int8_t* W, float scale, const float* scales, const float* bias,
-                       float* Y, int B, int out_dim, int in_dim, int relu, void* stream) {
+                       float* Y, int B, int out_dim, int in_dim, int relu, void* stream) {  DGX_FAULT_POINT("dgx_dense_q");
+
   if (B < 0 || out_dim < 0 || in_dim < 0) return set_error(DGX_EINVAL, "dgx_dense_q: negative size");
   if (B == 0 || out_dim == 0) return DGX_OK;
   if (!X || !W || !Y) return set_error(DGX_EINVAL, "dgx_dense_q: null pointer");
@@ -350,24 +353,14 @@ constexpr int kNoAllocMaxRows = 4096;                // row scales (16 KiB)
 static __device__ __align__(256) unsigned char g_w8a8_noalloc_scratch[kNoAllocMaxActs + kNoAllocMaxRows * sizeof(float)];
 
 namespace {
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};  // device address of the array, per device
-
 // In host code the array's name only stands for it; the kernels need its
-// device address, fetched once per device with that device current.
+// device address, looked up on every call with the caller's device current
+// (the lookup allocates nothing and stays right after a device reset).
 dgx_status noalloc_scratch(unsigned char** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return dgx::cuda_status(e, "dgx_gemm_w8a8_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= 64) return dgx::set_error(DGX_EUNSUPPORTED, "dgx_gemm_w8a8_noalloc: device %d", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_w8a8_noalloc_scratch);
-    if (e != cudaSuccess) return dgx::cuda_status(e, "dgx_gemm_w8a8_noalloc: cudaGetSymbolAddress");
-    g_noalloc_addr[dev] = p;
-  }
-  *out = static_cast<unsigned char*>(g_noalloc_addr[dev]);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_w8a8_noalloc_scratch);
+  if (e != cudaSuccess) return dgx::cuda_status(e, "dgx_gemm_w8a8_noalloc: cudaGetSymbolAddress");
+  *out = static_cast<unsigned char*>(p);
   return DGX_OK;
 }
 }  // namespace

@@ -37,26 +37,6 @@
 #include "sm100.cuh"
 #include "w8.h"
 
-// Optional phase tracing for kernel tuning: built with -DDGX_TRACE, each of
-// the first 256 CTAs records clock64() at the marked points (slot 15: the
-// global timer at entry) into dgx_w8_trace, read back with
-// dgx_w8_trace_read. Compiled out otherwise.
-#ifdef DGX_TRACE
-__device__ unsigned long long dgx_w8_trace[256 * 16];
-#define W8_TRACE(slot)                                                                                 \
-  do {                                                                                                 \
-    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);              \
-    if (cta_ < 256) dgx_w8_trace[cta_ * 16 + (slot)] = clock64();                                      \
-  } while (0)
-extern "C" int dgx_w8_trace_read(void* dst) {
-  return (int)cudaMemcpyFromSymbol(dst, dgx_w8_trace, sizeof(dgx_w8_trace));
-}
-#else
-#define W8_TRACE(slot) \
-  do {                 \
-  } while (0)
-#endif
-
 namespace dgx {
 
 namespace {
@@ -170,15 +150,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // L2 lines at once (the int32 sums do not depend on the order).
   const int krot = (int)((blockIdx.y * 5u) % (unsigned)nk);
   WaitCtx wc{abort_flag, a.err};
-#ifdef DGX_TRACE
-  if (threadIdx.x == 0) {
-    W8_TRACE(0);
-    unsigned long long gt;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
-    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    if (cta < 256) dgx_w8_trace[cta * 16 + 15] = gt;
-  }
-#endif
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -197,7 +168,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (threadIdx.x == 0) W8_TRACE(1);
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
@@ -213,9 +183,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         mbar_arrive_expect_tx(&full_bar[i], TC_W_BYTES + xbytes);
         tma_load_2d(smem + i * a.stage_bytes, &tmW, &full_bar[i], kx(i), m0);
       }
-      W8_TRACE(2);
       grid_dep_wait();
-      W8_TRACE(3);
       for (int i = 0; i < pro; ++i)
         tma_load_3d(smem + i * a.stage_bytes + TC_W_BYTES, &tmX, &full_bar[i], kx(i), b0, 0);
       int filled = pro;
@@ -227,7 +195,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tma_load_2d(st, &tmW, &full_bar[s], kx(i), m0);
         tma_load_3d(st + TC_W_BYTES, &tmX, &full_bar[s], kx(i), b0, 0);
       }
-      W8_TRACE(4);
       // Teardown: every stage filled must have landed before the CTA leaves.
       for (int f = max(0, filled - S); f < filled; ++f) mbar_drain(&full_bar[f % S], (f / S) & 1);
     }
@@ -244,7 +211,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           break;
         }
         tc_fence_after();
-        if (i == 0) W8_TRACE(5);
         const uint32_t sa = smem_u32(smem + s * a.stage_bytes);
         const uint32_t sb = sa + TC_W_BYTES;
 #pragma unroll
@@ -253,7 +219,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     (i > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&empty_bar[s]);
       }
-      W8_TRACE(6);
       if (ok) tc_commit(done_bar);
     }
     __syncwarp();
@@ -277,7 +242,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     named_bar_sync(1, 128);
     have = mbar_wait(done_bar, 0, wc);
     tc_fence_after();
-    if (threadIdx.x == 0) W8_TRACE(7);
     const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16);
     if (have && a.splits == 1 && a.tma_out) {
       // The tile [bc rows][128 channels] is assembled in the free stage ring
@@ -290,7 +254,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           uint32_t v[32];
           tmem_ld32(taddr + c, v);
           tmem_ld_wait();
-          if (threadIdx.x == 0 && c == 0) W8_TRACE(13);
           if (acc_only) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) tile[(c + j) * TC_BM] = __int_as_float((int)v[j]);
@@ -311,7 +274,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tmem_ld16(taddr + a.bc + c, v1);
           tmem_ld16(taddr + 2 * a.bc + c, v2);
           tmem_ld_wait();
-          if (threadIdx.x == 0 && c == 0) W8_TRACE(13);
           float f[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) f[j] = 0x1p-14f * rs_s[c + j];
@@ -326,7 +288,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       fence_proxy_async_smem();
       named_bar_sync(1, 128);
       if (threadIdx.x == 0) {
-        W8_TRACE(14);
         tma_store_2d(&tmOut, tile, m0, b0);
         bulk_commit();
         bulk_wait0();
@@ -394,10 +355,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   }
-  if (threadIdx.x == 0) W8_TRACE(8);
   if (a.splits > 1) {
     cluster_sync_all();  // every partial has landed in its inbox
-    if (threadIdx.x == 0) W8_TRACE(9);
     if (warp < 4 && n < a.N) {
       const int me = (int)cluster_rank();
       const int bs = me * a.per, be = min(nb, bs + a.per);
@@ -408,7 +367,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         w8_store(a, b0 + b, n, sc, bi, rs_s[b], acc[0], acc[1], acc[2]);
       }
     }
-    if (threadIdx.x == 0) W8_TRACE(10);
   }
 
   tc_fence_before();
@@ -417,7 +375,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, a.tmem_cols);
   }
-  if (threadIdx.x == 0) W8_TRACE(12);
 }
 
 // The power-of-two scale of a row with largest magnitude m: s = m/127
