@@ -1,6 +1,8 @@
 // C ABI entry points of libdgx: argument validation, dispatch to the sm_100a
 // kernels, error reporting. See include/dgx.h for the contract.
+#include <atomic>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -65,14 +67,34 @@ struct DeviceState {
 static std::mutex g_dev_mu;
 static DeviceState g_dev[64];
 
+// The error word lives in libdgx's device image (zero when the module
+// loads), so no entry point allocates to get it. Its device address is
+// looked up once per device; dgx_init looks it up again, so a caller that
+// reset the device calls dgx_init before the next op.
+static __device__ uint32_t g_error_word;
+
+static uint32_t* lookup_error_word() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_error_word) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return static_cast<uint32_t*>(p);
+}
+
 uint32_t* device_error_word() {
   const int d = current_device();
   std::lock_guard<std::mutex> lk(g_dev_mu);
   DeviceState& st = g_dev[d & 63];
-  if (!st.err_word) {
-    if (cudaMalloc(&st.err_word, sizeof(uint32_t)) != cudaSuccess) return nullptr;
-    cudaMemset(st.err_word, 0, sizeof(uint32_t));
-  }
+  if (!st.err_word) st.err_word = lookup_error_word();
+  return st.err_word;
+}
+
+static uint32_t* refresh_error_word() {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceState& st = g_dev[d & 63];
+  st.err_word = lookup_error_word();
   return st.err_word;
 }
 
@@ -101,6 +123,36 @@ void* library_scratch_slot(int slot, size_t bytes, cudaStream_t s) {
 
 void* library_scratch(size_t bytes, cudaStream_t s) { return library_scratch_slot(kScratchGeneral, bytes, s); }
 
+// Fault injection state: calls counted since the last dgx_fault_inject (or
+// process start), the call that fails (0: none) and its status.
+static std::atomic<long long> g_fault_calls{0};
+static std::atomic<long long> g_fault_at{-1};  // -1: environment not read yet
+static std::atomic<int> g_fault_status{DGX_ETIMEOUT};
+
+static void fault_from_env() {
+  long long at = 0;
+  int st = DGX_ETIMEOUT;
+  if (const char* v = getenv("DGX_FAIL_AT")) {
+    char* end = nullptr;
+    at = strtoll(v, &end, 10);
+    if (end && *end == ':') st = (int)strtol(end + 1, nullptr, 10);
+    if (at < 0) at = 0;
+    if (st <= DGX_OK || st > DGX_ENOMEM) st = DGX_ETIMEOUT;
+  }
+  long long expect = -1;
+  if (g_fault_at.compare_exchange_strong(expect, at)) g_fault_status.store(st);
+}
+
+bool fault_fires(const char* entry, dgx_status* st) {
+  if (g_fault_at.load(std::memory_order_relaxed) < 0) fault_from_env();
+  const long long at = g_fault_at.load(std::memory_order_relaxed);
+  if (at <= 0) return false;
+  const long long n = g_fault_calls.fetch_add(1) + 1;
+  if (n != at) return false;
+  *st = set_error((dgx_status)g_fault_status.load(), "injected fault at call %lld (%s)", n, entry);
+  return true;
+}
+
 static thread_local cudaEvent_t g_timer_start = nullptr, g_timer_stop = nullptr;
 
 TimerScope::TimerScope(cudaStream_t st) : s(st), stop(g_timer_stop) {
@@ -127,6 +179,19 @@ void dgx_set_timer_events(void* start, void* stop) {
   g_timer_stop = (cudaEvent_t)stop;
 }
 
+dgx_status dgx_fault_inject(long long at_call, int status) {
+  if (at_call < 0) return set_error(DGX_EINVAL, "dgx_fault_inject: negative call index");
+  if (at_call > 0 && (status <= DGX_OK || status > DGX_ENOMEM))
+    return set_error(DGX_EINVAL, "dgx_fault_inject: status %d is not an error status", status);
+  g_fault_at.store(-2);  // keep the environment from overriding this setting
+  g_fault_status.store(at_call > 0 ? status : DGX_ETIMEOUT);
+  g_fault_calls.store(0);
+  g_fault_at.store(at_call);
+  return DGX_OK;
+}
+
+long long dgx_fault_calls(void) { return g_fault_calls.load(); }
+
 dgx_status dgx_gemm_set_algo(int algo) {
   if (algo != 0 && algo != 1) return set_error(DGX_EINVAL, "dgx_gemm_set_algo: %d", algo);
   gemm_set_algo(algo);
@@ -146,16 +211,17 @@ dgx_status dgx_init(int device) {
   if (p.major != 10) return set_error(DGX_EUNSUPPORTED, "dgx_init: device is sm_%d%d, libdgx is built for sm_100a",
                                       p.major, p.minor);
   if (!get_tensor_map_encoder()) return set_error(DGX_ECUDA, "cuTensorMapEncodeTiled unavailable");
-  if (!device_error_word()) return set_error(DGX_ENOMEM, "dgx_init: cannot allocate the error word");
+  if (!refresh_error_word()) return set_error(DGX_ECUDA, "dgx_init: cannot find the device error word");
   return DGX_OK;
 }
 
-dgx_status dgx_sync_check(void* stream) {
+dgx_status dgx_sync_check(void* stream) {  DGX_FAULT_POINT("dgx_sync_check");
+
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_status(e, "dgx_sync_check");
   uint32_t* w = device_error_word();
-  if (!w) return set_error(DGX_ENOMEM, "dgx_sync_check: no error word");
+  if (!w) return set_error(DGX_ECUDA, "dgx_sync_check: no device error word");
   uint32_t v = 0;
   e = cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_status(e, "dgx_sync_check: read error word");
@@ -179,7 +245,8 @@ size_t dgx_gemm_workspace_size(int M, int N, int K, int transA, int transB, dgx_
 
 dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb, int ldc,
                     int transA, int transB, dgx_dtype ab_type, dgx_dtype c_type, int f32_mode, const float* bias,
-                    int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream) {
+                    int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream) {  DGX_FAULT_POINT("dgx_gemm");
+
   if (M < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm: negative size %dx%dx%d", M, N, K);
   if (M == 0 || N == 0) return DGX_OK;
   if (!C || (K > 0 && (!A || !B))) return set_error(DGX_EINVAL, "dgx_gemm: null operand");
@@ -248,7 +315,8 @@ extern "C" {
 
 dgx_status dgx_gemm_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K, int lda,
                             int ldb, int ldc, long long strideA, long long strideB, long long strideC, int transA,
-                            int transB, dgx_dtype ab_type, dgx_dtype c_type, float beta, void* stream) {
+                            int transB, dgx_dtype ab_type, dgx_dtype c_type, float beta, void* stream) {  DGX_FAULT_POINT("dgx_gemm_batched");
+
   if (batch < 0 || M < 0 || N < 0 || K < 0)
     return set_error(DGX_EINVAL, "dgx_gemm_batched: negative size %d x %dx%dx%d", batch, M, N, K);
   if (batch == 0 || M == 0 || N == 0) return DGX_OK;

@@ -21,6 +21,18 @@ TensorMapEncodeFn get_tensor_map_encoder();
 int num_sms();
 uint32_t* device_error_word();  // per-device word in global memory
 
+// Host-side fault injection (dgx_fault_inject, or DGX_FAIL_AT=<n>[:<status>]
+// in the environment): every entry point that launches device work counts
+// its calls; the n-th returns the chosen status with a message, launching
+// nothing. Failure handling above the library is tested this way without a
+// device fault.
+bool fault_fires(const char* entry, dgx_status* st);
+#define DGX_FAULT_POINT(entry)                     \
+  do {                                             \
+    dgx_status fault_st_;                          \
+    if (dgx::fault_fires(entry, &fault_st_)) return fault_st_; \
+  } while (0)
+
 // Record a message as the calling thread's last error and return `st`.
 dgx_status set_error(dgx_status st, const char* fmt, ...);
 dgx_status cuda_status(cudaError_t e, const char* what);

@@ -12,7 +12,8 @@ size_t dgx_flash_bwd_workspace_size(int BH, int S, int D) {
 }
 
 dgx_status dgx_flash_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int BH, int S, int D,
-                         float scale, int causal, dgx_dtype dtype, void* stream) {
+                         float scale, int causal, dgx_dtype dtype, void* stream) {  DGX_FAULT_POINT("dgx_flash_fwd");
+
   if (BH < 0 || S < 0 || D <= 0) return set_error(DGX_EINVAL, "dgx_flash_fwd: bad size BH=%d S=%d D=%d", BH, S, D);
   if (dtype != DGX_BF16) return set_error(DGX_EUNSUPPORTED, "dgx_flash_fwd: dtype %d (bf16 only)", dtype);
   if (BH == 0 || S == 0) return DGX_OK;
@@ -28,7 +29,8 @@ dgx_status dgx_flash_fwd(const void* Q, const void* K, const void* V, void* O, f
 
 dgx_status dgx_flash_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
                          const float* LSE, void* dQ, void* dK, void* dV, int BH, int S, int D, float scale,
-                         int causal, dgx_dtype dtype, void* workspace, size_t workspace_bytes, void* stream) {
+                         int causal, dgx_dtype dtype, void* workspace, size_t workspace_bytes, void* stream) {  DGX_FAULT_POINT("dgx_flash_bwd");
+
   if (BH < 0 || S < 0 || D <= 0) return set_error(DGX_EINVAL, "dgx_flash_bwd: bad size BH=%d S=%d D=%d", BH, S, D);
   if (dtype != DGX_BF16) return set_error(DGX_EUNSUPPORTED, "dgx_flash_bwd: dtype %d (bf16 only)", dtype);
   if (BH == 0 || S == 0) return DGX_OK;
@@ -68,7 +70,8 @@ static dgx_status rows_check(const char* op, int B, int H, int S, int D, const v
 }
 
 dgx_status dgx_flash_fwd_rows(const void* Q, int ldq, const void* K, int ldk, const void* V, int ldv, void* O,
-                              int ldo, float* LSE, int B, int H, int S, int D, float scale, int causal, void* stream) {
+                              int ldo, float* LSE, int B, int H, int S, int D, float scale, int causal, void* stream) {  DGX_FAULT_POINT("dgx_flash_fwd_rows");
+
   const void* ptrs[4] = {Q, K, V, O};
   const int lds[4] = {ldq, ldk, ldv, ldo};
   dgx_status st = rows_check("dgx_flash_fwd_rows", B, H, S, D, ptrs, lds, 4);
@@ -86,7 +89,8 @@ dgx_status dgx_flash_fwd_rows(const void* Q, int ldq, const void* K, int ldk, co
 dgx_status dgx_flash_bwd_rows(const void* Q, int ldq, const void* K, int ldk, const void* V, int ldv, const void* O,
                               int ldo, const void* dO, int lddo, const float* LSE, void* dQ, int lddq, void* dK,
                               int lddk, void* dV, int lddv, int B, int H, int S, int D, float scale, int causal,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+                              void* workspace, size_t workspace_bytes, void* stream) {  DGX_FAULT_POINT("dgx_flash_bwd_rows");
+
   const void* ptrs[8] = {Q, K, V, O, dO, dQ, dK, dV};
   const int lds[8] = {ldq, ldk, ldv, ldo, lddo, lddq, lddk, lddv};
   dgx_status st = rows_check("dgx_flash_bwd_rows", B, H, S, D, ptrs, lds, 8);

@@ -81,6 +81,20 @@ struct SignalArgs {
   uint32_t* err;
 };
 
+// Wait until *flag >= epoch (system-scope acquire), at most budget_cycles
+// SM clocks; on running out record DGX_DEV_ERR_TIMEOUT and return false.
+__device__ __forceinline__ bool bounded_flag_wait(const unsigned long long* flag, unsigned long long epoch,
+                                                  long long budget_cycles, uint32_t* err) {
+  const long long t0 = clock64();
+  while (ld_acquire_sys(flag) < epoch) {
+    if (clock64() - t0 > budget_cycles) {
+      if (err) atomicOr(err, DGX_DEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Lane i < world: publish "rank done" into rank i's slot array, then wait for
 // slot i of our own array. Runs after the GEMM kernel on the same stream, so
 // every peer store of this rank's tiles precedes the release.
@@ -89,14 +103,30 @@ __global__ void tp_signal_wait_kernel(SignalArgs a) {
   if (i < a.world) {
     __threadfence_system();
     st_release_sys(a.peer_flags[i] + a.rank, a.epoch);
-    const long long t0 = clock64();
-    while (ld_acquire_sys(a.my_flags + i) < a.epoch) {
-      if (clock64() - t0 > a.budget_cycles) {
-        atomicOr(a.err, DGX_DEV_ERR_TIMEOUT);
-        break;
-      }
-    }
+    bounded_flag_wait(a.my_flags + i, a.epoch, a.budget_cycles, a.err);
   }
+}
+
+// dgx_wait_probe: one warp runs one of the library's bounded waits.
+//   kind 0: the cross-rank completion wait above, on `flag`, `budget_cycles`.
+//   kind 1: the mbarrier wait every tensor-core kernel pipeline uses
+//           (mbar_wait, its fixed budget of about a second); when `expect` is
+//           0 the probe completes the barrier phase itself first.
+__global__ void wait_probe_kernel(int kind, const unsigned long long* flag, unsigned long long expect,
+                                  long long budget_cycles, uint32_t* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;
+  if (kind == 0) {
+    bounded_flag_wait(flag, expect, budget_cycles, err);
+    return;
+  }
+  abort_flag = 0;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  if (expect == 0) mbar_arrive(&bar);
+  WaitCtx wc{&abort_flag, err};
+  mbar_wait(&bar, 0, wc);
 }
 
 }  // namespace
@@ -143,7 +173,8 @@ dgx_status dgx_tp_export(void* C_full, size_t c_bytes, void* handle_out, size_t 
   return DGX_OK;
 }
 
-dgx_status dgx_tp_open(int rank, int world, const void* handles) {
+dgx_status dgx_tp_open(int rank, int world, const void* handles) {  DGX_FAULT_POINT("dgx_tp_open");
+
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
     return set_error(DGX_EINVAL, "dgx_tp_open: rank %d of world %d (max %d)", rank, world, kMaxRanks);
   if (!handles) return set_error(DGX_EINVAL, "dgx_tp_open: null handles");
@@ -176,7 +207,8 @@ dgx_status dgx_tp_open(int rank, int world, const void* handles) {
 }
 
 dgx_status dgx_tp_gemm_colsplit(const void* A, const void* B_shard, int M, int N, int K, dgx_dtype ab_type,
-                                dgx_dtype c_type, int timeout_ms, void* stream) {
+                                dgx_dtype c_type, int timeout_ms, void* stream) {  DGX_FAULT_POINT("dgx_tp_gemm_colsplit");
+
   if (M < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_tp_gemm_colsplit: negative size");
   if (ab_type != DGX_BF16 && ab_type != DGX_F32) return set_error(DGX_EINVAL, "dgx_tp_gemm_colsplit: ab_type");
   if (c_type != DGX_BF16 && c_type != DGX_F32) return set_error(DGX_EINVAL, "dgx_tp_gemm_colsplit: c_type");
@@ -227,6 +259,17 @@ dgx_status dgx_tp_gemm_colsplit(const void* A, const void* B_shard, int M, int N
   sa.err = device_error_word();
   tp_signal_wait_kernel<<<1, 32, 0, s>>>(sa);
   return cuda_status(cudaGetLastError(), "dgx_tp_gemm_colsplit signal");
+}
+
+dgx_status dgx_wait_probe(int kind, const unsigned long long* flag, unsigned long long expect, int timeout_us,
+                          void* stream) {
+  DGX_FAULT_POINT("dgx_wait_probe");
+  if (kind != 0 && kind != 1) return set_error(DGX_EINVAL, "dgx_wait_probe: kind %d", kind);
+  if (kind == 0 && !flag) return set_error(DGX_EINVAL, "dgx_wait_probe: null flag");
+  if (timeout_us < 0) return set_error(DGX_EINVAL, "dgx_wait_probe: negative timeout");
+  const long long budget = (long long)timeout_us * 2000ll;  // ~2 GHz SM clock
+  wait_probe_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(kind, flag, expect, budget, device_error_word());
+  return cuda_status(cudaGetLastError(), "dgx_wait_probe");
 }
 
 dgx_status dgx_tp_close(void) {

@@ -57,6 +57,36 @@ dgx_status dgx_init(int device);
  * waits in the kernels report into. DGX_ETIMEOUT if any wait ran out. */
 dgx_status dgx_sync_check(void* stream);
 
+/* Failure detection without a device fault.
+ *
+ * dgx_fault_inject: host-side fault injection. Every entry point that
+ * launches device work (and dgx_sync_check, dgx_tp_open) counts its calls
+ * from 1; call number `at_call` returns `status` (an error status) with the
+ * message "injected fault at call n (<entry point>)" and launches nothing.
+ * at_call = 0 turns injection off. The counter restarts on every
+ * dgx_fault_inject. The environment variable DGX_FAIL_AT=<n>[:<status>]
+ * (status defaults to DGX_ETIMEOUT) sets the same thing at the first call.
+ * Calls a convolution makes through dgx_gemm count as well. The reference
+ * has no counterpart; its error path (RUNTIME ERROR and a 1x1 result,
+ * runtime/ops/elementwise.inc:972-989) is what the Dream op mirror turns a
+ * non-OK status into, and this lets callers test that path.
+ * dgx_fault_calls: calls counted so far. */
+dgx_status dgx_fault_inject(long long at_call, int status);
+long long dgx_fault_calls(void);
+
+/* dgx_wait_probe: run one of the library's bounded device waits in a
+ * one-warp kernel on `stream`, so a caller can check on one GPU that a wait
+ * which never completes ends with DGX_ETIMEOUT from dgx_sync_check and
+ * leaves the context usable.
+ *   kind 0: the cross-rank completion wait of dgx_tp_gemm_colsplit: wait
+ *           until *flag (device memory) >= expect, at most timeout_us.
+ *   kind 1: the mbarrier wait of every tensor-core kernel's pipeline, with
+ *           its fixed budget of about one second; expect = 0 completes the
+ *           barrier first (the wait succeeds), anything else leaves it
+ *           incomplete (flag and timeout_us are not used). */
+dgx_status dgx_wait_probe(int kind, const unsigned long long* flag, unsigned long long expect, int timeout_us,
+                          void* stream);
+
 /* Profiling hook: the next main kernel this thread launches (the tensor-core
  * kernel behind dgx_gemm, dgx_flash_fwd or dgx_flash_bwd) is bracketed by
  * cudaEventRecord(start) / cudaEventRecord(stop) on the stream it runs on,
@@ -223,8 +253,10 @@ dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, cons
  *   libdgx's device image (4 MiB + 16 KiB, held on every GPU that loads the
  *   library until the process exits), so the call allocates nothing.
  *   Limits: B <= 4096 and B*K <= 4,194,304; larger problems return DGX_EINVAL.
- *   The first call on a device looks up the array's device address
- *   (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   Every call looks up the array's device address (cudaGetSymbolAddress,
+ *   which allocates nothing); make the first call on a device before any
+ *   stream capture. dgx_init is not required first: the device error word
+ *   the kernels report into is a fixed word in the same image as well.
  *   All calls share the array and it keeps the last call's contents: calls
  *   that overlap on the GPU (other streams, other host threads) race on it,
  *   so issue them in order on one stream.
