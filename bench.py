@@ -51,13 +51,16 @@ def parse():
 
 
 def peaks():
+    """(burst, sustained, source) dense bf16 TFLOP/s. The headline kernels are
+    timed in a region of a few milliseconds, so the burst figure is their
+    denominator."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             p = json.load(f)
-        return p["bf16_tflops_sustained"], p["bf16_tflops"], "measured"
+        return p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
     except Exception:
-        return 1400.0, 1590.0, "fallback"
+        return 1590.0, 1400.0, "fallback"
 
 
 # ---------------------------------------------------------------- CPU side
@@ -317,17 +320,43 @@ def run_tp_gemm(args, rank, world, local_rank):
     column-sharded over the ranks (reference widths), the all-gather of C
     fused into the GEMM epilogue (NVLink peer stores). Strong scaling: the
     problem is fixed, each rank computes N/world columns. Returns the max over
-    ranks of the per-step time."""
+    ranks of the per-step time, and (N > 1) the max over ranks of a 1-GPU
+    pass of the whole product timed just before it on the same GPUs, the
+    denominator of the strong-scaling efficiency."""
     import torch
     import torch.distributed as dist
+    import dreamcompiler_b200 as dgx
     from dreamcompiler_b200 import tp
     dev = torch.device("cuda", local_rank)
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     n = TP_N
+    steps = max(3, min(args.steps, 20))
+    t1 = None
+    if world > 1:
+        # every rank runs the unsharded GEMM alone (no peer traffic): T(1)
+        A1 = (torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16()
+        B1 = (torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16()
+        C1 = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+        s1 = max(3, steps // 2)
+        for _ in range(2):
+            dgx.gemm(A1, B1, out=C1)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(s1):
+            dgx.gemm(A1, B1, out=C1)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        dgx.sync_check()
+        tt = torch.tensor([e0.elapsed_time(e1) / 1e3 / s1], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t1 = tt.item()
+        del A1, B1, C1
+        torch.cuda.empty_cache()
     gemm = tp.ColumnParallelGemm(n, n, n, rank, world, out_dtype=torch.bfloat16, device=dev)
     A = (torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16()
     B = (torch.randn(n, gemm.ncol, device=dev, generator=g) / n ** 0.5).bfloat16()
-    steps = max(3, min(args.steps, 20))
     for _ in range(3):
         gemm(A, B)
     torch.cuda.synchronize(dev)
@@ -339,7 +368,6 @@ def run_tp_gemm(args, rank, world, local_rank):
         gemm(A, B)
     e1.record()
     torch.cuda.synchronize(dev)
-    import dreamcompiler_b200 as dgx
     dgx.sync_check()
     t = torch.tensor([e0.elapsed_time(e1) / 1e3 / steps], device=dev, dtype=torch.float64)
     if world > 1:
@@ -348,7 +376,7 @@ def run_tp_gemm(args, rank, world, local_rank):
     gemm.close()
     del A, B, gemm
     torch.cuda.empty_cache()
-    return t.item(), steps
+    return t.item(), steps, (t1 if t1 is not None else t.item())
 
 
 def run_secondary(local_rank):
@@ -391,7 +419,9 @@ def run_secondary(local_rank):
                 graph.replay()
             e1.record()
             torch.cuda.synchronize(dev)
-        last_clk["sm_mhz"] = clk.summary()["sm_mhz"]
+        summ = clk.summary()
+        last_clk.clear()
+        last_clk.update({"sm_mhz": summ["sm_mhz"], "sm_max_mhz": summ["sm_max_mhz"], "reasons": summ["reasons"]})
         dgx.sync_check()
         del graph
         return e0.elapsed_time(e1) / 1e3 / (iters * reps)
@@ -412,7 +442,7 @@ def run_secondary(local_rank):
             byts = N * K + Bn * K * 4 + Bn * N * 4 + N * 8
             w8[f"B{Bn}_{'w8a32' if mode == 0 else 'w8a8'}"] = {"us": t * 1e6, "gb_s": byts / t / 1e9,
                                                                "tops": 2 * Bn * N * K / t / 1e12,
-                                                               "sm_mhz": last_clk["sm_mhz"]}
+                                                               "clocks": dict(last_clk)}
     res["config5_int8_w8"] = w8
     del Ws
     torch.cuda.empty_cache()
@@ -432,7 +462,7 @@ def run_secondary(local_rank):
         dgx.gemm(A, dC, transA=True, out=dB, workspace=ws)
     t = timed(f32_step, 50)
     res["config1_f32_gemm_1024_fwd_bwd"] = {"ms_per_step": t * 1e3, "tflops": 6 * n ** 3 / t / 1e12,
-                                            "sm_mhz": last_clk["sm_mhz"],
+                                            "clocks": dict(last_clk),
                                             "path": "3xTF32 on tcgen05 kind::tf32 (3 MMAs per K step)"}
     del sets, C, dA, dB, ws
 
@@ -447,7 +477,7 @@ def run_secondary(local_rank):
     t = timed(lambda i: model.step(), 4)
     res["config3_gpt_train_step"] = {"ms_per_step": t * 1e3, "tokens_per_s": cfg.batch * cfg.seq_len / t,
                                      "tflops": cfg.flops_per_step() / t / 1e12, "loss": float(model.loss.item()),
-                                     "sm_mhz": last_clk["sm_mhz"],
+                                     "clocks": dict(last_clk),
                                      "params": cfg.n_params(), "algorithmic_flop_per_step": cfg.flops_per_step(),
                                      "precision": "bf16 GEMM/attention operands, fp32 master weights, grads, AdamW"}
     del model
@@ -461,7 +491,7 @@ def run_secondary(local_rank):
         B = [(torch.randn(n, n, device=dev, generator=g) / n ** 0.5).bfloat16() for _ in range(copies)]
         Cb = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
         t = timed(lambda i: dgx.gemm(A[i % copies], B[i % copies], out=Cb), 20 if n < 16384 else 6)
-        sweep[str(n)] = {"ms": t * 1e3, "tflops": 2 * n ** 3 / t / 1e12, "sm_mhz": last_clk["sm_mhz"]}
+        sweep[str(n)] = {"ms": t * 1e3, "tflops": 2 * n ** 3 / t / 1e12, "clocks": dict(last_clk)}
         del A, B, Cb
         torch.cuda.empty_cache()
     res["config4_bf16_gemm"] = sweep
@@ -524,9 +554,12 @@ def main():
         from oracle import cpu_bench
         kind = cpu_bench.available_kind()
         w = cpu_workers()
-        tf, wall = cpu_flash_sample(w, kind)
-        cpu = {"value": tf, "unit": "TFLOPS", "cores": w, "kind": kind,
-               "sample": f"{w} heads of config 2 (S=2048, dk=64) fwd+bwd, one per process, {wall:.2f} s wall"}
+        samples = [cpu_flash_sample(w, kind, seed0=i * w) for i in range(3)]
+        tfs = sorted(tf for tf, _ in samples)
+        cpu = {"value": statistics.median(tfs), "unit": "TFLOPS", "cores": w, "kind": kind,
+               "samples": tfs,
+               "sample": f"median of 3 samples, each {w} heads of config 2 (S=2048, dk=64) fwd+bwd, one per "
+                         f"process ({', '.join('%.2f' % wl for _, wl in samples)} s wall)"}
 
     if world > 1:
         import torch.distributed as dist
@@ -536,7 +569,7 @@ def main():
     # the secondary configs (1 GPU) before the TP GEMM: its 16384^3 steps
     # leave the part power-capped for a while
     secondary = run_secondary(local_rank) if world == 1 and not args.no_secondary else None
-    tp_s, tp_steps = run_tp_gemm(args, rank, world, local_rank)
+    tp_s, tp_steps, tp_s1 = run_tp_gemm(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -544,7 +577,7 @@ def main():
         return
     step_flop = FWD_FLOP + BWD_FLOP
     value = n * step_flop * args.steps / elapsed / 1e12
-    sustained, burst, src = peaks()
+    burst, sustained, src = peaks()
     achieved = BWD_FLOP / bwd_kernel_s / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": n, "steps": args.steps,
@@ -552,10 +585,10 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: bf16 Q/K/V/dO ~ N(0,1), seeded, config 2 shapes", "config": CONFIG,
         "pct_of_peak": {"per_gpu_tflops": value / n, "of_nominal_dense_bf16_2250": value / n / NOMINAL_DENSE_BF16,
-                        f"of_{src}_bf16_sustained": value / n / sustained},
-        "roofline": {"kernel": "flash_bwd_kernel", "bound": "tensor", "achieved": achieved, "peak": sustained,
-                     "peak_source": f"{src} bf16 sustained (kernel timed inside a long loop)",
-                     "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": traffic_per_launch(),
+                        f"of_{src}_bf16_burst": value / n / burst},
+        "roofline": {"kernel": "flash_bwd_kernel", "bound": "tensor", "achieved": achieved, "peak": burst,
+                     "peak_source": f"{src} bf16 burst (the kernel is timed in a region of a few ms)",
+                     "unit": "TFLOP/s", "frac": achieved / burst, "traffic": traffic_per_launch(),
                      "algorithmic": f"{BWD_FLOP:.4g} FLOP per launch = 10*BH*S^2*D/2 (causal)"},
         "e2e": {"value": n * step_flop / e2e_s / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": 4 * BH * S * D * 2,
                 "d2h_bytes_per_step": 4 * BH * S * D * 2,
@@ -567,6 +600,8 @@ def main():
                               "GPU(s), all-gather fused into the epilogue (NVLink peer stores)",
                     "scaling": "strong", "value": 2.0 * TP_N ** 3 / tp_s / 1e12, "unit": "TFLOPS",
                     "ms_per_step": tp_s * 1e3, "steps": tp_steps,
+                    "ms_per_step_1gpu_same_run": tp_s1 * 1e3,
+                    "efficiency_vs_n1": tp_s1 / (n * tp_s),
                     "per_gpu_frac_of_measured_bf16": 2.0 * TP_N ** 3 / tp_s / 1e12 / n / burst},
         "gpu_launches": 4 * args.steps,
         "clocks": clocks,
