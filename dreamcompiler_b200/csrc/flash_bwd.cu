@@ -343,9 +343,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               float lv[32];
 #pragma unroll
               for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
-              static_for<0, 32, 1>([&](auto tt) {
+              static_for<0, 32, 2>([&](auto tt) {  // column pairs: one packed fp32 FMA per two scores
                 constexpr int t = decltype(tt)::value;
-                p[cc + t] = ex2(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
+                const float2 a = ffma2(__uint_as_float(sv[cc + t]), __uint_as_float(sv[cc + t + 1]), sl2, -lv[t],
+                                       -lv[t + 1]);
+                p[cc + t] = ex2(a.x);
+                p[cc + t + 1] = ex2(a.y);
               });
             }
           } else {
@@ -389,10 +392,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_ld_wait();
           uint32_t pk[16];
 #pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            const float ds0 = p[cc + t] * (__uint_as_float(dv[t]) - dd[t]);
-            const float ds1 = p[cc + t + 1] * (__uint_as_float(dv[t + 1]) - dd[t + 1]);
-            pk[t / 2] = pack_bf16x2(ds0, ds1);
+          for (int t = 0; t < 32; t += 2) {  // dS = P o (dP - D), two columns per packed op
+            const float2 ds = fsubmul2(__uint_as_float(dv[t]), __uint_as_float(dv[t + 1]), dd[t], dd[t + 1], p[cc + t],
+                                       p[cc + t + 1]);
+            pk[t / 2] = pack_bf16x2(ds.x, ds.y);
           }
           tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
           // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries

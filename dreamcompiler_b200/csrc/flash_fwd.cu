@@ -9,7 +9,7 @@
 // the heaviest (latest causal) blocks first; Q of the next item loads into a
 // second buffer while the current one runs. An item is two 128-row tiles
 // (A, B) that share every K/V tile load. Warps 0-3 run tile A's softmax, warps 4-7 tile B's, warp 8
-// issues TMA loads, warp 9 issues tcgen05.mma. TMEM holds S_A, S_B (128 fp32
+// issues TMA loads, warps 9 and 10 issue tile A's and tile B's tcgen05.mma. TMEM holds S_A, S_B (128 fp32
 // columns each), O_A, O_B (D fp32 columns each) and P_A, P_B (128 bf16 = 64
 // columns each, the A operand of the P.V MMA read straight from TMEM). A
 // softmax warpgroup frees its S buffer as soon as S is in registers, so the
@@ -38,7 +38,7 @@ constexpr int BLOCK_N = 128;   // keys per K/V tile
 constexpr int DP = 64;         // head dim held in shared memory / TMEM (D <= 64 zero-padded)
 constexpr int KV_STAGES = 3;
 constexpr int TILE_BYTES = BLOCK_M * DP * 2;  // 16 KB for every Q/K/V tile
-constexpr int NUM_THREADS = 384;  // WG0: softmax A, WG1: softmax B, WG2: TMA warp, MMA warp, 2 idle
+constexpr int NUM_THREADS = 384;  // WG0: softmax A, WG1: softmax B, WG2: TMA warp, two MMA warps, 1 idle
 // setmaxnreg split (per thread): 2 x 224 + 56 = 504 <= 3 x 168 (65536 / 384 rounded down to 8).
 constexpr uint32_t REG_SOFTMAX = 224, REG_CTRL = 56;
 constexpr float RESCALE_LOG2 = 8.0f;
@@ -111,12 +111,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->q_full[b], 1);
-      mbar_init(&bars->q_empty[b], 1);
+      mbar_init(&bars->q_empty[b], 2);
     }
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->kv_empty[s], 2);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->s_full[x], 1);
@@ -174,76 +174,76 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_drain(&bars->v_full[f % KV_STAGES], (f / KV_STAGES) & 1);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 9 || warp == 10) {
     // ---------------------------------------------------------------- MMA
+    // One issuing warp per Q tile (warp 9: A, warp 10: B), so each tile's
+    // S -> softmax -> P -> PV chain runs at its own pace and neither waits
+    // behind the other's MMAs in one issue order. Each warp's commits cover
+    // its own MMAs: a K/V stage and a Q buffer are free once both warps
+    // have committed (barriers of count 2).
     if (elect_one_lane()) {
+      const int x = warp - 9;
       constexpr uint32_t idesc_s = make_idesc(1, 0, 0, BLOCK_M, BLOCK_N);  // Q.K^T, both K-major
       constexpr uint32_t idesc_o = make_idesc(1, 0, 1, BLOCK_M, DP);       // P (TMEM) . V (MN-major)
       const uint32_t sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V);
-      // issued S / PV per softmax group, over all items
-      uint32_t ns[2] = {0, 0}, np[2] = {0, 0};
-      uint32_t gkv = 0, ic = 0;
+      const uint32_t t_sx = tmem + (x ? T_S1 : T_S0), t_ox = tmem + (x ? T_O1 : T_O0), t_px = tmem + (x ? T_P1 : T_P0);
+      uint32_t ns = 0, np = 0;  // S and PV tiles issued by this warp
+      uint32_t gkv = 0, ic = 0;  // K/V tiles and items walked
       bool ok = true;
       // Descriptors advance by adding (byte offset >> 4) to the start field.
-      auto issue_s = [&](uint32_t sq, int x, uint32_t kvi) {
+      auto issue_s = [&](uint32_t sq, uint32_t kvi) {
         const uint64_t dq = sw128_desc(sq + x * TILE_BYTES, 16, 1024);
         const uint64_t dk = sw128_desc(sk + (kvi % KV_STAGES) * TILE_BYTES, 16, 1024);
-        const uint32_t d = tmem + (x ? T_S1 : T_S0);
 #pragma unroll 1
-        for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(d, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(t_sx, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
         tc_commit(&bars->s_full[x]);
-        ++ns[x];
+        ++ns;
       };
-      auto issue_pv = [&](int x, uint32_t kvi, bool first) {
+      auto issue_pv = [&](uint32_t kvi, bool first) {
         const uint64_t dv = sw128_desc(sv + (kvi % KV_STAGES) * TILE_BYTES, DP * 128, 1024);
-        const uint32_t d = tmem + (x ? T_O1 : T_O0), a = tmem + (x ? T_P1 : T_P0);
 #pragma unroll 1
         for (int kk = 0; kk < BLOCK_N / 16; ++kk)  // 16 keys = 8 packed bf16 columns per step
-          mma_f16_ts(d, a + kk * 8, dv + 128 * kk, idesc_o, (!first || kk > 0) ? 1u : 0u);
+          mma_f16_ts(t_ox, t_px + kk * 8, dv + 128 * kk, idesc_o, (!first || kk > 0) ? 1u : 0u);
         tc_commit(&bars->pv_done[x]);
-        ++np[x];
+        ++np;
       };
-      // The S buffer of group x is free once the softmax read the previous S.
-      auto s_ready = [&](int x) { return ns[x] == 0 || mbar_wait(&bars->s_free[x], (ns[x] - 1) & 1, wc); };
+      // The S buffer is free once the softmax has read the previous S.
+      auto s_ready = [&]() { return ns == 0 || mbar_wait(&bars->s_free[x], (ns - 1) & 1, wc); };
       for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
         const FwdItem I = fwd_item(args, w);
         const int qb2 = ic & 1;
+        const int n = x ? I.nB : I.nA;
         const uint32_t sq = smem_u32(smem + SM_Q + qb2 * 2 * TILE_BYTES);
-        if (!(ok = mbar_wait(&bars->q_full[qb2], (ic >> 1) & 1, wc) &&
-                   mbar_wait(&bars->k_full[gkv % KV_STAGES], (gkv / KV_STAGES) & 1, wc)))
-          break;
-        if (I.nA > 0) {
-          if (!(ok = s_ready(0))) break;
+        if (!(ok = mbar_wait(&bars->q_full[qb2], (ic >> 1) & 1, wc))) break;
+        if (n > 0) {
+          if (!(ok = mbar_wait(&bars->k_full[gkv % KV_STAGES], (gkv / KV_STAGES) & 1, wc) && s_ready())) break;
           tc_fence_after();
-          issue_s(sq, 0, gkv);
+          issue_s(sq, gkv);
         }
-        if (!(ok = s_ready(1))) break;
-        tc_fence_after();
-        issue_s(sq, 1, gkv);
-        for (int j = 0; ok && j < I.nB; ++j) {
+        for (int j = 0; ok && j < n; ++j) {
           const uint32_t kvi = gkv + j;
-          const int s = kvi % KV_STAGES;
-          if (j + 1 < I.nB) {
-            if (!(ok = mbar_wait(&bars->k_full[(kvi + 1) % KV_STAGES], ((kvi + 1) / KV_STAGES) & 1, wc))) break;
-            if (j + 1 < I.nA) {
-              if (!(ok = s_ready(0))) break;
-              tc_fence_after();
-              issue_s(sq, 0, kvi + 1);
-            }
-            if (!(ok = s_ready(1))) break;
+          if (j + 1 < n) {
+            if (!(ok = mbar_wait(&bars->k_full[(kvi + 1) % KV_STAGES], ((kvi + 1) / KV_STAGES) & 1, wc) &&
+                       s_ready()))
+              break;
             tc_fence_after();
-            issue_s(sq, 1, kvi + 1);
+            issue_s(sq, kvi + 1);
           }
-          if (!(ok = mbar_wait(&bars->v_full[s], (kvi / KV_STAGES) & 1, wc))) break;
-          if (j < I.nA) {
-            if (!(ok = mbar_wait(&bars->p_full[0], np[0] & 1, wc))) break;
-            tc_fence_after();
-            issue_pv(0, kvi, j == 0);
-          }
-          if (!(ok = mbar_wait(&bars->p_full[1], np[1] & 1, wc))) break;
+          if (!(ok = mbar_wait(&bars->v_full[kvi % KV_STAGES], (kvi / KV_STAGES) & 1, wc) &&
+                     mbar_wait(&bars->p_full[x], np & 1, wc)))
+            break;
           tc_fence_after();
-          issue_pv(1, kvi, j == 0);
-          tc_commit(&bars->kv_empty[s]);
+          issue_pv(kvi, j == 0);
+          tc_commit(&bars->kv_empty[kvi % KV_STAGES]);
+        }
+        if (!ok) break;
+        // K/V tiles this tile does not see (tile A under causal: the last one)
+        // still need this warp's arrival; their load having landed means the
+        // stage's previous use is released, so the arrival counts for this use.
+        for (int j = n; ok && j < I.nB; ++j) {
+          const uint32_t kvi = gkv + j;
+          if (!(ok = mbar_wait(&bars->k_full[kvi % KV_STAGES], (kvi / KV_STAGES) & 1, wc))) break;
+          tc_commit(&bars->kv_empty[kvi % KV_STAGES]);
         }
         tc_commit(&bars->q_empty[qb2]);  // every S of this item has read Q
         gkv += I.nB;
@@ -293,12 +293,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int c = 0; c < BLOCK_N; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
         }
         // Row max of the raw scores with 8 independent partial maxima (short
-        // dependency chains); scale > 0, so max(s)*sl2 = max(s*sl2).
+        // dependency chains, two new columns per three-input max); scale > 0,
+        // so max(s)*sl2 = max(s*sl2).
         float pm[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) pm[i] = s[i];
 #pragma unroll
-        for (int c = 8; c < BLOCK_N; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+        for (int c = 8; c < BLOCK_N; c += 2) pm[(c >> 1) & 7] = max3f(pm[(c >> 1) & 7], s[c], s[c + 1]);
         const float mt = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                                fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
         // lazy rescale
@@ -312,12 +313,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (x == 0 ? j > 0 : j < I.nA) {
           if (!(ok = mbar_wait(&bars->turn[x], (x == 0 ? tbase + j - 1 : tbase + j) & 1, wc))) break;
         }
-        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // Column pairs go through the packed fp32 forms: one FMA-pipe
+        // instruction scales two scores, one adds two exponentials into the
+        // row sum's four partial pairs.
+        float2 ps[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
         uint32_t p[BLOCK_N / 2];
         auto step = [&](auto cc) {
           constexpr int c = decltype(cc)::value;
-          const float e0 = ex2(fmaf(s[c], sl2, nmb)), e1 = ex2(fmaf(s[c + 1], sl2, nmb));
-          ps[(c >> 1) & 7] += e0 + e1;
+          const float2 a = ffma2(s[c], s[c + 1], sl2, nmb);
+          const float e0 = ex2(a.x), e1 = ex2(a.y);
+          ps[(c >> 1) & 3] = fadd2(ps[(c >> 1) & 3], e0, e1);
           p[c / 2] = pack_bf16x2(e0, e1);
         };
         // Hand the turn to the other group (B only while A has tiles left)
@@ -328,7 +333,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
         if (lane == 0 && (x == 0 || j + 1 < I.nA)) mbar_arrive(&bars->turn[x ^ 1]);
         static_for<TURN_AT, BLOCK_N, 2>(step);
-        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        const float rs = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
         l_run = l_run * factor + rs;
         if (j > 0) {
           // PV(j-1) must be done: it reads the P buffer and accumulates O.

@@ -328,6 +328,50 @@ __device__ __forceinline__ void static_for(F&& f) {
 }
 
 // ---------------------------------------------------------------- numerics
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// Packed fp32 pairs (sm_100 f32x2): {a0, a1} * b + c and {a0, a1} + {b0, b1},
+// each one instruction for two lanes' worth of FMA-pipe work, rounded as the
+// scalar forms.
+__device__ __forceinline__ float2 ffma2(float a0, float a1, float b, float c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+  return r;
+}
+// {a0, a1} * b + {c0, c1}
+__device__ __forceinline__ float2 ffma2(float a0, float a1, float b, float c0, float c1) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %6};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c0), "f"(c1));
+  return r;
+}
+// ({a0, a1} - {b0, b1}) * {p0, p1}
+__device__ __forceinline__ float2 fsubmul2(float a0, float a1, float b0, float b1, float p0, float p1) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rp, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rp, {%6, %7};\n\tsub.rn.f32x2 rd, ra, rb;\n\tmul.rn.f32x2 rd, rd, rp;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(p0), "f"(p1));
+  return r;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float b0, float b1) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b0), "f"(b1));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
