@@ -43,6 +43,7 @@ SIGNATURES = {
     "dgx_convert": (_i, [_vp, _i, _vp, _i, _sz, _i, _vp]),
     "dgx_gemm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _f, _vp, _sz, _vp]),
     "dgx_gemm_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
+    "dgx_gemm_f64": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, C.c_double, _vp]),
     "dgx_gemm_set_algo": (_i, [_i]),
     "dgx_bmm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "dgx_conv2d_fwd": (_i, [_vp] * 4 + [_i] * 10 + [_vp]),

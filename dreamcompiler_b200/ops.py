@@ -47,12 +47,26 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, transA: bool = False, transB: bool
          bias: Optional[torch.Tensor] = None, relu: bool = False, beta: float = 0.0,
          f32_mode: int = L.DGX_F32_3XTF32, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """C = beta*C + op(A) @ op(B) (+bias) (ReLU). A, B: 2-D row-major CUDA tensors,
-    possibly with a row pitch (stride(0)) larger than their width."""
+    possibly with a row pitch (stride(0)) larger than their width. float64
+    operands run the f64 kernel (dgx_gemm_f64) with an f64 result and bias."""
     assert A.is_cuda and B.is_cuda and A.dtype == B.dtype and A.dim() == 2 and B.dim() == 2
     assert A.stride(1) == 1 and B.stride(1) == 1, "inner dimension must be contiguous"
     M, K = (A.shape[1], A.shape[0]) if transA else (A.shape[0], A.shape[1])
     Kb, N = (B.shape[1], B.shape[0]) if transB else (B.shape[0], B.shape[1])
     assert K == Kb, f"inner dimensions differ: {K} vs {Kb}"
+    if A.dtype == torch.float64:
+        if out is None:
+            out = torch.empty(M, N, device=A.device, dtype=torch.float64)
+        assert out.dtype == torch.float64 and out.stride(1) == 1 and out.shape == (M, N)
+        epi = L.DGX_EPI_NONE
+        if bias is not None:
+            assert bias.dtype == torch.float64 and bias.is_contiguous() and bias.numel() == N
+            epi = L.DGX_EPI_BIAS_RELU if relu else L.DGX_EPI_BIAS
+        elif relu:
+            epi = L.DGX_EPI_RELU
+        L.call("dgx_gemm_f64", A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K, A.stride(0), B.stride(0),
+               out.stride(0), int(transA), int(transB), _ptr(bias), epi, float(beta), _stream(A))
+        return out
     if out is None:
         out = torch.empty(M, N, device=A.device, dtype=out_dtype or torch.float32)
     assert out.stride(1) == 1 and out.shape == (M, N)

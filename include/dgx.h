@@ -129,6 +129,21 @@ dgx_status dgx_convert(const void* src, dgx_dtype src_type, void* dst, dgx_dtype
 dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb, int ldc,
                     int transA, int transB, dgx_dtype ab_type, dgx_dtype c_type, int f32_mode, const float* bias,
                     int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * C[M,N] = beta*C + op(A)[M,K] . op(B)[K,N] (+bias[N]) (ReLU), all in f64:
+ * every product and sum an f64 fused multiply-add, so results carry the
+ * reference's float64 precision (no tensor-core splitting).
+ *   Operand layouts, pitches, transA/transB and epilogue as dgx_gemm; bias is
+ *   f64 [N]; beta any value (0: C is not read).
+ * Replaces, for the reference's default float64 tensors: dream_gemm_d
+ * (runtime/ops/elementwise.inc:516-638, the CPU branch of tensor_matmul
+ * :1020-1031), the f64 "matmul" backward loops (runtime/ops/autograd.inc:91-125)
+ * and the f64 dream_linear / "linear" backward (elementwise.inc:1432-1521,
+ * autograd.inc:156-211).
+ */
+dgx_status dgx_gemm_f64(const double* A, const double* B, double* C, int M, int N, int K, int lda, int ldb, int ldc,
+                        int transA, int transB, const double* bias, int epilogue, double beta, void* stream);
 size_t dgx_gemm_workspace_size(int M, int N, int K, int transA, int transB, dgx_dtype ab_type, int f32_mode);
 /* bf16 GEMM kernel selection: 0 = single-CTA tiles (128 x 256) only;
  * 1 (default) = 2-SM tiles (256 x 256 over a CTA pair, tcgen05 cta_group::2)
