@@ -37,10 +37,15 @@ SIGNATURES = {
     "dgx_init": (_i, [_i]),
     "dgx_sync_check": (_i, [_vp]),
     "dgx_set_timer_events": (None, [_vp, _vp]),
+    "dgx_stream_create": (_i, [_vp]),
+    "dgx_device_alloc": (_i, [_sz, _vp]),
+    "dgx_device_free": (_i, [_vp]),
+    "dgx_copy": (_i, [_vp, _vp, _sz, _i, _vp]),
     "dgx_fault_inject": (_i, [C.c_longlong, _i]),
     "dgx_fault_calls": (C.c_longlong, []),
     "dgx_wait_probe": (_i, [_i, _vp, C.c_ulonglong, _i, _vp]),
     "dgx_convert": (_i, [_vp, _i, _vp, _i, _sz, _i, _vp]),
+    "dgx_fingerprint": (_i, [_vp, _sz, _vp, _vp]),
     "dgx_gemm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _f, _vp, _sz, _vp]),
     "dgx_gemm_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
     "dgx_gemm_f64": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, C.c_double, _vp]),

@@ -192,6 +192,36 @@ dgx_status dgx_fault_inject(long long at_call, int status) {
 
 long long dgx_fault_calls(void) { return g_fault_calls.load(); }
 
+dgx_status dgx_stream_create(void** stream) {
+  if (!stream) return set_error(DGX_EINVAL, "dgx_stream_create: null pointer");
+  cudaStream_t s = nullptr;
+  const cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return cuda_status(e, "dgx_stream_create");
+  *stream = s;
+  return DGX_OK;
+}
+
+dgx_status dgx_device_alloc(size_t bytes, void** ptr) {
+  if (!ptr) return set_error(DGX_EINVAL, "dgx_device_alloc: null pointer");
+  *ptr = nullptr;
+  const cudaError_t e = cudaMalloc(ptr, bytes ? bytes : 1);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(DGX_ENOMEM, "dgx_device_alloc: %zu bytes: %s", bytes, cudaGetErrorString(e));
+  }
+  return DGX_OK;
+}
+
+dgx_status dgx_device_free(void* ptr) { return cuda_status(cudaFree(ptr), "dgx_device_free"); }
+
+dgx_status dgx_copy(void* dst, const void* src, size_t bytes, int direction, void* stream) {
+  if (bytes == 0) return DGX_OK;
+  if (!dst || !src) return set_error(DGX_EINVAL, "dgx_copy: null pointer");
+  const cudaMemcpyKind kinds[3] = {cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost, cudaMemcpyDeviceToDevice};
+  if (direction < 0 || direction > 2) return set_error(DGX_EINVAL, "dgx_copy: direction %d", direction);
+  return cuda_status(cudaMemcpyAsync(dst, src, bytes, kinds[direction], (cudaStream_t)stream), "dgx_copy");
+}
+
 dgx_status dgx_gemm_set_algo(int algo) {
   if (algo != 0 && algo != 1) return set_error(DGX_EINVAL, "dgx_gemm_set_algo: %d", algo);
   gemm_set_algo(algo);

@@ -73,3 +73,53 @@ extern "C" dgx_status dgx_convert(const void* src, dgx_dtype src_type, void* dst
   convert_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(src, src_type, dst, dst_type, n, accumulate);
   return cuda_status(cudaGetLastError(), "dgx_convert");
 }
+
+// ---------------------------------------------------------------------------
+// Content fingerprint of a device buffer, the same value a host computes
+// over the same bytes (dgx_fingerprint in include/dgx.h). Word i (8 bytes,
+// little endian; a tail of fewer than 8 bytes zero-padded into one last word)
+// contributes splitmix64(w_i + (i + 1) * 0x9E3779B97F4A7C15) and the
+// contributions are summed mod 2^64. splitmix64 is Vigna's published 64-bit
+// finalizer; the sum makes the result independent of reduction order.
+namespace dgx {
+namespace {
+
+__device__ __forceinline__ unsigned long long fp_mix(unsigned long long z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void fingerprint_kernel(const unsigned char* p, size_t bytes, unsigned long long* out) {
+  const size_t words = bytes / 8, tail = bytes % 8;
+  unsigned long long acc = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < words; i += (size_t)gridDim.x * blockDim.x) {
+    unsigned long long w;
+    memcpy(&w, p + i * 8, 8);
+    acc += fp_mix(w + (i + 1) * 0x9E3779B97F4A7C15ull);
+  }
+  if (tail && blockIdx.x == 0 && threadIdx.x == 0) {
+    unsigned long long w = 0;
+    for (size_t b = 0; b < tail; ++b) w |= (unsigned long long)p[words * 8 + b] << (8 * b);
+    acc += fp_mix(w + (words + 1) * 0x9E3779B97F4A7C15ull);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0 && acc) atomicAdd(out, acc);
+}
+
+}  // namespace
+}  // namespace dgx
+
+extern "C" dgx_status dgx_fingerprint(const void* data, size_t bytes, unsigned long long* out, void* stream) {
+  DGX_FAULT_POINT("dgx_fingerprint");
+  if (!out || (bytes && !data)) return set_error(DGX_EINVAL, "dgx_fingerprint: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(out, 0, sizeof(unsigned long long), s);
+  if (e != cudaSuccess) return cuda_status(e, "dgx_fingerprint");
+  if (bytes == 0) return DGX_OK;
+  const size_t words = bytes / 8 + 1;
+  const int blocks = (int)((words + 255) / 256 < (size_t)(4 * num_sms()) ? (words + 255) / 256 : 4 * num_sms());
+  fingerprint_kernel<<<blocks, 256, 0, s>>>(static_cast<const unsigned char*>(data), bytes, out);
+  return cuda_status(cudaGetLastError(), "dgx_fingerprint");
+}

@@ -57,6 +57,17 @@ dgx_status dgx_init(int device);
  * waits in the kernels report into. DGX_ETIMEOUT if any wait ran out. */
 dgx_status dgx_sync_check(void* stream);
 
+/* Device memory, streams and copies for callers that do not include the CUDA
+ * headers (the Dream runtime loads CUDA dynamically and defines its own
+ * names for it, runtime/backend/gpu.inc:1-110). dgx_copy is asynchronous on
+ * `stream`: direction 0 host -> device, 1 device -> host, 2 device -> device
+ * (pageable host memory makes it return after the host side is read or
+ * written, as cudaMemcpyAsync does). */
+dgx_status dgx_stream_create(void** stream);
+dgx_status dgx_device_alloc(size_t bytes, void** ptr);
+dgx_status dgx_device_free(void* ptr);
+dgx_status dgx_copy(void* dst, const void* src, size_t bytes, int direction, void* stream);
+
 /* Failure detection without a device fault.
  *
  * dgx_fault_inject: host-side fault injection. Every entry point that
@@ -107,6 +118,19 @@ void dgx_set_timer_events(void* start, void* stop);
  */
 dgx_status dgx_convert(const void* src, dgx_dtype src_type, void* dst, dgx_dtype dst_type, size_t n, int accumulate,
                        void* stream);
+
+/*
+ * Content fingerprint of `bytes` bytes of device memory into *out (device
+ * memory, 8 bytes): the sum mod 2^64 over 8-byte little-endian words w_i
+ * (a shorter tail zero-padded into one last word) of
+ * splitmix64(w_i + (i + 1) * 0x9E3779B97F4A7C15). A host computes the same
+ * value over the same bytes, so a caller holding a device copy of a host
+ * buffer can tell whether the host buffer still holds those bytes. No
+ * counterpart in the reference: the B200 backend of the Dream runtime uses it
+ * to keep device copies of tensors across ops (the reference re-uploads every
+ * operand on every call, runtime/ops/elementwise.inc:1033-1090).
+ */
+dgx_status dgx_fingerprint(const void* data, size_t bytes, unsigned long long* out, void* stream);
 
 /*
  * C[M,N] = beta*C + op(A)[M,K] . op(B)[K,N] (+bias[N]) (ReLU)

@@ -102,3 +102,16 @@ def test_tp_shard_matches_reference_widths(lib, orc, N, G):
     for g in range(G):
         lib.dgx_tp_shard(N, G, g, C.byref(c0), C.byref(nc))
         assert (c0.value, nc.value) == orc.tp_shard(N, G, g)
+
+
+def test_reference_runtime_with_b200_backend_loads():
+    """The reference runtime built with the B200 backend (refside/build.sh)
+    exports the reference's ops and the backend's op counter."""
+    from dreamcompiler_b200 import refside
+    if not refside.available():
+        pytest.skip("libdream_ref_b200.so needs the reference sources to build")
+    rt = refside.load()
+    for n in ("tensor_matmul", "dream_linear", "dream_linear_relu", "dream_flash_attention", "backward",
+              "dream_tp_matmul_column", "dream_set_precision", "dream_b200_count"):
+        assert hasattr(rt, n)
+    assert rt.dream_b200_count(0) == 0 and rt.dream_b200_count(99) == -1
