@@ -312,6 +312,59 @@ def run_ours(args, rank, world, local_rank):
     return t[0].item(), t[1].item(), bwd_kernel_s, clocks.summary()
 
 
+def run_reference_api_e2e(steps: int):
+    """The same config-2 step through the reference's own operator boundary:
+    the Dream runtime with the B200 backend (refside), f64 `Tensor*` in and
+    out. One step = dream_flash_attention(Q, K, V, 128, 2048, 64) then
+    backward(sum(O * G)) (how a Dream program injects dO = G), every operand
+    a host f64 tensor; the backend uploads Q, K, V, G, converts, runs the
+    kernels and writes O and the three gradients back into the host tensors.
+    Each step changes one element of Q, K, V and G first, so every step
+    uploads its inputs (the device copies fail their fingerprints). Host wall
+    time per step (host work included: the runtime's allocations, the
+    elementwise mul and sum on the host)."""
+    import ctypes as C
+    import numpy as np
+    from dreamcompiler_b200 import refside
+    if not refside.available():
+        return {"unavailable": "libdream_ref_b200.so not built"}
+    R = refside
+    R.load()
+    rng = np.random.default_rng(17)
+    shape = (BH, S * D)
+    ts = [R.tensor(rng.standard_normal(shape)) for _ in range(4)]
+    Q, K, V, G = ts
+    args = [R.scalar(v) for v in (BH, S, D, 64)]
+    views = [R.view(t) for t in ts]
+
+    def step(i):
+        for v in views:
+            v[i % v.size] += 1e-3
+        O = R.call("dream_flash_attention", Q, K, V, *args)
+        prod = R.call("tensor_mul", O, G)
+        loss = R.call("sum", prod)
+        R.call("backward", loss)
+        for t in (loss, prod, O):
+            R.call("tensor_decref", t)
+
+    before = R.counts()
+    step(0)
+    walls = []
+    for i in range(steps):
+        t0 = time.perf_counter()
+        step(i + 1)
+        walls.append(time.perf_counter() - t0)
+    after = R.counts()
+    t = statistics.median(walls)
+    nbytes = BH * S * D * 8
+    return {"value": (FWD_FLOP + BWD_FLOP) / t / 1e12, "unit": "TFLOPS", "ms_per_step": t * 1e3,
+            "steps": steps, "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes,
+            "device_ops": {k: after[k] - before[k] for k in after},
+            "path": "reference Dream runtime (its own struct Tensor, ops and autograd) with the B200 backend: "
+                    "f64 host tensors Q, K, V, G -> dream_flash_attention + backward(sum(O*G)) -> O, dQ, dK, dV "
+                    "as f64 host tensors; host wall time, median over steps"}
+
+
 TP_N = 16384
 
 
@@ -568,6 +621,7 @@ def main():
     elapsed, e2e_s, bwd_kernel_s, clocks = run_ours(args, rank, world, local_rank)
     # the secondary configs (1 GPU) before the TP GEMM: its 16384^3 steps
     # leave the part power-capped for a while
+    ref_api = run_reference_api_e2e(3) if world == 1 and not args.no_secondary else None
     secondary = run_secondary(local_rank) if world == 1 and not args.no_secondary else None
     tp_s, tp_steps, tp_s1 = run_tp_gemm(args, rank, world, local_rank)
     if world > 1:
@@ -608,6 +662,8 @@ def main():
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if ref_api is not None:
+        line["e2e_reference_api"] = ref_api
     if secondary is not None:
         line["other_configs"] = secondary
     print(json.dumps(line))
