@@ -245,8 +245,8 @@ dgx_status dgx_init(int device) {
   return DGX_OK;
 }
 
-dgx_status dgx_sync_check(void* stream) {  DGX_FAULT_POINT("dgx_sync_check");
-
+dgx_status dgx_sync_check(void* stream) {
+  DGX_FAULT_POINT("dgx_sync_check");
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_status(e, "dgx_sync_check");
@@ -275,8 +275,8 @@ size_t dgx_gemm_workspace_size(int M, int N, int K, int transA, int transB, dgx_
 
 dgx_status dgx_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb, int ldc,
                     int transA, int transB, dgx_dtype ab_type, dgx_dtype c_type, int f32_mode, const float* bias,
-                    int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream) {  DGX_FAULT_POINT("dgx_gemm");
-
+                    int epilogue, float beta, void* workspace, size_t workspace_bytes, void* stream) {
+  DGX_FAULT_POINT("dgx_gemm");
   if (M < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm: negative size %dx%dx%d", M, N, K);
   if (M == 0 || N == 0) return DGX_OK;
   if (!C || (K > 0 && (!A || !B))) return set_error(DGX_EINVAL, "dgx_gemm: null operand");
@@ -345,8 +345,8 @@ extern "C" {
 
 dgx_status dgx_gemm_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K, int lda,
                             int ldb, int ldc, long long strideA, long long strideB, long long strideC, int transA,
-                            int transB, dgx_dtype ab_type, dgx_dtype c_type, float beta, void* stream) {  DGX_FAULT_POINT("dgx_gemm_batched");
-
+                            int transB, dgx_dtype ab_type, dgx_dtype c_type, float beta, void* stream) {
+  DGX_FAULT_POINT("dgx_gemm_batched");
   if (batch < 0 || M < 0 || N < 0 || K < 0)
     return set_error(DGX_EINVAL, "dgx_gemm_batched: negative size %d x %dx%dx%d", batch, M, N, K);
   if (batch == 0 || M == 0 || N == 0) return DGX_OK;

@@ -206,8 +206,8 @@ size_t dgx_conv2d_workspace_size(int N, int Cin, int H, int W, int Cout, int KH,
 }
 
 dgx_status dgx_conv2d_fwd(const float* X, const float* Kw, const float* bias, float* Y, int N, int Cin, int H, int W,
-                          int Cout, int KH, int KW, int pad, int stride, dgx_dtype ab_type, void* stream) {  DGX_FAULT_POINT("dgx_conv2d_fwd");
-
+                          int Cout, int KH, int KW, int pad, int stride, dgx_dtype ab_type, void* stream) {
+  DGX_FAULT_POINT("dgx_conv2d_fwd");
   ConvGeom g;
   dgx_status st = make_geom("dgx_conv2d_fwd", N, Cin, H, W, Cout, KH, KW, pad, stride, &g);
   if (st != DGX_OK) return st;
@@ -249,8 +249,8 @@ dgx_status dgx_conv2d_fwd(const float* X, const float* Kw, const float* bias, fl
 
 dgx_status dgx_conv2d_bwd(const float* X, const float* Kw, const float* dY, float* dX, float* dK, int N, int Cin, int H,
                           int W, int Cout, int KH, int KW, int pad, int stride, dgx_dtype ab_type, int accumulate,
-                          void* stream) {  DGX_FAULT_POINT("dgx_conv2d_bwd");
-
+                          void* stream) {
+  DGX_FAULT_POINT("dgx_conv2d_bwd");
   ConvGeom g;
   dgx_status st = make_geom("dgx_conv2d_bwd", N, Cin, H, W, Cout, KH, KW, pad, stride, &g);
   if (st != DGX_OK) return st;

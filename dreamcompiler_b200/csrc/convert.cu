@@ -62,8 +62,8 @@ __global__ void convert_kernel(const void* src, int st, void* dst, int dt, size_
 using namespace dgx;
 
 extern "C" dgx_status dgx_convert(const void* src, dgx_dtype src_type, void* dst, dgx_dtype dst_type, size_t n,
-                                  int accumulate, void* stream) {  DGX_FAULT_POINT("dgx_convert");
-
+                                  int accumulate, void* stream) {
+  DGX_FAULT_POINT("dgx_convert");
   if (n == 0) return DGX_OK;
   if (!src || !dst) return set_error(DGX_EINVAL, "dgx_convert: null pointer");
   if (src_type < DGX_F32 || src_type > DGX_F64 || dst_type < DGX_F32 || dst_type > DGX_F64 || dst_type == DGX_I8)

@@ -61,12 +61,14 @@ inline void flash_dense_layout(FlashBwdArgs& a) {
 inline int flash_spad(int S) { return (S + 127) / 128 * 128; }
 size_t flash_bwd_scratch_bytes(int BH, int S, int D);
 
-bool flash_tc_supported(int D, const void* const* ptrs, int n);
+// Head dims the tensor-core kernels take: D % 8 == 0, D <= 128 forward, D <= 64 backward.
+constexpr int kFlashFwdMaxD = 128, kFlashBwdMaxD = 64;
+bool flash_tc_supported(int D, int max_d, const void* const* ptrs, int n);
 bool make_head_map(CUtensorMap* map, const void* base, int BH, int H, int S, int D, int ld);
 cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s);
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s);
-// SIMT kernels for head dims the tensor-core kernels do not take (D % 8 != 0
-// or D > 64): fp32 math, one thread per query row / key row.
+// SIMT kernels for head dims the tensor-core kernels do not take (D % 8 != 0,
+// or D above the kernel's limit): fp32 math, one thread per query row / key row.
 cudaError_t flash_fwd_simt(const FlashFwdArgs& a, cudaStream_t s);
 cudaError_t flash_bwd_simt(const FlashBwdArgs& a, cudaStream_t s);
 

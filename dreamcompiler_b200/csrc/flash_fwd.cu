@@ -35,9 +35,7 @@ namespace {
 
 constexpr int BLOCK_M = 128;   // rows per Q tile
 constexpr int BLOCK_N = 128;   // keys per K/V tile
-constexpr int DP = 64;         // head dim held in shared memory / TMEM (D <= 64 zero-padded)
-constexpr int KV_STAGES = 3;
-constexpr int TILE_BYTES = BLOCK_M * DP * 2;  // 16 KB for every Q/K/V tile
+constexpr int HALF_BYTES = 128 * 128;  // one 64-column (128-byte) SW128 sub-tile of 128 rows
 constexpr int NUM_THREADS = 384;  // WG0: softmax A, WG1: softmax B, WG2: TMA warp, two MMA warps, 1 idle
 // setmaxnreg split (per thread): 2 x 224 + 56 = 504 <= 3 x 168 (65536 / 384 rounded down to 8).
 constexpr uint32_t REG_SOFTMAX = 224, REG_CTRL = 56;
@@ -45,15 +43,34 @@ constexpr float RESCALE_LOG2 = 8.0f;
 // Exponential column after which a softmax group hands the MUFU turn over.
 constexpr int TURN_AT = 80;
 
-// shared memory map (offsets from a 1024-aligned base)
-constexpr int SM_Q = 0;                               // Q_A, Q_B (two buffers: next item's Q)
-constexpr int SM_K = SM_Q + 4 * TILE_BYTES;           // K stages
-constexpr int SM_V = SM_K + KV_STAGES * TILE_BYTES;   // V stages
-constexpr int SM_BAR = SM_V + KV_STAGES * TILE_BYTES;
-constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
-
-// TMEM columns
-constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + DP, T_P0 = 384, T_P1 = 448;
+// Layout per head-dim class: DP = 64 (D <= 64) or 128 (64 < D <= 128), the
+// head dim held in shared memory and TMEM (columns past D zero-filled).
+//   DP = 64: a Q/K/V tile is one 16 KB SW128 tile; Q for the next item loads
+//     into a second buffer; 3 K/V stages; TMEM S_A, S_B, O_A, O_B, P_A, P_B.
+//   DP = 128: a tile is two 64-column SW128 halves (32 KB); one Q buffer and
+//     2 K/V stages (192 KB in all); TMEM S_A, S_B (128 columns each) and
+//     O_A, O_B (128 each) fill all 512 columns, so P(j) is written over the
+//     first 64 columns of its S buffer, and the MMA warp issues S(j+1) into
+//     that buffer only after PV(j) has read P(j).
+template <int DP_>
+struct FwdCfg {
+  static constexpr int DP = DP_;
+  static constexpr bool ALIAS = DP_ > 64;
+  static constexpr int HALVES = DP_ / 64;
+  static constexpr int TILE_BYTES = BLOCK_M * DP_ * 2;
+  static constexpr int Q_BUFS = ALIAS ? 1 : 2;
+  static constexpr int KV_STAGES = ALIAS ? 2 : 3;
+  // shared memory map (offsets from a 1024-aligned base)
+  static constexpr int SM_Q = 0;                                 // Q_A, Q_B per Q buffer
+  static constexpr int SM_K = SM_Q + Q_BUFS * 2 * TILE_BYTES;    // K stages
+  static constexpr int SM_V = SM_K + KV_STAGES * TILE_BYTES;     // V stages
+  static constexpr int SM_BAR = SM_V + KV_STAGES * TILE_BYTES;
+  static constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+  // TMEM columns
+  static constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + DP_;
+  static constexpr uint32_t T_P0 = ALIAS ? T_S0 : 384, T_P1 = ALIAS ? T_S1 : 448;
+};
+constexpr int MAX_KV_STAGES = 3;
 constexpr uint32_t TMEM_COLS = 512;
 
 __device__ __forceinline__ float ex2(float x) {
@@ -63,7 +80,7 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 struct FwdBars {
-  uint64_t q_full[2], q_empty[2], k_full[KV_STAGES], v_full[KV_STAGES], kv_empty[KV_STAGES];
+  uint64_t q_full[2], q_empty[2], k_full[MAX_KV_STAGES], v_full[MAX_KV_STAGES], kv_empty[MAX_KV_STAGES];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], turn[2];
   uint32_t tmem_slot;
   int abort;
@@ -96,9 +113,15 @@ __device__ __forceinline__ FwdItem fwd_item(const FlashFwdArgs& a, int w) {
   return I;
 }
 
+template <int DP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, FlashFwdArgs args) {
+  using Cfg = FwdCfg<DP>;
+  constexpr int TILE_BYTES = Cfg::TILE_BYTES, KV_STAGES = Cfg::KV_STAGES, Q_BUFS = Cfg::Q_BUFS;
+  constexpr int SM_Q = Cfg::SM_Q, SM_K = Cfg::SM_K, SM_V = Cfg::SM_V, SM_BAR = Cfg::SM_BAR;
+  constexpr uint32_t T_S0 = Cfg::T_S0, T_S1 = Cfg::T_S1, T_O0 = Cfg::T_O0, T_O1 = Cfg::T_O1, T_P0 = Cfg::T_P0,
+                     T_P1 = Cfg::T_P1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + SM_BAR);
@@ -149,26 +172,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmV);
       uint32_t gkv = 0, ic = 0;
       bool ok = true;
+      // A tile is HALVES boxes of 64 columns, one per SW128 half.
+      auto load_tile = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row, const FwdItem& I) {
+#pragma unroll
+        for (int hf = 0; hf < Cfg::HALVES; ++hf) tma_load_4d(dst + hf * HALF_BYTES, map, bar, hf * 64, I.h, row, I.b);
+      };
       for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
         const FwdItem I = fwd_item(args, w);
-        const int qb2 = ic & 1;
-        if (!(ok = mbar_wait(&bars->q_empty[qb2], ((ic >> 1) & 1) ^ 1, wc))) break;
-        mbar_arrive_expect_tx(&bars->q_full[qb2], 2 * TILE_BYTES);
-        uint8_t* sq = smem + SM_Q + qb2 * 2 * TILE_BYTES;
-        tma_load_4d(sq, &tmQ, &bars->q_full[qb2], 0, I.h, I.q0, I.b);
-        tma_load_4d(sq + TILE_BYTES, &tmQ, &bars->q_full[qb2], 0, I.h, I.q0 + BLOCK_M, I.b);
+        const int qb = ic % Q_BUFS;
+        if (!(ok = mbar_wait(&bars->q_empty[qb], ((ic / Q_BUFS) & 1) ^ 1, wc))) break;
+        mbar_arrive_expect_tx(&bars->q_full[qb], 2 * TILE_BYTES);
+        uint8_t* sq = smem + SM_Q + qb * 2 * TILE_BYTES;
+        load_tile(sq, &tmQ, &bars->q_full[qb], I.q0, I);
+        load_tile(sq + TILE_BYTES, &tmQ, &bars->q_full[qb], I.q0 + BLOCK_M, I);
         ++ic;  // counted as issued before any later wait can fail
         for (int j = 0; j < I.nB; ++j, ++gkv) {
           const int s = gkv % KV_STAGES;
           if (!(ok = mbar_wait(&bars->kv_empty[s], ((gkv / KV_STAGES) & 1) ^ 1, wc))) break;
           mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
-          tma_load_4d(smem + SM_K + s * TILE_BYTES, &tmK, &bars->k_full[s], 0, I.h, j * BLOCK_N, I.b);
+          load_tile(smem + SM_K + s * TILE_BYTES, &tmK, &bars->k_full[s], j * BLOCK_N, I);
           mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
-          tma_load_4d(smem + SM_V + s * TILE_BYTES, &tmV, &bars->v_full[s], 0, I.h, j * BLOCK_N, I.b);
+          load_tile(smem + SM_V + s * TILE_BYTES, &tmV, &bars->v_full[s], j * BLOCK_N, I);
         }
       }
       // Teardown: every copy issued must have landed before the CTA leaves.
-      for (uint32_t f = ic > 2 ? ic - 2 : 0; f < ic; ++f) mbar_drain(&bars->q_full[f & 1], (f >> 1) & 1);
+      for (uint32_t f = ic > (uint32_t)Q_BUFS ? ic - Q_BUFS : 0; f < ic; ++f)
+        mbar_drain(&bars->q_full[f % Q_BUFS], (f / Q_BUFS) & 1);
       for (uint32_t f = gkv > KV_STAGES ? gkv - KV_STAGES : 0; f < gkv; ++f) {
         mbar_drain(&bars->k_full[f % KV_STAGES], (f / KV_STAGES) & 1);
         mbar_drain(&bars->v_full[f % KV_STAGES], (f / KV_STAGES) & 1);
@@ -190,31 +219,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t ns = 0, np = 0;  // S and PV tiles issued by this warp
       uint32_t gkv = 0, ic = 0;  // K/V tiles and items walked
       bool ok = true;
-      // Descriptors advance by adding (byte offset >> 4) to the start field.
+      // Descriptors advance by adding (byte offset >> 4) to the start field;
+      // at DP = 128 the contraction over D crosses into the second SW128 half
+      // after four K steps, and V's two 64-column halves are the B operand's
+      // two 128-byte atoms along N (leading byte offset = one half).
       auto issue_s = [&](uint32_t sq, uint32_t kvi) {
         const uint64_t dq = sw128_desc(sq + x * TILE_BYTES, 16, 1024);
         const uint64_t dk = sw128_desc(sk + (kvi % KV_STAGES) * TILE_BYTES, 16, 1024);
 #pragma unroll 1
-        for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(t_sx, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < DP / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (HALF_BYTES >> 4) + (kk & 3) * 2;
+          mma_f16_ss(t_sx, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+        }
         tc_commit(&bars->s_full[x]);
         ++ns;
       };
       auto issue_pv = [&](uint32_t kvi, bool first) {
-        const uint64_t dv = sw128_desc(sv + (kvi % KV_STAGES) * TILE_BYTES, DP * 128, 1024);
+        const uint64_t dv = sw128_desc(sv + (kvi % KV_STAGES) * TILE_BYTES, HALF_BYTES, 1024);
 #pragma unroll 1
         for (int kk = 0; kk < BLOCK_N / 16; ++kk)  // 16 keys = 8 packed bf16 columns per step
           mma_f16_ts(t_ox, t_px + kk * 8, dv + 128 * kk, idesc_o, (!first || kk > 0) ? 1u : 0u);
         tc_commit(&bars->pv_done[x]);
         ++np;
       };
-      // The S buffer is free once the softmax has read the previous S.
-      auto s_ready = [&]() { return ns == 0 || mbar_wait(&bars->s_free[x], (ns - 1) & 1, wc); };
+      // The S buffer is free once the softmax has read the previous S
+      // (DP = 64) or once the previous PV has read the P written over it
+      // (DP = 128).
+      auto s_ready = [&]() {
+        if constexpr (Cfg::ALIAS) return np == 0 || mbar_wait(&bars->pv_done[x], (np - 1) & 1, wc);
+        return ns == 0 || mbar_wait(&bars->s_free[x], (ns - 1) & 1, wc);
+      };
       for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
         const FwdItem I = fwd_item(args, w);
-        const int qb2 = ic & 1;
+        const int qb = ic % Q_BUFS;
         const int n = x ? I.nB : I.nA;
-        const uint32_t sq = smem_u32(smem + SM_Q + qb2 * 2 * TILE_BYTES);
-        if (!(ok = mbar_wait(&bars->q_full[qb2], (ic >> 1) & 1, wc))) break;
+        const uint32_t sq = smem_u32(smem + SM_Q + qb * 2 * TILE_BYTES);
+        if (!(ok = mbar_wait(&bars->q_full[qb], (ic / Q_BUFS) & 1, wc))) break;
         if (n > 0) {
           if (!(ok = mbar_wait(&bars->k_full[gkv % KV_STAGES], (gkv / KV_STAGES) & 1, wc) && s_ready())) break;
           tc_fence_after();
@@ -222,7 +262,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int j = 0; ok && j < n; ++j) {
           const uint32_t kvi = gkv + j;
-          if (j + 1 < n) {
+          const bool more = j + 1 < n;
+          // DP = 64: S(j+1) goes ahead of PV(j), into the other half of the
+          // overlap; DP = 128: after PV(j), which must read P(j) first.
+          if (!Cfg::ALIAS && more) {
             if (!(ok = mbar_wait(&bars->k_full[(kvi + 1) % KV_STAGES], ((kvi + 1) / KV_STAGES) & 1, wc) &&
                        s_ready()))
               break;
@@ -235,6 +278,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           issue_pv(kvi, j == 0);
           tc_commit(&bars->kv_empty[kvi % KV_STAGES]);
+          if (Cfg::ALIAS && more) {
+            if (!(ok = mbar_wait(&bars->k_full[(kvi + 1) % KV_STAGES], ((kvi + 1) / KV_STAGES) & 1, wc) &&
+                       s_ready()))
+              break;
+            tc_fence_after();
+            issue_s(sq, kvi + 1);
+          }
         }
         if (!ok) break;
         // K/V tiles this tile does not see (tile A under causal: the last one)
@@ -245,7 +295,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!(ok = mbar_wait(&bars->k_full[kvi % KV_STAGES], (kvi / KV_STAGES) & 1, wc))) break;
           tc_commit(&bars->kv_empty[kvi % KV_STAGES]);
         }
-        tc_commit(&bars->q_empty[qb2]);  // every S of this item has read Q
+        tc_commit(&bars->q_empty[qb]);  // every S of this item has read Q
         gkv += I.nB;
       }
     }
@@ -369,32 +419,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (n > 0) {
         if (!(ok = mbar_wait(&bars->pv_done[x], (kbase + n - 1) & 1, wc))) break;
         tc_fence_after();
-        uint32_t o[DP];
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.O) +
+                              ((size_t)I.b * args.S + qrow) * args.ldo + (size_t)I.h * args.D;
+        // 64 columns of O at a time (all the rows of the tile load together;
+        // rows past S only skip the stores).
 #pragma unroll
-        for (int c = 0; c < DP; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
-        tmem_ld_wait();
-        tc_fence_before();
-        if (qrow < args.S) {
-          const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-          __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.O) +
-                                ((size_t)I.b * args.S + qrow) * args.ldo + (size_t)I.h * args.D;
-          if (args.D == DP) {
+        for (int c0 = 0; c0 < DP; c0 += 64) {
+          uint32_t o[64];
+          tmem_ld32(t_o + c0, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+          tmem_ld32(t_o + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+          tmem_ld_wait();
+          if (qrow < args.S) {
+            if (c0 + 64 <= args.D) {
 #pragma unroll
-            for (int c = 0; c < DP; c += 8) {
-              uint4 wv;
-              wv.x = pack_bf16x2(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
-              wv.y = pack_bf16x2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
-              wv.z = pack_bf16x2(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
-              wv.w = pack_bf16x2(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow + c) = wv;
+              for (int c = 0; c < 64; c += 8) {
+                uint4 wv;
+                wv.x = pack_bf16x2(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
+                wv.y = pack_bf16x2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
+                wv.z = pack_bf16x2(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
+                wv.w = pack_bf16x2(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
+                *reinterpret_cast<uint4*>(orow + c0 + c) = wv;
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 64; ++c)
+                if (c0 + c < args.D) orow[c0 + c] = __float2bfloat16_rn(__uint_as_float(o[c]) * inv);
             }
-          } else {
-#pragma unroll
-            for (int c = 0; c < DP; ++c)
-              if (c < args.D) orow[c] = __float2bfloat16_rn(__uint_as_float(o[c]) * inv);
           }
-          if (args.lse) args.lse[(size_t)row_base + qrow] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
         }
+        tc_fence_before();
+        if (qrow < args.S && args.lse)
+          args.lse[(size_t)row_base + qrow] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
       }
       kbase += n;
       tbase += x == 0 ? (I.nA - 1) : I.nA;
@@ -426,21 +482,21 @@ bool make_head_map(CUtensorMap* map, const void* base, int BH, int H, int S, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool flash_tc_supported(int D, const void* const* ptrs, int n) {
-  if (D < 8 || D > DP || D % 8) return false;
+bool flash_tc_supported(int D, int max_d, const void* const* ptrs, int n) {
+  if (D < 8 || D > max_d || D % 8) return false;
   for (int i = 0; i < n; ++i)
     if (reinterpret_cast<uintptr_t>(ptrs[i]) & 15) return false;
   return true;
 }
 
-cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s) {
-  CUtensorMap mq{}, mk{}, mv{};
-  if (!make_head_map(&mq, a.Q, a.BH, a.H, a.S, a.D, a.ldq) || !make_head_map(&mk, a.K, a.BH, a.H, a.S, a.D, a.ldk) ||
-      !make_head_map(&mv, a.V, a.BH, a.H, a.S, a.D, a.ldv))
-    return cudaErrorInvalidValue;
+namespace {
+template <int DP>
+cudaError_t launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FlashFwdArgs& a,
+                       cudaStream_t s) {
+  constexpr int smem = FwdCfg<DP>::SMEM_BYTES;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -448,9 +504,20 @@ cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s) {
   const int items = nqb * a.BH;
   {
     TimerScope timer(s);
-    flash_fwd_kernel<<<items < num_sms() ? items : num_sms(), NUM_THREADS, SMEM_BYTES, s>>>(mq, mk, mv, a);
+    flash_fwd_kernel<DP><<<items < num_sms() ? items : num_sms(), NUM_THREADS, smem, s>>>(mq, mk, mv, a);
   }
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s) {
+  CUtensorMap mq{}, mk{}, mv{};
+  if (!make_head_map(&mq, a.Q, a.BH, a.H, a.S, a.D, a.ldq) || !make_head_map(&mk, a.K, a.BH, a.H, a.S, a.D, a.ldk) ||
+      !make_head_map(&mv, a.V, a.BH, a.H, a.S, a.D, a.ldv))
+    return cudaErrorInvalidValue;
+  if (a.D <= 64) return launch_fwd<64>(mq, mk, mv, a, s);
+  if (a.D <= 128) return launch_fwd<128>(mq, mk, mv, a, s);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace dgx

@@ -537,8 +537,8 @@ bool ln_vec_ok(int C, const void* a, const void* b = nullptr, const void* c = nu
 
 extern "C" {
 
-dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd, int R, int C, void* stream) {  DGX_FAULT_POINT("dgx_layernorm_fwd");
-
+dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd, int R, int C, void* stream) {
+  DGX_FAULT_POINT("dgx_layernorm_fwd");
   if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_fwd: R=%d C=%d", R, C);
   if (R == 0) return DGX_OK;
   if (!x || !y16 || !mean || !rstd) return set_error(DGX_EINVAL, "dgx_layernorm_fwd: null pointer");
@@ -550,8 +550,8 @@ dgx_status dgx_layernorm_fwd(const float* x, void* y16, float* mean, float* rstd
 }
 
 dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rstd, const float* dy, float* dx, int R,
-                             int C, int accumulate, void* stream) {  DGX_FAULT_POINT("dgx_layernorm_bwd");
-
+                             int C, int accumulate, void* stream) {
+  DGX_FAULT_POINT("dgx_layernorm_bwd");
   if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_bwd: R=%d C=%d", R, C);
   if (R == 0) return DGX_OK;
   if (!x || !mean || !rstd || !dy || !dx) return set_error(DGX_EINVAL, "dgx_layernorm_bwd: null pointer");
@@ -563,8 +563,8 @@ dgx_status dgx_layernorm_bwd(const float* x, const float* mean, const float* rst
 }
 
 dgx_status dgx_layernorm_bwd_x16(const float* x, const float* mean, const float* rstd, const float* dy, float* dx,
-                                 void* dx16, int R, int C, int accumulate, void* stream) {  DGX_FAULT_POINT("dgx_layernorm_bwd_x16");
-
+                                 void* dx16, int R, int C, int accumulate, void* stream) {
+  DGX_FAULT_POINT("dgx_layernorm_bwd_x16");
   if (R < 0 || C <= 0) return set_error(DGX_EINVAL, "dgx_layernorm_bwd_x16: R=%d C=%d", R, C);
   if (R == 0) return DGX_OK;
   if (!x || !mean || !rstd || !dy || !dx || !dx16) return set_error(DGX_EINVAL, "dgx_layernorm_bwd_x16: null pointer");
@@ -577,8 +577,8 @@ dgx_status dgx_layernorm_bwd_x16(const float* x, const float* mean, const float*
   return cuda_status(cudaGetLastError(), "dgx_layernorm_bwd_x16");
 }
 
-dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream) {  DGX_FAULT_POINT("dgx_gelu_fwd");
-
+dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void* stream) {
+  DGX_FAULT_POINT("dgx_gelu_fwd");
   if (n < 0) return set_error(DGX_EINVAL, "dgx_gelu_fwd: n=%lld", n);
   if (x_type != DGX_F32 && x_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_gelu_fwd: type %d", x_type);
   if (n == 0) return DGX_OK;
@@ -599,8 +599,8 @@ dgx_status dgx_gelu_fwd(const void* x, int x_type, void* y16, long long n, void*
   return cuda_status(cudaGetLastError(), "dgx_gelu_fwd");
 }
 
-dgx_status dgx_gelu_bwd(const void* x, int x_type, const void* dy, int dy_type, void* dx16, long long n, void* stream) {  DGX_FAULT_POINT("dgx_gelu_bwd");
-
+dgx_status dgx_gelu_bwd(const void* x, int x_type, const void* dy, int dy_type, void* dx16, long long n, void* stream) {
+  DGX_FAULT_POINT("dgx_gelu_bwd");
   if (n < 0) return set_error(DGX_EINVAL, "dgx_gelu_bwd: n=%lld", n);
   const bool xt = x_type == DGX_F32 || x_type == DGX_BF16, gt = dy_type == DGX_F32 || dy_type == DGX_BF16;
   if (!xt || !gt) return set_error(DGX_EINVAL, "dgx_gelu_bwd: types %d %d", x_type, dy_type);
@@ -631,8 +631,8 @@ dgx_status dgx_gelu_bwd(const void* x, int x_type, const void* dy, int dy_type, 
 }
 
 dgx_status dgx_embedding_fwd(const int* tok, const float* W, const float* P, float* x, int n, int S, int d, int V,
-                             void* stream) {  DGX_FAULT_POINT("dgx_embedding_fwd");
-
+                             void* stream) {
+  DGX_FAULT_POINT("dgx_embedding_fwd");
   if (n < 0 || d <= 0 || V <= 0 || (P && S <= 0)) return set_error(DGX_EINVAL, "dgx_embedding_fwd: sizes");
   if (n == 0) return DGX_OK;
   if (!tok || !W || !x) return set_error(DGX_EINVAL, "dgx_embedding_fwd: null pointer");
@@ -641,8 +641,8 @@ dgx_status dgx_embedding_fwd(const int* tok, const float* W, const float* P, flo
 }
 
 dgx_status dgx_embedding_bwd(const int* tok, const float* dx, float* dW, float* dP, int n, int S, int d, int V,
-                             void* stream) {  DGX_FAULT_POINT("dgx_embedding_bwd");
-
+                             void* stream) {
+  DGX_FAULT_POINT("dgx_embedding_bwd");
   if (n < 0 || d <= 0 || V <= 0) return set_error(DGX_EINVAL, "dgx_embedding_bwd: sizes");
   if (dP && (S <= 0 || n % S)) return set_error(DGX_EINVAL, "dgx_embedding_bwd: n=%d not a multiple of S=%d", n, S);
   if (n == 0) return DGX_OK;
@@ -654,8 +654,8 @@ dgx_status dgx_embedding_bwd(const int* tok, const float* dx, float* dW, float* 
 }
 
 dgx_status dgx_softmax_nll(const float* logits, int ld, int V, const int* target, int n, float* loss, void* dlogits,
-                           int dlogits_type, void* stream) {  DGX_FAULT_POINT("dgx_softmax_nll");
-
+                           int dlogits_type, void* stream) {
+  DGX_FAULT_POINT("dgx_softmax_nll");
   if (n < 0 || V <= 0 || ld < V) return set_error(DGX_EINVAL, "dgx_softmax_nll: n=%d V=%d ld=%d", n, V, ld);
   if (dlogits && dlogits_type != DGX_F32 && dlogits_type != DGX_BF16)
     return set_error(DGX_EINVAL, "dgx_softmax_nll: dlogits type %d", dlogits_type);
@@ -674,8 +674,8 @@ dgx_status dgx_softmax_nll(const float* logits, int ld, int V, const int* target
 }
 
 dgx_status dgx_adamw(float* param, float* grad, float* m, float* v, long long n, float lr, float b1, float b2,
-                     float eps, float wd, int step, const int* step_dev, void* stream) {  DGX_FAULT_POINT("dgx_adamw");
-
+                     float eps, float wd, int step, const int* step_dev, void* stream) {
+  DGX_FAULT_POINT("dgx_adamw");
   if (n < 0 || (!step_dev && step < 1)) return set_error(DGX_EINVAL, "dgx_adamw: n=%lld step=%d", n, step);
   if (n == 0) return DGX_OK;
   if (!param || !grad || !m || !v) return set_error(DGX_EINVAL, "dgx_adamw: null pointer");
@@ -687,8 +687,8 @@ dgx_status dgx_adamw(float* param, float* grad, float* m, float* v, long long n,
   return cuda_status(cudaGetLastError(), "dgx_adamw");
 }
 
-dgx_status dgx_colsum(const void* dy, int dy_type, float* db, int R, int N, int accumulate, void* stream) {  DGX_FAULT_POINT("dgx_colsum");
-
+dgx_status dgx_colsum(const void* dy, int dy_type, float* db, int R, int N, int accumulate, void* stream) {
+  DGX_FAULT_POINT("dgx_colsum");
   if (R < 0 || N <= 0) return set_error(DGX_EINVAL, "dgx_colsum: R=%d N=%d", R, N);
   if (dy_type != DGX_F32 && dy_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_colsum: type %d", dy_type);
   if (!dy || !db) return set_error(DGX_EINVAL, "dgx_colsum: null pointer");
@@ -719,8 +719,8 @@ dgx_status dgx_colsum(const void* dy, int dy_type, float* db, int R, int N, int 
 }
 
 dgx_status dgx_rows_to_heads(const void* src, int src_type, int ld, int col0, void* dst, int B, int S, int H, int D,
-                             void* stream) {  DGX_FAULT_POINT("dgx_rows_to_heads");
-
+                             void* stream) {
+  DGX_FAULT_POINT("dgx_rows_to_heads");
   if (B < 0 || S < 0 || H <= 0 || D <= 0 || D % 8 || col0 < 0 || col0 % 8 || ld % 8 || col0 + H * D > ld)
     return set_error(DGX_EINVAL, "dgx_rows_to_heads: sizes (D, col0 and ld must be multiples of 8)");
   if (src_type != DGX_F32 && src_type != DGX_BF16) return set_error(DGX_EINVAL, "dgx_rows_to_heads: type");
@@ -739,8 +739,8 @@ dgx_status dgx_rows_to_heads(const void* src, int src_type, int ld, int col0, vo
   return cuda_status(cudaGetLastError(), "dgx_rows_to_heads");
 }
 
-dgx_status dgx_heads_to_rows(const void* src, void* dst, int ld, int col0, int B, int S, int H, int D, void* stream) {  DGX_FAULT_POINT("dgx_heads_to_rows");
-
+dgx_status dgx_heads_to_rows(const void* src, void* dst, int ld, int col0, int B, int S, int H, int D, void* stream) {
+  DGX_FAULT_POINT("dgx_heads_to_rows");
   if (B < 0 || S < 0 || H <= 0 || D <= 0 || D % 8 || col0 < 0 || col0 % 8 || ld % 8 || col0 + H * D > ld)
     return set_error(DGX_EINVAL, "dgx_heads_to_rows: sizes (D, col0 and ld must be multiples of 8)");
   const long long n = (long long)B * S * H * D;

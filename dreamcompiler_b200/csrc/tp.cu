@@ -173,8 +173,8 @@ dgx_status dgx_tp_export(void* C_full, size_t c_bytes, void* handle_out, size_t 
   return DGX_OK;
 }
 
-dgx_status dgx_tp_open(int rank, int world, const void* handles) {  DGX_FAULT_POINT("dgx_tp_open");
-
+dgx_status dgx_tp_open(int rank, int world, const void* handles) {
+  DGX_FAULT_POINT("dgx_tp_open");
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
     return set_error(DGX_EINVAL, "dgx_tp_open: rank %d of world %d (max %d)", rank, world, kMaxRanks);
   if (!handles) return set_error(DGX_EINVAL, "dgx_tp_open: null handles");
@@ -207,8 +207,8 @@ dgx_status dgx_tp_open(int rank, int world, const void* handles) {  DGX_FAULT_PO
 }
 
 dgx_status dgx_tp_gemm_colsplit(const void* A, const void* B_shard, int M, int N, int K, dgx_dtype ab_type,
-                                dgx_dtype c_type, int timeout_ms, void* stream) {  DGX_FAULT_POINT("dgx_tp_gemm_colsplit");
-
+                                dgx_dtype c_type, int timeout_ms, void* stream) {
+  DGX_FAULT_POINT("dgx_tp_gemm_colsplit");
   if (M < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_tp_gemm_colsplit: negative size");
   if (ab_type != DGX_BF16 && ab_type != DGX_F32) return set_error(DGX_EINVAL, "dgx_tp_gemm_colsplit: ab_type");
   if (c_type != DGX_BF16 && c_type != DGX_F32) return set_error(DGX_EINVAL, "dgx_tp_gemm_colsplit: c_type");

@@ -255,16 +255,16 @@ using namespace dgx;
 
 extern "C" {
 
-dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, int K, void* stream) {  DGX_FAULT_POINT("dgx_quantize_rows_i8");
-
+dgx_status dgx_quantize_rows_i8(const float* X, int8_t* Xq, float* sx, int B, int K, void* stream) {
+  DGX_FAULT_POINT("dgx_quantize_rows_i8");
   if (B < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_quantize_rows_i8: negative size");
   if (B == 0) return DGX_OK;
   if (!X || !Xq || !sx) return set_error(DGX_EINVAL, "dgx_quantize_rows_i8: null pointer");
   return cuda_status(quantize_rows(X, Xq, sx, B, K, (cudaStream_t)stream), "dgx_quantize_rows_i8");
 }
 
-dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream) {  DGX_FAULT_POINT("dgx_gemm_i8i32");
-
+dgx_status dgx_gemm_i8i32(const int8_t* Xq, const int8_t* W, int32_t* acc, int B, int N, int K, void* stream) {
+  DGX_FAULT_POINT("dgx_gemm_i8i32");
   if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: negative size");
   if (B == 0 || N == 0) return DGX_OK;
   if (!Xq || !W || !acc) return set_error(DGX_EINVAL, "dgx_gemm_i8i32: null pointer");
@@ -305,8 +305,8 @@ static dgx_status w8_layer(const char* op, const float* X, const int8_t* W, cons
 extern "C" {
 
 dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, const float* bias, float* Y, int B,
-                       int N, int K, int mode, void* stream) {  DGX_FAULT_POINT("dgx_gemm_w8");
-
+                       int N, int K, int mode, void* stream) {
+  DGX_FAULT_POINT("dgx_gemm_w8");
   if (B < 0 || N < 0 || K < 0) return set_error(DGX_EINVAL, "dgx_gemm_w8: negative size");
   if (mode != 0 && mode != 1) return set_error(DGX_EINVAL, "dgx_gemm_w8: mode %d", mode);
   if (B == 0 || N == 0) return DGX_OK;
@@ -316,8 +316,8 @@ dgx_status dgx_gemm_w8(const float* X, const int8_t* W, const float* scale, cons
 }
 
 dgx_status dgx_dense_q(const float* X, const int8_t* W, float scale, const float* scales, const float* bias,
-                       float* Y, int B, int out_dim, int in_dim, int relu, void* stream) {  DGX_FAULT_POINT("dgx_dense_q");
-
+                       float* Y, int B, int out_dim, int in_dim, int relu, void* stream) {
+  DGX_FAULT_POINT("dgx_dense_q");
   if (B < 0 || out_dim < 0 || in_dim < 0) return set_error(DGX_EINVAL, "dgx_dense_q: negative size");
   if (B == 0 || out_dim == 0) return DGX_OK;
   if (!X || !W || !Y) return set_error(DGX_EINVAL, "dgx_dense_q: null pointer");

@@ -70,11 +70,14 @@ def test_reference_test26(dgx, orc, golden):
 
 
 @pytest.mark.parametrize("BH,S,D", [(2, 128, 64), (3, 384, 64), (2, 300, 64), (2, 1000, 64), (1, 1, 64),
-                                    (2, 257, 32), (1, 129, 16), (2, 77, 20), (1, 200, 128), (4, 256, 8)])
+                                    (2, 257, 32), (1, 129, 16), (2, 77, 20), (1, 200, 128), (4, 256, 8),
+                                    (2, 256, 128), (3, 513, 128), (1, 300, 96), (2, 129, 80), (1, 1000, 128),
+                                    (1, 64, 72), (2, 200, 136)])
 @pytest.mark.parametrize("causal", [True, False])
 def test_shapes(dgx, orc, BH, S, D, causal):
-    """Ragged S, tensor-core head dims (8..64, multiple of 8) and the SIMT
-    path (D=20, 128); causal and full attention."""
+    """Ragged S, tensor-core head dims (8..128, multiples of 8; D > 64 takes
+    the two-half tiles with P written over S) and the SIMT path (D=20, 136);
+    causal and full attention."""
     orc.set_seed(1000 + BH * S + D)
     Q, K, V, dO = (orc.randn(BH, S, D) for _ in range(4))
     res = run(dgx, Q, K, V, dO, causal)
