@@ -61,12 +61,17 @@ inline void flash_dense_layout(FlashBwdArgs& a) {
 inline int flash_spad(int S) { return (S + 127) / 128 * 128; }
 size_t flash_bwd_scratch_bytes(int BH, int S, int D);
 
-// Head dims the tensor-core kernels take: D % 8 == 0, D <= 128 forward, D <= 64 backward.
-constexpr int kFlashFwdMaxD = 128, kFlashBwdMaxD = 64;
+// Head dims the tensor-core kernels take: D % 8 == 0, D <= 128. The backward
+// runs one kernel for D <= 64 (dQ reduced through an fp32 accumulator) and two
+// for 64 < D <= 128 (dK/dV per key tile, dQ per query tile).
+constexpr int kFlashFwdMaxD = 128, kFlashBwdMaxD = 128;
 bool flash_tc_supported(int D, int max_d, const void* const* ptrs, int n);
 bool make_head_map(CUtensorMap* map, const void* base, int BH, int H, int S, int D, int ld);
 cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s);
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s);
+cudaError_t flash_bwd128_tc(const FlashBwdArgs& a, cudaStream_t s);
+// The backward's row pre-pass alone: D_i and LSE_i*log2 e into a.rowstat.
+cudaError_t flash_bwd_rowstats(const FlashBwdArgs& a, cudaStream_t s);
 // SIMT kernels for head dims the tensor-core kernels do not take (D % 8 != 0,
 // or D above the kernel's limit): fp32 math, one thread per query row / key row.
 cudaError_t flash_fwd_simt(const FlashFwdArgs& a, cudaStream_t s);

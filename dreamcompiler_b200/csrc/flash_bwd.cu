@@ -564,7 +564,15 @@ size_t flash_bwd_scratch_bytes(int BH, int S, int D) {
   return ((size_t)BH * S * D + 2 * (size_t)BH * flash_spad(S)) * sizeof(float);
 }
 
+cudaError_t flash_bwd_rowstats(const FlashBwdArgs& a, cudaStream_t s) {
+  FlashBwdArgs pa = a;
+  pa.zero_acc = 0;
+  flash_bwd_pre_kernel<<<8 * num_sms(), 256, 0, s>>>(pa);
+  return cudaGetLastError();
+}
+
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
+  if (a.D > DP) return flash_bwd128_tc(a, s);
   CUtensorMap mq{}, mk{}, mv{}, mdo{};
   FlashBwdArgs la = a;
   la.dense3d = a.H == 1 && a.ldq == a.D && a.ldk == a.D && a.ldv == a.D && a.lddo == a.D;

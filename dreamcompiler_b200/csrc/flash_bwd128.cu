@@ -1,0 +1,642 @@
+// FlashAttention backward for head dims 64 < D <= 128 on sm_100a.
+//
+// Replaces the "flash_attention" branch of backward()
+// (runtime/ops/autograd.inc:779-840) for the head sizes the reference's GPU
+// kernel serves up to (dk <= 128, runtime/nn/training.inc:318, :336). At
+// D = 128 one CTA's TMEM cannot hold S^T, dP^T, the dV and dK accumulators
+// and a dQ accumulator at once (512 columns: 128 each for the first four),
+// so the gradients come from two tensor-core kernels with one owner per
+// output element:
+//
+//   flash_bwd128_dkdv_kernel  per 128-key tile, walking the Q tiles that see
+//     it:  S^T = K Q^T, dP^T = V dO^T, P^T and dS^T written back over them
+//     in TMEM as bf16, dV += P^T dO, dK += dS^T Q.
+//   flash_bwd128_dq_kernel    per 128-query tile, walking the key tiles it
+//     sees:  S = Q K^T (two buffers), dP = dO V^T, dS written over its S
+//     buffer, dQ += dS K; dQ leaves as bf16 straight from TMEM.
+//
+// S and dP are computed twice (once per kernel), but nothing is reduced
+// through memory: no fp32 dQ accumulator, no atomics, and the result is the
+// same bits on every run. The row statistics (D_i = dO_i.O_i, LSE_i*log2 e)
+// come from the backward's row pre-pass (flash_bwd.cu).
+//
+// Tiles are 128 rows x 128 columns bf16 held as two 64-column SW128 halves;
+// contractions over D cross into the second half after four K steps, and
+// an MN-major operand's two halves are its two 128-byte atoms along N.
+#include <math.h>
+
+#include "common.h"
+#include "flash.h"
+#include "sm100.cuh"
+
+namespace dgx {
+namespace {
+
+constexpr int BT = 128;                  // rows of every tile (keys or queries)
+constexpr int HALF = 128 * 128;          // one 64-column SW128 half: 128 rows x 128 B
+constexpr int TILE = 2 * HALF;           // 32 KB
+constexpr int NUM_THREADS = 384;         // WG0-1: compute, warp 8: TMA, warp 9: MMA, 2 idle
+// setmaxnreg split (per thread): 2 x 4 warps x 224 + 4 warps x 56 = 168 x 12 warps.
+constexpr uint32_t REG_COMPUTE = 224, REG_CTRL = 56;
+constexpr uint32_t TMEM_COLS = 512;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// d = a . b^T over D = 128 (both K-major, 8 K steps across the two halves)
+__device__ __forceinline__ void mma_kmajor_d128(uint32_t d, uint32_t a_smem, uint32_t b_smem, uint32_t idesc) {
+  const uint64_t da = sw128_desc(a_smem, 16, 1024), db = sw128_desc(b_smem, 16, 1024);
+#pragma unroll 1
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t off = (kk >> 2) * (HALF >> 4) + (kk & 3) * 2;
+    mma_f16_ss(d, da + off, db + off, idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+// d (+)= A(tmem, 128 bf16 columns packed as [64h, 64h+32) for h = 0, 1) .
+// B (smem, 128 rows of the contraction x 128 columns N, MN-major halves)
+__device__ __forceinline__ void mma_tmem_a_d128(uint32_t d, uint32_t a_tmem, uint32_t b_smem, uint32_t idesc,
+                                                bool first) {
+  const uint64_t db = sw128_desc(b_smem, HALF, 1024);
+#pragma unroll 1
+  for (int kk = 0; kk < 8; ++kk)
+    mma_f16_ts(d, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), db + 128 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
+}
+
+__device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int h, int row,
+                                          int b) {
+  tma_load_4d(dst, map, bar, 0, h, row, b);
+  tma_load_4d(dst + HALF, map, bar, 64, h, row, b);
+}
+
+// Store 64 fp32 accumulator columns (times `mul`) of one row as bf16
+// columns [c0, c0 + 64) of `dst` (D columns in all).
+__device__ __forceinline__ void store_row64(__nv_bfloat16* dst, const uint32_t (&v)[64], int c0, int D, float mul) {
+  if (c0 + 64 <= D) {
+#pragma unroll
+    for (int c = 0; c < 64; c += 8) {
+      uint4 w;
+      w.x = pack_bf16x2(__uint_as_float(v[c + 0]) * mul, __uint_as_float(v[c + 1]) * mul);
+      w.y = pack_bf16x2(__uint_as_float(v[c + 2]) * mul, __uint_as_float(v[c + 3]) * mul);
+      w.z = pack_bf16x2(__uint_as_float(v[c + 4]) * mul, __uint_as_float(v[c + 5]) * mul);
+      w.w = pack_bf16x2(__uint_as_float(v[c + 6]) * mul, __uint_as_float(v[c + 7]) * mul);
+      *reinterpret_cast<uint4*>(dst + c0 + c) = w;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 64; ++c)
+      if (c0 + c < D) dst[c0 + c] = __float2bfloat16_rn(__uint_as_float(v[c]) * mul);
+  }
+}
+
+// ============================================================================ dK, dV
+constexpr int KV_SM_K = 0, KV_SM_V = TILE, KV_SM_Q = 2 * TILE, KV_SM_DO = KV_SM_Q + 2 * TILE;  // Q, dO: 2 stages
+constexpr int KV_STAT = 2 * BT * 4;                       // per stage: L2 stats [128], then D stats [128]
+constexpr int KV_SM_STAT = KV_SM_DO + 2 * TILE;
+constexpr int KV_SM_BAR = KV_SM_STAT + 2 * KV_STAT;
+constexpr int KV_SMEM_BYTES = KV_SM_BAR + 256 + 1024;
+constexpr uint32_t KV_T_ST = 0, KV_T_DPT = 128, KV_T_DV = 256, KV_T_DK = 384;
+
+struct KvBars {
+  uint64_t kv_full, kv_empty, q_full[2], q_empty[2];
+  uint64_t s_full, dp_full, p_ready, ds_ready, acc_done;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flash_bwd128_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                             FlashBwdArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  KvBars* bars = reinterpret_cast<KvBars*>(smem + KV_SM_BAR);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WaitCtx wc{&bars->abort, args.err};
+  // Work item w: key tile j = w / BH of head bh = w % BH (key tile 0, which
+  // the most Q tiles see under causal, first); it walks Q tiles i0 .. nq-1.
+  const int nq = (args.S + BT - 1) / BT;
+  const int nitems = nq * args.BH;
+  struct Item {
+    int j, bh, i0, n, b, h;
+  };
+  auto item = [&](int w) {
+    Item it;
+    it.j = w / args.BH;
+    it.bh = w % args.BH;
+    it.b = it.bh / args.H;
+    it.h = it.bh - it.b * args.H;
+    it.i0 = args.causal ? it.j : 0;
+    it.n = nq - it.i0;
+    return it;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    mbar_init(&bars->kv_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->q_full[s], 1);
+      mbar_init(&bars->q_empty[s], 1);
+    }
+    mbar_init(&bars->s_full, 1);
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->p_ready, 8);
+    mbar_init(&bars->ds_ready, 8);
+    mbar_init(&bars->acc_done, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp >= 8) {
+   regs_dec<REG_CTRL>();
+   if (warp == 8) {
+    // ---------------------------------------------------------------- TMA
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      uint32_t gt = 0, ic = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+        const Item I = item(w);
+        if (!(ok = mbar_wait(&bars->kv_empty, (ic & 1) ^ 1, wc))) break;
+        mbar_arrive_expect_tx(&bars->kv_full, 2 * TILE);
+        load_tile(smem + KV_SM_K, &tmK, &bars->kv_full, I.h, I.j * BT, I.b);
+        load_tile(smem + KV_SM_V, &tmV, &bars->kv_full, I.h, I.j * BT, I.b);
+        ++ic;
+        const float* Dstat = args.rowstat + (size_t)I.bh * args.Spad;
+        const float* L2stat = args.rowstat + (size_t)args.BH * args.Spad + (size_t)I.bh * args.Spad;
+        for (int it = 0; it < I.n; ++it, ++gt) {
+          const int s = gt & 1;
+          if (!(ok = mbar_wait(&bars->q_empty[s], ((gt >> 1) & 1) ^ 1, wc))) break;
+          mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE + KV_STAT);
+          const int row = (I.i0 + it) * BT;
+          load_tile(smem + KV_SM_Q + s * TILE, &tmQ, &bars->q_full[s], I.h, row, I.b);
+          load_tile(smem + KV_SM_DO + s * TILE, &tmdO, &bars->q_full[s], I.h, row, I.b);
+          uint8_t* st = smem + KV_SM_STAT + s * KV_STAT;
+          bulk_load(st, L2stat + row, BT * 4, &bars->q_full[s]);
+          bulk_load(st + BT * 4, Dstat + row, BT * 4, &bars->q_full[s]);
+        }
+      }
+      // Teardown: every copy issued must have landed before the CTA leaves.
+      if (ic > 0) mbar_drain(&bars->kv_full, (ic - 1) & 1);
+      for (uint32_t f = gt > 2 ? gt - 2 : 0; f < gt; ++f) mbar_drain(&bars->q_full[f & 1], (f >> 1) & 1);
+    }
+   } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA
+    if (elect_one_lane()) {
+      constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);    // K-major x K-major, N = 128 queries
+      constexpr uint32_t id_acc = make_idesc(1, 0, 1, 128, 128);  // TMEM A x MN-major B, N = D = 128
+      const uint32_t sK = smem_u32(smem + KV_SM_K), sV = smem_u32(smem + KV_SM_V);
+      const uint32_t sQ = smem_u32(smem + KV_SM_Q), sdO = smem_u32(smem + KV_SM_DO);
+      uint32_t gt = 0, ic = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+        const Item I = item(w);
+        if (!(ok = mbar_wait(&bars->kv_full, ic & 1, wc) && mbar_wait(&bars->q_full[gt & 1], (gt >> 1) & 1, wc)))
+          break;
+        tc_fence_after();
+        // S^T and dP^T of the item's first Q tile: their TMEM was last read by
+        // the previous item's final dV / dK MMAs, issued before them.
+        mma_kmajor_d128(tmem + KV_T_ST, sK, sQ + (gt & 1) * TILE, id_s);
+        tc_commit(&bars->s_full);
+        mma_kmajor_d128(tmem + KV_T_DPT, sV, sdO + (gt & 1) * TILE, id_s);
+        tc_commit(&bars->dp_full);
+        for (int it = 0; it < I.n; ++it, ++gt) {
+          const int s = gt & 1, s1 = (gt + 1) & 1;
+          const bool next = it + 1 < I.n;
+          // p_ready of an item's first tile also means the compute warps have
+          // read out the previous item's dV / dK, so dV(0) may overwrite them.
+          if (!(ok = mbar_wait(&bars->p_ready, gt & 1, wc))) break;
+          tc_fence_after();
+          mma_tmem_a_d128(tmem + KV_T_DV, tmem + KV_T_ST, sdO + s * TILE, id_acc, it == 0);  // dV += P^T dO
+          if (next) {
+            if (!(ok = mbar_wait(&bars->q_full[s1], ((gt + 1) >> 1) & 1, wc))) break;
+            tc_fence_after();
+            mma_kmajor_d128(tmem + KV_T_ST, sK, sQ + s1 * TILE, id_s);  // S^T(i+1), after dV(i) read P^T(i)
+            tc_commit(&bars->s_full);
+          }
+          if (!(ok = mbar_wait(&bars->ds_ready, gt & 1, wc))) break;
+          tc_fence_after();
+          mma_tmem_a_d128(tmem + KV_T_DK, tmem + KV_T_DPT, sQ + s * TILE, id_acc, it == 0);  // dK += dS^T Q
+          tc_commit(&bars->q_empty[s]);
+          if (next) {
+            mma_kmajor_d128(tmem + KV_T_DPT, sV, sdO + s1 * TILE, id_s);  // dP^T(i+1), after dK(i) read dS^T(i)
+            tc_commit(&bars->dp_full);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&bars->acc_done);  // dV, dK of this item complete
+        tc_commit(&bars->kv_empty);  // K and V no longer read
+      }
+    }
+    __syncwarp();
+   }
+  } else {
+    regs_inc<REG_COMPUTE>();
+    // ---------------------------------------------------------------- compute (P^T, dS^T)
+    // Warp quarter qw holds keys (TMEM lanes) 32qw..; h picks the query half.
+    const int qw = warp & 3, h = warp >> 2;
+    const int kr = qw * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const float sl2 = args.scale * 1.4426950408889634f;
+    uint32_t gt = 0, ic = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+      const Item I = item(w);
+      const int key = I.j * BT + kr;
+      const bool kvalid = key < args.S;
+      for (int it = 0; it < I.n; ++it, ++gt) {
+        const int qt0 = (I.i0 + it) * BT;
+        const bool diag = args.causal && it == 0;
+        const float* st = reinterpret_cast<const float*>(smem + KV_SM_STAT + (gt & 1) * KV_STAT);
+        const float* Ls = st + 64 * h;
+        const float* Ds = st + BT + 64 * h;
+        if (!(ok = mbar_wait(&bars->s_full, gt & 1, wc))) break;
+        tc_fence_after();
+        float p[64];
+        {
+          uint32_t sv[64];
+          tmem_ld32(tmem + lane_off + KV_T_ST + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(tmem + lane_off + KV_T_ST + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int cc = 0; cc < 64; cc += 32) {
+            float lv[32];
+#pragma unroll
+            for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
+            static_for<0, 32, 2>([&](auto tt) {
+              constexpr int t = decltype(tt)::value;
+              const float2 a = ffma2(__uint_as_float(sv[cc + t]), __uint_as_float(sv[cc + t + 1]), sl2, -lv[t],
+                                     -lv[t + 1]);
+              p[cc + t] = ex2(a.x);
+              p[cc + t + 1] = ex2(a.y);
+            });
+          }
+          if (diag) {  // causal: query q sees keys <= q
+#pragma unroll
+            for (int t = 0; t < 64; ++t) p[t] = (qt0 + 64 * h + t < key) ? 0.f : p[t];
+          }
+          if (!kvalid) {  // key rows past S were loaded as zeros
+#pragma unroll
+            for (int t = 0; t < 64; ++t) p[t] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int cc = 0; cc < 64; cc += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(p[cc + 2 * t], p[cc + 2 * t + 1]);
+          tmem_st16(tmem + lane_off + KV_T_ST + 64 * h + cc / 2, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_ready);
+        if (!(ok = mbar_wait(&bars->dp_full, gt & 1, wc))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 64; cc += 32) {
+          uint32_t dv[32];
+          tmem_ld32(tmem + lane_off + KV_T_DPT + 64 * h + cc, dv);
+          float dd[32];
+#pragma unroll
+          for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&dd[t]) = *reinterpret_cast<const float4*>(Ds + cc + t);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {  // dS = P o (dP - D)
+            const float2 ds = fsubmul2(__uint_as_float(dv[t]), __uint_as_float(dv[t + 1]), dd[t], dd[t + 1], p[cc + t],
+                                       p[cc + t + 1]);
+            pk[t / 2] = pack_bf16x2(ds.x, ds.y);
+          }
+          tmem_st16(tmem + lane_off + KV_T_DPT + 64 * h + cc / 2, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_ready);
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------- item epilogue: dV (h = 0), dK (h = 1)
+      if (!(ok = mbar_wait(&bars->acc_done, ic & 1, wc))) break;
+      tc_fence_after();
+      const uint32_t col = h ? KV_T_DK : KV_T_DV;
+      const float mul = h ? args.scale : 1.f;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) +
+                           ((size_t)I.b * args.S + key) * (h ? args.lddk : args.lddv) + (size_t)I.h * args.D;
+#pragma unroll
+      for (int c0 = 0; c0 < 128; c0 += 64) {
+        uint32_t v[64];
+        tmem_ld32(tmem + lane_off + col + c0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tmem + lane_off + col + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld_wait();
+        if (kvalid) store_row64(dst, v, c0, args.D, mul);
+      }
+      tc_fence_before();  // the next item's first dV / dK MMAs follow this warp's next p_ready
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ============================================================================ dQ
+constexpr int DQ_SM_Q = 0, DQ_SM_DO = TILE, DQ_SM_K = 2 * TILE, DQ_SM_V = DQ_SM_K + 2 * TILE;  // K, V: 2 stages
+constexpr int DQ_SM_BAR = DQ_SM_V + 2 * TILE;
+constexpr int DQ_SMEM_BYTES = DQ_SM_BAR + 256 + 1024;
+constexpr uint32_t DQ_T_S0 = 0, DQ_T_DP = 128, DQ_T_DQ = 256, DQ_T_S1 = 384;
+
+struct DqBars {
+  uint64_t q_full, q_empty, k_full[2], v_full[2], kv_empty[2];
+  uint64_t s_full[2], dp_full, dp_free, ds_ready, dq_done, dq_free;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flash_bwd128_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                           FlashBwdArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DqBars* bars = reinterpret_cast<DqBars*>(smem + DQ_SM_BAR);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WaitCtx wc{&bars->abort, args.err};
+  // Work item w: query tile i of head bh (causal: the last query tiles, which
+  // see the most key tiles, first); it walks key tiles 0 .. n-1.
+  const int nq = (args.S + BT - 1) / BT;
+  const int nitems = nq * args.BH;
+  struct Item {
+    int i, bh, n, b, h;
+  };
+  auto item = [&](int w) {
+    Item it;
+    it.i = args.causal ? nq - 1 - w / args.BH : w / args.BH;
+    it.bh = w % args.BH;
+    it.b = it.bh / args.H;
+    it.h = it.bh - it.b * args.H;
+    it.n = args.causal ? it.i + 1 : nq;
+    return it;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->s_full[s], 1);
+    }
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->dp_free, 8);
+    mbar_init(&bars->ds_ready, 8);
+    mbar_init(&bars->dq_done, 1);
+    mbar_init(&bars->dq_free, 8);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp >= 8) {
+   regs_dec<REG_CTRL>();
+   if (warp == 8) {
+    // ---------------------------------------------------------------- TMA
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      uint32_t g = 0, ic = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+        const Item I = item(w);
+        if (!(ok = mbar_wait(&bars->q_empty, (ic & 1) ^ 1, wc))) break;
+        mbar_arrive_expect_tx(&bars->q_full, 2 * TILE);
+        load_tile(smem + DQ_SM_Q, &tmQ, &bars->q_full, I.h, I.i * BT, I.b);
+        load_tile(smem + DQ_SM_DO, &tmdO, &bars->q_full, I.h, I.i * BT, I.b);
+        ++ic;
+        for (int j = 0; j < I.n; ++j, ++g) {
+          const int s = g & 1;
+          if (!(ok = mbar_wait(&bars->kv_empty[s], ((g >> 1) & 1) ^ 1, wc))) break;
+          mbar_arrive_expect_tx(&bars->k_full[s], TILE);
+          load_tile(smem + DQ_SM_K + s * TILE, &tmK, &bars->k_full[s], I.h, j * BT, I.b);
+          mbar_arrive_expect_tx(&bars->v_full[s], TILE);
+          load_tile(smem + DQ_SM_V + s * TILE, &tmV, &bars->v_full[s], I.h, j * BT, I.b);
+        }
+      }
+      if (ic > 0) mbar_drain(&bars->q_full, (ic - 1) & 1);
+      for (uint32_t f = g > 2 ? g - 2 : 0; f < g; ++f) {
+        mbar_drain(&bars->k_full[f & 1], (f >> 1) & 1);
+        mbar_drain(&bars->v_full[f & 1], (f >> 1) & 1);
+      }
+    }
+   } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA
+    if (elect_one_lane()) {
+      constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);   // Q.K^T and dO.V^T: K-major, N = 128 keys
+      constexpr uint32_t id_dq = make_idesc(1, 0, 1, 128, 128);  // dS (TMEM) . K (MN-major), N = D = 128
+      const uint32_t sQ = smem_u32(smem + DQ_SM_Q), sdO = smem_u32(smem + DQ_SM_DO);
+      const uint32_t sK = smem_u32(smem + DQ_SM_K), sV = smem_u32(smem + DQ_SM_V);
+      auto t_s = [&](uint32_t g) { return tmem + ((g & 1) ? DQ_T_S1 : DQ_T_S0); };
+      uint32_t g = 0, ic = 0;
+      bool ok = true;
+      // S(g) into buffer g & 1, dP(g) into the one dP buffer once the compute
+      // warps have read dP(g-1); S(g+2) reuses S(g)'s buffer after dQ(g)
+      // (issued before it) has read the dS written there.
+      auto issue_s = [&](uint32_t gg) {
+        mma_kmajor_d128(t_s(gg), sQ, sK + (gg & 1) * TILE, id_s);
+        tc_commit(&bars->s_full[gg & 1]);
+      };
+      auto issue_dp = [&](uint32_t gg) {
+        if (gg > 0 && !mbar_wait(&bars->dp_free, (gg - 1) & 1, wc)) return false;
+        if (!mbar_wait(&bars->v_full[gg & 1], (gg >> 1) & 1, wc)) return false;
+        tc_fence_after();
+        mma_kmajor_d128(tmem + DQ_T_DP, sdO, sV + (gg & 1) * TILE, id_s);
+        tc_commit(&bars->dp_full);
+        return true;
+      };
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+        const Item I = item(w);
+        const uint32_t g0 = g;
+        if (!(ok = mbar_wait(&bars->q_full, ic & 1, wc) && mbar_wait(&bars->k_full[g0 & 1], (g0 >> 1) & 1, wc)))
+          break;
+        tc_fence_after();
+        issue_s(g0);
+        if (!(ok = issue_dp(g0))) break;
+        if (I.n > 1) {
+          if (!(ok = mbar_wait(&bars->k_full[(g0 + 1) & 1], ((g0 + 1) >> 1) & 1, wc))) break;
+          tc_fence_after();
+          issue_s(g0 + 1);
+        }
+        // The previous item's dQ must have been read out before dQ(0) overwrites it.
+        if (ic > 0 && !(ok = mbar_wait(&bars->dq_free, (ic - 1) & 1, wc))) break;
+        for (int j = 0; ok && j < I.n; ++j, ++g) {
+          if (!(ok = mbar_wait(&bars->ds_ready, g & 1, wc))) break;
+          tc_fence_after();
+          mma_tmem_a_d128(tmem + DQ_T_DQ, t_s(g), sK + (g & 1) * TILE, id_dq, j == 0);  // dQ += dS K
+          tc_commit(&bars->kv_empty[g & 1]);
+          if (j + 1 < I.n && !(ok = issue_dp(g + 1))) break;
+          if (j + 2 < I.n) {
+            if (!(ok = mbar_wait(&bars->k_full[g & 1], ((g + 2) >> 1) & 1, wc))) break;
+            tc_fence_after();
+            issue_s(g + 2);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&bars->dq_done);
+        tc_commit(&bars->q_empty);
+      }
+    }
+    __syncwarp();
+   }
+  } else {
+    regs_inc<REG_COMPUTE>();
+    // ---------------------------------------------------------------- compute (P, dS), epilogue dQ
+    // Warp quarter qw holds queries (TMEM lanes) 32qw..; h picks the key half.
+    const int qw = warp & 3, h = warp >> 2;
+    const int qr = qw * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const float sl2 = args.scale * 1.4426950408889634f;
+    uint32_t g = 0, ic = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+      const Item I = item(w);
+      const int query = I.i * BT + qr;
+      // this row's statistics (rows past S: L2 = +inf, so P = 0)
+      const float l2 = args.rowstat[(size_t)args.BH * args.Spad + (size_t)I.bh * args.Spad + query];
+      const float drow = args.rowstat[(size_t)I.bh * args.Spad + query];
+      for (int j = 0; j < I.n; ++j, ++g) {
+        const int k0 = j * BT + 64 * h;  // first key of this warp's columns
+        const uint32_t ts = tmem + lane_off + ((g & 1) ? DQ_T_S1 : DQ_T_S0) + 64 * h;
+        if (!(ok = mbar_wait(&bars->s_full[g & 1], (g >> 1) & 1, wc))) break;
+        tc_fence_after();
+        float p[64];
+        {
+          uint32_t sv[64];
+          tmem_ld32(ts, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_ld_wait();
+          static_for<0, 64, 2>([&](auto tt) {
+            constexpr int t = decltype(tt)::value;
+            const float2 a = ffma2(__uint_as_float(sv[t]), __uint_as_float(sv[t + 1]), sl2, -l2);
+            p[t] = ex2(a.x);
+            p[t + 1] = ex2(a.y);
+          });
+          // causal: keys <= query; and key rows past S (loaded as zeros) drop out
+          const int last = args.causal ? min(query, args.S - 1) : args.S - 1;
+          if (k0 + 63 > last) {
+#pragma unroll
+            for (int t = 0; t < 64; ++t) p[t] = (k0 + t <= last) ? p[t] : 0.f;
+          }
+        }
+        if (!(ok = mbar_wait(&bars->dp_full, g & 1, wc))) break;
+        tc_fence_after();
+        uint32_t dv[64];
+        tmem_ld32(tmem + lane_off + DQ_T_DP + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
+        tmem_ld32(tmem + lane_off + DQ_T_DP + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->dp_free);  // the MMA warp may compute dP(g+1)
+#pragma unroll
+        for (int cc = 0; cc < 64; cc += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {  // dS = P o (dP - D)
+            const float2 ds = fsubmul2(__uint_as_float(dv[cc + t]), __uint_as_float(dv[cc + t + 1]), drow, drow,
+                                       p[cc + t], p[cc + t + 1]);
+            pk[t / 2] = pack_bf16x2(ds.x, ds.y);
+          }
+          tmem_st16(ts + cc / 2, pk);  // dS over the first half of this warp's S columns
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_ready);
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------- item epilogue: dQ columns [64h, 64h+64)
+      if (!(ok = mbar_wait(&bars->dq_done, ic & 1, wc))) break;
+      tc_fence_after();
+      uint32_t v[64];
+      tmem_ld32(tmem + lane_off + DQ_T_DQ + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(tmem + lane_off + DQ_T_DQ + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->dq_free);
+      if (query < args.S) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.dQ) +
+                             ((size_t)I.b * args.S + query) * args.lddq + (size_t)I.h * args.D;
+        store_row64(dst, v, 64 * h, args.D, args.scale);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+// Row pre-pass (flash_bwd.cu) then the two kernels, in order on `s`.
+cudaError_t flash_bwd128_tc(const FlashBwdArgs& a, cudaStream_t s) {
+  CUtensorMap mq{}, mk{}, mv{}, mdo{};
+  if (!make_head_map(&mq, a.Q, a.BH, a.H, a.S, a.D, a.ldq) || !make_head_map(&mk, a.K, a.BH, a.H, a.S, a.D, a.ldk) ||
+      !make_head_map(&mv, a.V, a.BH, a.H, a.S, a.D, a.ldv) ||
+      !make_head_map(&mdo, a.dO, a.BH, a.H, a.S, a.D, a.lddo))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(flash_bwd128_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         KV_SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(flash_bwd128_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  cudaError_t e = flash_bwd_rowstats(a, s);
+  if (e != cudaSuccess) return e;
+  const int sms = num_sms();
+  const int items = ((a.S + BT - 1) / BT) * a.BH;
+  const int grid = items < sms ? items : sms;
+  {
+    TimerScope timer(s);
+    flash_bwd128_dkdv_kernel<<<grid, NUM_THREADS, KV_SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  flash_bwd128_dq_kernel<<<grid, NUM_THREADS, DQ_SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+  return cudaGetLastError();
+}
+
+}  // namespace dgx
