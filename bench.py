@@ -517,7 +517,7 @@ def run_secondary(local_rank):
     t = timed(fa128_step, 10)
     fl = 14.0 * BH * Sd * Sd * Dd / 2
     res["fa_d128_fwd_bwd"] = {"ms_per_step": t * 1e3, "tflops": fl / t / 1e12, "clocks": dict(last_clk),
-                              "shape": f"B={B} H={H} S={Sd} D={Dd} causal",
+                              "shape": f"BH={BH} (8 x 16) S={Sd} D={Dd} causal",
                               "flop": "(4 + 10) * BH * S^2 * D / 2 (algorithmic; the backward issues 14)"}
     del fa_sets, Od, Ld, gq, gk, gv, wsd
     torch.cuda.empty_cache()

@@ -10,11 +10,6 @@ two launches of each kernel).
     python -m dreamcompiler_b200.profile_case gpt                     # one config-3 training step
     python -m dreamcompiler_b200.profile_case linear                  # GPT MLP-up: 16384x1536x384 + bias
     python -m dreamcompiler_b200.profile_case gemm_f64 --n 4096       # f64 DFMA GEMM
-    python -m dreamcompiler_b200.profile_case stream --n 16           # cold reads of n MiB (dgx_fingerprint)
-
-`stream` also prints the CUDA-event time per cold read of an n MiB buffer
-(16 buffers in rotation, 256 MiB > L2), the floor any kernel streaming that
-many bytes from HBM meets on this part.
 """
 from __future__ import annotations
 
@@ -26,7 +21,7 @@ def main() -> None:
     import dreamcompiler_b200 as dgx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["flash", "gemm", "w8", "gemm_f32", "conv", "gpt", "linear", "gemm_f64", "stream"])
+    ap.add_argument("kind", choices=["flash", "gemm", "w8", "gemm_f32", "conv", "gpt", "linear", "gemm_f64"])
     ap.add_argument("--bh", type=int, default=16)
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--dim", type=int, default=64)
@@ -72,23 +67,6 @@ def main() -> None:
         A, B = (torch.randn(a.n, a.n, device="cuda", generator=g, dtype=torch.float64) for _ in range(2))
         for _ in range(a.reps):
             dgx.gemm(A, B)
-    elif a.kind == "stream":
-        from dreamcompiler_b200 import _lib
-        nbytes = a.n << 20
-        bufs = [torch.empty(nbytes, device="cuda", dtype=torch.uint8) for _ in range(16)]
-        out = torch.empty(1, device="cuda", dtype=torch.int64)
-        s = torch.cuda.current_stream().cuda_stream
-        lib = _lib.load()
-        for i in range(32):
-            _lib.check(lib.dgx_fingerprint(bufs[i % 16].data_ptr(), nbytes, out.data_ptr(), s), "dgx_fingerprint")
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(160):
-            _lib.check(lib.dgx_fingerprint(bufs[i % 16].data_ptr(), nbytes, out.data_ptr(), s), "dgx_fingerprint")
-        e1.record()
-        torch.cuda.synchronize()
-        t = e0.elapsed_time(e1) / 160 * 1e-3
-        print(f"cold read of {a.n} MiB: {t * 1e6:.2f} us per call, {nbytes / t / 1e9:.0f} GB/s")
     elif a.kind == "gpt":
         from dreamcompiler_b200.gpt import GPT, GPTConfig
         cfg = GPTConfig()
