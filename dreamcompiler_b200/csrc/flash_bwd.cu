@@ -38,9 +38,14 @@ constexpr int BQ = 128;   // queries per step
 constexpr int DP = 64;
 constexpr int Q_STAGES = 2;
 constexpr int TILE = 128 * DP * 2;  // 16 KB
-constexpr int NUM_THREADS = 512;    // WG0-1 compute, WG2 dQ drain, WG3: TMA warp, MMA warp, 2 idle
-// setmaxnreg split (per thread): 2 x 184 + 96 + 40 = 504 <= 512 = 65536 / 128.
-constexpr uint32_t REG_COMPUTE = 184, REG_DRAIN = 96, REG_CTRL = 40;
+// Warps 0-15 compute (four groups of four, one per 32 queries of the Q tile),
+// 16-19 dQ drain, 20 TMA, 21 MMA, 22-23 idle: four compute warps per SM
+// sub-partition, so one warp's TMEM loads and exponentials hide behind the
+// others'.
+constexpr int NUM_THREADS = 768;
+constexpr int W_DRAIN = 16, W_TMA = 20, W_MMA = 21;
+// setmaxnreg split (per thread): 16 x 88 + 4 x 72 + 4 x 56 = 24 x 80 (the launch allocation).
+constexpr uint32_t REG_COMPUTE = 88, REG_DRAIN = 72, REG_CTRL = 56;
 
 constexpr int SM_K = 0, SM_V = 2 * TILE, SM_Q = 4 * TILE, SM_DO = SM_Q + Q_STAGES * TILE;  // K, V: 2 buffers
 constexpr int SM_DS = SM_DO + Q_STAGES * TILE;  // 128 queries x 128 keys bf16, MN-major (2 x 16 KB)
@@ -110,8 +115,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->p_ready, 8);
-    mbar_init(&bars->ds_ready, 8);
+    mbar_init(&bars->p_ready, 16);
+    mbar_init(&bars->ds_ready, 16);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->dq_full[b], 1);
       mbar_init(&bars->dq_empty[b], 4);
@@ -120,7 +125,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     bars->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 13) {
+  if (warp == W_MMA) {
     tmem_alloc(&bars->tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -136,9 +141,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   // Each role's setmaxnreg sits inside its branch so that it dominates (and
   // sets the register limit for) exactly that role's code.
-  if (warp >= 12) {
+  if (warp >= W_TMA) {
    regs_dec<REG_CTRL>();
-   if (warp == 12) {
+   if (warp == W_TMA) {
     // ---------------------------------------------------------------- TMA
     if (elect_one_lane()) {
       tma_prefetch_desc(&tmQ);
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (uint32_t f = kv_filled > 2 ? kv_filled - 2 : 0; f < kv_filled; ++f) mbar_drain(&bars->kv_full[f & 1], (f >> 1) & 1);
       for (int f = max(0, gt - Q_STAGES); f < gt; ++f) mbar_drain(&bars->q_full[f % Q_STAGES], (f / Q_STAGES) & 1);
     }
-  } else if (warp == 13) {
+  } else if (warp == W_MMA) {
     // ---------------------------------------------------------------- MMA
     if (elect_one_lane()) {
       constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);   // K-major x K-major, N = 128 queries
@@ -200,7 +205,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint64_t db = sw128_desc(b, DP * 128, 1024);
 #pragma unroll 1
         for (int kk = 0; kk < BQ / 16; ++kk)
-          mma_f16_ts(d, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), db + 128 * kk, id_acc, (!first || kk > 0) ? 1u : 0u);
+          mma_f16_ts(d, a_tmem + 32 * (kk >> 1) + 8 * (kk & 1), db + 128 * kk, id_acc, (!first || kk > 0) ? 1u : 0u);
       };
       int gt = 0, ic = 0;
       bool ok = true;
@@ -260,13 +265,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
    }
-  } else if (warp >= 8) {
+  } else if (warp >= W_DRAIN) {
     regs_dec<REG_DRAIN>();
     // ---------------------------------------------------------------- dQ drain
     const int qw = warp & 3;
     const int row = qw * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
-    const bool issuer = warp == 8 && lane == 0;
+    const bool issuer = warp == W_DRAIN && lane == 0;
     uint8_t* stage = smem + SM_DQ;
     if (issuer) tma_prefetch_desc(&tmdQacc);
     int gt = 0;
@@ -276,24 +281,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int it = 0; it < I.n; ++it, ++gt) {
         const int b = gt & 1;
         if (!(ok = mbar_wait(&bars->dq_full[b], (gt >> 1) & 1, wc))) break;
-        tc_fence_after();
-        uint32_t v[DP];
-        tmem_ld32(tmem + lane_off + T_DQ + 64 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld32(tmem + lane_off + T_DQ + 64 * b + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->dq_empty[b]);
         // The previous tile's bulk reduce must have read the staging tile.
         if (issuer) bulk_wait_read0();
         named_bar_sync(1, 128);
+        tc_fence_after();
         // Row `row`, columns [32c, 32c+32) -> box c; 16-byte unit u at u ^ (row & 7).
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_off + T_DQ + 64 * b + 32 * c, v);
+          tmem_ld_wait();
 #pragma unroll
           for (int u = 0; u < 8; ++u)
             *reinterpret_cast<uint4*>(stage + c * DQ_BOX + row * 128 + ((u ^ (row & 7)) << 4)) =
-                make_uint4(v[32 * c + 4 * u], v[32 * c + 4 * u + 1], v[32 * c + 4 * u + 2], v[32 * c + 4 * u + 3]);
+                make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->dq_empty[b]);
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (issuer) {
@@ -308,11 +313,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     regs_inc<REG_COMPUTE>();
     // ---------------------------------------------------------------- compute (P, dS)
-    const int qw = warp & 3, h = warp >> 2;
+    // Warp quarter qw holds keys (TMEM lanes) 32qw..; group g the queries
+    // [32g, 32g+32) of the Q tile. Each group writes its packed bf16 P^T and
+    // dS^T (16 columns) over the first half of the 32 columns it read.
+    const int qw = warp & 3, g = warp >> 2;
     const int kr = qw * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const float sl2 = args.scale * 1.4426950408889634f;
-    uint8_t* ds_tile = smem + SM_DS + h * TILE;  // queries [64h, 64h+64)
+    uint8_t* ds_tile = smem + SM_DS + (g >> 1) * TILE;  // queries [64(g/2), 64(g/2)+64)
+    const int unit0 = 4 * (g & 1);                      // this group's 16-byte units in a 128-byte row
     int gt = 0, ic = 0;
     bool ok = true;
     for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
@@ -320,61 +329,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int key = I.j * BKV + kr;
       const bool kvalid = key < args.S;
       for (int it = 0; it < I.n; ++it, ++gt) {
-        const int qt0 = (I.i0 + it) * BQ;
-        // Causal mask only on the diagonal tile; rows past S carry L2 = +inf
-        // (P = 0) in the padded statistics, so they need no test here.
-        const bool diag = args.causal && qt0 < I.j * BKV + BKV - 1;
+        const int q0 = (I.i0 + it) * BQ + 32 * g;  // first query of this group
+        // Causal mask only where a query of the group precedes this key;
+        // rows past S carry L2 = +inf (P = 0) in the padded statistics.
+        const bool diag = args.causal && q0 < I.j * BKV + BKV - 1;
         const float* st = reinterpret_cast<const float*>(smem + SM_STAT + (gt % Q_STAGES) * STAT_BYTES);
-        const float* Ls = st + 64 * h;
-        const float* Ds = st + BQ + 64 * h;
+        const float* Ls = st + 32 * g;
+        const float* Ds = st + BQ + 32 * g;
         if (!(ok = mbar_wait(&bars->s_full, gt & 1, wc))) break;
         tc_fence_after();
-        // Both 32-column loads in flight before one wait.
-        float p[64];
-        {
-          uint32_t sv[64];
-          tmem_ld32(tmem + lane_off + T_ST + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-          tmem_ld32(tmem + lane_off + T_ST + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        float p[32];
+#pragma unroll
+        for (int cc = 0; cc < 32; cc += 16) {
+          uint32_t sv[16];
+          tmem_ld16(tmem + lane_off + T_ST + 32 * g + cc, sv);
+          float lv[16];
+#pragma unroll
+          for (int t = 0; t < 16; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
           tmem_ld_wait();
-          if (!diag) {
-            // Off the diagonal every query of the tile sees this key: no mask.
-#pragma unroll
-            for (int cc = 0; cc < 64; cc += 32) {
-              float lv[32];
-#pragma unroll
-              for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
-              static_for<0, 32, 2>([&](auto tt) {  // column pairs: one packed fp32 FMA per two scores
-                constexpr int t = decltype(tt)::value;
-                const float2 a = ffma2(__uint_as_float(sv[cc + t]), __uint_as_float(sv[cc + t + 1]), sl2, -lv[t],
-                                       -lv[t + 1]);
-                p[cc + t] = ex2(a.x);
-                p[cc + t + 1] = ex2(a.y);
-              });
-            }
-          } else {
-#pragma unroll
-            for (int cc = 0; cc < 64; cc += 32) {
-              float lv[32];
-#pragma unroll
-              for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&lv[t]) = *reinterpret_cast<const float4*>(Ls + cc + t);
-              static_for<0, 32, 1>([&](auto tt) {
-                constexpr int t = decltype(tt)::value;
-                const float e = ex2(fmaf(__uint_as_float(sv[cc + t]), sl2, -lv[t]));
-                p[cc + t] = qt0 + 64 * h + cc + t < key ? 0.f : e;
-              });
-            }
-          }
-          if (!kvalid) {
-#pragma unroll
-            for (int t = 0; t < 64; ++t) p[t] = 0.f;
-          }
+          static_for<0, 16, 2>([&](auto tt) {  // column pairs: one packed fp32 FMA per two scores
+            constexpr int t = decltype(tt)::value;
+            const float2 a = ffma2(__uint_as_float(sv[t]), __uint_as_float(sv[t + 1]), sl2, -lv[t], -lv[t + 1]);
+            p[cc + t] = ex2(a.x);
+            p[cc + t + 1] = ex2(a.y);
+          });
         }
+        if (diag) {
 #pragma unroll
-        for (int cc = 0; cc < 64; cc += 32) {
+          for (int t = 0; t < 32; ++t) p[t] = q0 + t < key ? 0.f : p[t];
+        }
+        if (!kvalid) {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) p[t] = 0.f;
+        }
+        {
           uint32_t pk[16];
 #pragma unroll
-          for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(p[cc + 2 * t], p[cc + 2 * t + 1]);
-          tmem_st16(tmem + lane_off + T_ST + 64 * h + cc / 2, pk);
+          for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(p[2 * t], p[2 * t + 1]);
+          tmem_st16(tmem + lane_off + T_ST + 32 * g, pk);
         }
         tmem_st_wait();
         tc_fence_before();
@@ -382,30 +374,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&bars->p_ready);
         if (!(ok = mbar_wait(&bars->dp_full, gt & 1, wc))) break;
         tc_fence_after();
+        uint32_t pk[16];
 #pragma unroll
-        for (int cc = 0; cc < 64; cc += 32) {
-          uint32_t dv[32];
-          tmem_ld32(tmem + lane_off + T_DPT + 64 * h + cc, dv);
-          float dd[32];
+        for (int cc = 0; cc < 32; cc += 16) {
+          uint32_t dv[16];
+          tmem_ld16(tmem + lane_off + T_DPT + 32 * g + cc, dv);
+          float dd[16];
 #pragma unroll
-          for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(&dd[t]) = *reinterpret_cast<const float4*>(Ds + cc + t);
+          for (int t = 0; t < 16; t += 4) *reinterpret_cast<float4*>(&dd[t]) = *reinterpret_cast<const float4*>(Ds + cc + t);
           tmem_ld_wait();
-          uint32_t pk[16];
 #pragma unroll
-          for (int t = 0; t < 32; t += 2) {  // dS = P o (dP - D), two columns per packed op
+          for (int t = 0; t < 16; t += 2) {  // dS = P o (dP - D), two columns per packed op
             const float2 ds = fsubmul2(__uint_as_float(dv[t]), __uint_as_float(dv[t + 1]), dd[t], dd[t + 1], p[cc + t],
                                        p[cc + t + 1]);
-            pk[t / 2] = pack_bf16x2(ds.x, ds.y);
+            pk[(cc + t) / 2] = pack_bf16x2(ds.x, ds.y);
           }
-          tmem_st16(tmem + lane_off + T_DPT + 64 * h + cc / 2, pk);
-          // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
-          // [64h, 64h+64) of this half, 16-byte units XOR-swizzled by (kr & 7).
+        }
+        tmem_st16(tmem + lane_off + T_DPT + 32 * g, pk);
+        // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
+        // [64(g/2), 64(g/2)+64), 16-byte units XOR-swizzled by (kr & 7).
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int unit = cc / 8 + u;
-            uint4* dst = reinterpret_cast<uint4*>(ds_tile + kr * 128 + ((unit ^ (kr & 7)) << 4));
-            *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-          }
+        for (int u = 0; u < 4; ++u) {
+          const int unit = unit0 + u;
+          uint4* dst = reinterpret_cast<uint4*>(ds_tile + kr * 128 + ((unit ^ (kr & 7)) << 4));
+          *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
         tmem_st_wait();
         fence_proxy_async_smem();
@@ -414,33 +406,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&bars->ds_ready);
       }
       if (!ok) break;
-      // ---------------------------------------------------------- item epilogue: dV (h=0), dK (h=1)
+      // ---------------------------------------------------------- item epilogue
+      // groups 0, 1: dV columns [32g, 32g+32); groups 2, 3: dK columns [32(g-2), ...)
       if (!(ok = mbar_wait(&bars->acc_done, ic & 1, wc))) break;
       tc_fence_after();
-      uint32_t v[DP];
-      const uint32_t col = h ? T_DK : T_DV;
-      tmem_ld32(tmem + lane_off + col, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32(tmem + lane_off + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      const bool is_k = g >= 2;
+      const int c0 = 32 * (g & 1);
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_off + (is_k ? T_DK : T_DV) + c0, v);
       tmem_ld_wait();
       tc_fence_before();  // the next item's first dV / dK MMAs follow this warp's next p_ready
-      if (key < args.S) {
-        const float mul = h ? args.scale : 1.f;
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) +
-                             ((size_t)I.b * args.S + key) * (h ? args.lddk : args.lddv) + (size_t)I.h * args.D;
-        if (args.D == DP) {
+      if (kvalid) {
+        const float mul = is_k ? args.scale : 1.f;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(is_k ? args.dK : args.dV) +
+                             ((size_t)I.b * args.S + key) * (is_k ? args.lddk : args.lddv) + (size_t)I.h * args.D;
+        if (c0 + 32 <= args.D) {
 #pragma unroll
-          for (int c = 0; c < DP; c += 8) {
+          for (int c = 0; c < 32; c += 8) {
             uint4 wv;
             wv.x = pack_bf16x2(__uint_as_float(v[c + 0]) * mul, __uint_as_float(v[c + 1]) * mul);
             wv.y = pack_bf16x2(__uint_as_float(v[c + 2]) * mul, __uint_as_float(v[c + 3]) * mul);
             wv.z = pack_bf16x2(__uint_as_float(v[c + 4]) * mul, __uint_as_float(v[c + 5]) * mul);
             wv.w = pack_bf16x2(__uint_as_float(v[c + 6]) * mul, __uint_as_float(v[c + 7]) * mul);
-            *reinterpret_cast<uint4*>(dst + c) = wv;
+            *reinterpret_cast<uint4*>(dst + c0 + c) = wv;
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < DP; ++c)
-            if (c < args.D) dst[c] = __float2bfloat16_rn(__uint_as_float(v[c]) * mul);
+          for (int c = 0; c < 32; ++c)
+            if (c0 + c < args.D) dst[c0 + c] = __float2bfloat16_rn(__uint_as_float(v[c]) * mul);
         }
       }
     }
@@ -448,7 +441,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 13) {
+  if (warp == W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
