@@ -17,9 +17,10 @@ from __future__ import annotations
 from . import _lib
 from .ops import (  # noqa: F401
     gemm, bmm, gemm_batched, conv2d, conv2d_backward, flash_fwd_rows, flash_bwd_rows, flash_fwd, flash_bwd, gemm_w8, gemm_i8i32, quantize_rows_i8,
-    gemm_workspace_size, flash_bwd_workspace_size, init, sync_check, version,
+    gemm_workspace_size, flash_bwd_workspace_size, flash_set_deterministic, init, sync_check, version,
 )
 from ._lib import DgxError  # noqa: F401
 
 __all__ = ["gemm", "bmm", "gemm_batched", "conv2d", "conv2d_backward", "flash_fwd_rows", "flash_bwd_rows", "flash_fwd", "flash_bwd", "gemm_w8", "gemm_i8i32", "quantize_rows_i8",
-           "gemm_workspace_size", "flash_bwd_workspace_size", "init", "sync_check", "version", "DgxError"]
+           "gemm_workspace_size", "flash_bwd_workspace_size", "flash_set_deterministic", "init", "sync_check",
+           "version", "DgxError"]

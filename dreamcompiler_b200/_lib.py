@@ -63,6 +63,7 @@ SIGNATURES = {
     "dgx_flash_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp]),
     "dgx_flash_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _sz, _vp]),
     "dgx_flash_bwd_workspace_size": (_sz, [_i, _i, _i]),
+    "dgx_flash_set_deterministic": (_i, [_i]),
     "dgx_gemm_w8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "dgx_gemm_w8a8_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "dgx_gemm_i8i32": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),

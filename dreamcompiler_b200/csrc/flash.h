@@ -63,13 +63,19 @@ size_t flash_bwd_scratch_bytes(int BH, int S, int D);
 
 // Head dims the tensor-core kernels take: D % 8 == 0, D <= 128. The backward
 // runs one kernel for D <= 64 (dQ reduced through an fp32 accumulator) and two
-// for 64 < D <= 128 (dK/dV per key tile, dQ per query tile).
+// for 64 < D <= 128, or for any D in deterministic mode (dK/dV per key tile,
+// dQ per query tile).
 constexpr int kFlashFwdMaxD = 128, kFlashBwdMaxD = 128;
 bool flash_tc_supported(int D, int max_d, const void* const* ptrs, int n);
 bool make_head_map(CUtensorMap* map, const void* base, int BH, int H, int S, int D, int ld);
 cudaError_t flash_fwd_tc(const FlashFwdArgs& a, cudaStream_t s);
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s);
-cudaError_t flash_bwd128_tc(const FlashBwdArgs& a, cudaStream_t s);
+// Two kernels with one owner per gradient element (dK/dV per key tile, dQ
+// per query tile): D <= 128, bit-reproducible.
+cudaError_t flash_bwd_split_tc(const FlashBwdArgs& a, cudaStream_t s);
+// Whether backward calls with D <= 64 take the split, reproducible path too.
+void flash_set_deterministic(bool on);
+bool flash_deterministic();
 // The backward's row pre-pass alone: D_i and LSE_i*log2 e into a.rowstat.
 cudaError_t flash_bwd_rowstats(const FlashBwdArgs& a, cudaStream_t s);
 // SIMT kernels for head dims the tensor-core kernels do not take (D % 8 != 0,

@@ -6,6 +6,11 @@ using namespace dgx;
 
 extern "C" {
 
+dgx_status dgx_flash_set_deterministic(int on) {
+  flash_set_deterministic(on != 0);
+  return DGX_OK;
+}
+
 size_t dgx_flash_bwd_workspace_size(int BH, int S, int D) {
   if (BH <= 0 || S <= 0 || D <= 0) return 0;
   return flash_bwd_scratch_bytes(BH, S, D);

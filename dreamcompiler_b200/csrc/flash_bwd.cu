@@ -25,6 +25,8 @@
 // scales the accumulator and casts it to bf16.
 #include <math.h>
 
+#include <atomic>
+
 #include "common.h"
 #include "flash.h"
 #include "sm100.cuh"
@@ -564,8 +566,12 @@ cudaError_t flash_bwd_rowstats(const FlashBwdArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+static std::atomic<int> g_flash_deterministic{0};
+void flash_set_deterministic(bool on) { g_flash_deterministic.store(on ? 1 : 0); }
+bool flash_deterministic() { return g_flash_deterministic.load() != 0; }
+
 cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
-  if (a.D > DP) return flash_bwd128_tc(a, s);
+  if (a.D > DP || flash_deterministic()) return flash_bwd_split_tc(a, s);
   CUtensorMap mq{}, mk{}, mv{}, mdo{};
   FlashBwdArgs la = a;
   la.dense3d = a.H == 1 && a.ldq == a.D && a.ldk == a.D && a.ldv == a.D && a.lddo == a.D;

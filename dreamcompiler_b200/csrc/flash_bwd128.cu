@@ -1,28 +1,31 @@
-// FlashAttention backward for head dims 64 < D <= 128 on sm_100a.
+// FlashAttention backward as two kernels with one owner per gradient element,
+// on sm_100a. Used for head dims 64 < D <= 128, and for every head dim when
+// bit-reproducible results are asked for (dgx_flash_set_deterministic).
 //
 // Replaces the "flash_attention" branch of backward()
-// (runtime/ops/autograd.inc:779-840) for the head sizes the reference's GPU
-// kernel serves up to (dk <= 128, runtime/nn/training.inc:318, :336). At
-// D = 128 one CTA's TMEM cannot hold S^T, dP^T, the dV and dK accumulators
-// and a dQ accumulator at once (512 columns: 128 each for the first four),
-// so the gradients come from two tensor-core kernels with one owner per
-// output element:
+// (runtime/ops/autograd.inc:779-840), including the head sizes the
+// reference's GPU kernel serves up to (dk <= 128, runtime/nn/training.inc:318,
+// :336). At D = 128 one CTA's TMEM cannot hold S^T, dP^T, the dV and dK
+// accumulators and a dQ accumulator at once (512 columns: 128 each for the
+// first four), so the gradients come from two tensor-core kernels:
 //
-//   flash_bwd128_dkdv_kernel  per 128-key tile, walking the Q tiles that see
+//   flash_bwd_dkdv_kernel  per 128-key tile, walking the Q tiles that see
 //     it:  S^T = K Q^T, dP^T = V dO^T, P^T and dS^T written back over them
 //     in TMEM as bf16, dV += P^T dO, dK += dS^T Q.
-//   flash_bwd128_dq_kernel    per 128-query tile, walking the key tiles it
+//   flash_bwd_dq_kernel    per 128-query tile, walking the key tiles it
 //     sees:  S = Q K^T (two buffers), dP = dO V^T, dS written over its S
 //     buffer, dQ += dS K; dQ leaves as bf16 straight from TMEM.
 //
 // S and dP are computed twice (once per kernel), but nothing is reduced
-// through memory: no fp32 dQ accumulator, no atomics, and the result is the
-// same bits on every run. The row statistics (D_i = dO_i.O_i, LSE_i*log2 e)
-// come from the backward's row pre-pass (flash_bwd.cu).
+// through memory: no fp32 dQ accumulator, no atomics, and every run gives
+// the same bits, which is the reference's determinism property
+// (tests/16_determinism.dream) for dQ as well. The row statistics
+// (D_i = dO_i.O_i, LSE_i*log2 e) come from the backward's row pre-pass
+// (flash_bwd.cu).
 //
-// Tiles are 128 rows x 128 columns bf16 held as two 64-column SW128 halves;
-// contractions over D cross into the second half after four K steps, and
-// an MN-major operand's two halves are its two 128-byte atoms along N.
+// Tiles are 128 rows x DP columns bf16 (DP = 64 or 128) held as 64-column
+// SW128 halves; contractions over D cross into the second half after four K
+// steps, and an MN-major operand's halves are its 128-byte atoms along N.
 #include <math.h>
 
 #include "common.h"
@@ -34,7 +37,6 @@ namespace {
 
 constexpr int BT = 128;                  // rows of every tile (keys or queries)
 constexpr int HALF = 128 * 128;          // one 64-column SW128 half: 128 rows x 128 B
-constexpr int TILE = 2 * HALF;           // 32 KB
 constexpr int NUM_THREADS = 384;         // WG0-1: compute, warp 8: TMA, warp 9: MMA, 2 idle
 // setmaxnreg split (per thread): 2 x 4 warps x 224 + 4 warps x 56 = 168 x 12 warps.
 constexpr uint32_t REG_COMPUTE = 224, REG_CTRL = 56;
@@ -46,38 +48,40 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// d = a . b^T over D = 128 (both K-major, 8 K steps across the two halves)
-__device__ __forceinline__ void mma_kmajor_d128(uint32_t d, uint32_t a_smem, uint32_t b_smem, uint32_t idesc) {
+// d = a . b^T over D = DP (both K-major, DP/16 K steps across the halves)
+template <int DP>
+__device__ __forceinline__ void mma_kmajor(uint32_t d, uint32_t a_smem, uint32_t b_smem, uint32_t idesc) {
   const uint64_t da = sw128_desc(a_smem, 16, 1024), db = sw128_desc(b_smem, 16, 1024);
 #pragma unroll 1
-  for (int kk = 0; kk < 8; ++kk) {
+  for (int kk = 0; kk < DP / 16; ++kk) {
     const uint32_t off = (kk >> 2) * (HALF >> 4) + (kk & 3) * 2;
     mma_f16_ss(d, da + off, db + off, idesc, kk > 0 ? 1u : 0u);
   }
 }
 
 // d (+)= A(tmem, 128 bf16 columns packed as [64h, 64h+32) for h = 0, 1) .
-// B (smem, 128 rows of the contraction x 128 columns N, MN-major halves)
-__device__ __forceinline__ void mma_tmem_a_d128(uint32_t d, uint32_t a_tmem, uint32_t b_smem, uint32_t idesc,
-                                                bool first) {
+// B (smem, 128 rows of the contraction x N = DP columns, MN-major halves)
+__device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t a_tmem, uint32_t b_smem, uint32_t idesc,
+                                           bool first) {
   const uint64_t db = sw128_desc(b_smem, HALF, 1024);
 #pragma unroll 1
   for (int kk = 0; kk < 8; ++kk)
     mma_f16_ts(d, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), db + 128 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
 }
 
+template <int DP>
 __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int h, int row,
                                           int b) {
-  tma_load_4d(dst, map, bar, 0, h, row, b);
-  tma_load_4d(dst + HALF, map, bar, 64, h, row, b);
+#pragma unroll
+  for (int hf = 0; hf < DP / 64; ++hf) tma_load_4d(dst + hf * HALF, map, bar, 64 * hf, h, row, b);
 }
 
-// Store 64 fp32 accumulator columns (times `mul`) of one row as bf16
-// columns [c0, c0 + 64) of `dst` (D columns in all).
-__device__ __forceinline__ void store_row64(__nv_bfloat16* dst, const uint32_t (&v)[64], int c0, int D, float mul) {
-  if (c0 + 64 <= D) {
+// Store 32 fp32 accumulator columns (times `mul`) of one row as bf16
+// columns [c0, c0 + 32) of `dst` (D columns in all).
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (&v)[32], int c0, int D, float mul) {
+  if (c0 + 32 <= D) {
 #pragma unroll
-    for (int c = 0; c < 64; c += 8) {
+    for (int c = 0; c < 32; c += 8) {
       uint4 w;
       w.x = pack_bf16x2(__uint_as_float(v[c + 0]) * mul, __uint_as_float(v[c + 1]) * mul);
       w.y = pack_bf16x2(__uint_as_float(v[c + 2]) * mul, __uint_as_float(v[c + 3]) * mul);
@@ -87,18 +91,23 @@ __device__ __forceinline__ void store_row64(__nv_bfloat16* dst, const uint32_t (
     }
   } else {
 #pragma unroll
-    for (int c = 0; c < 64; ++c)
+    for (int c = 0; c < 32; ++c)
       if (c0 + c < D) dst[c0 + c] = __float2bfloat16_rn(__uint_as_float(v[c]) * mul);
   }
 }
 
 // ============================================================================ dK, dV
-constexpr int KV_SM_K = 0, KV_SM_V = TILE, KV_SM_Q = 2 * TILE, KV_SM_DO = KV_SM_Q + 2 * TILE;  // Q, dO: 2 stages
-constexpr int KV_STAT = 2 * BT * 4;                       // per stage: L2 stats [128], then D stats [128]
-constexpr int KV_SM_STAT = KV_SM_DO + 2 * TILE;
-constexpr int KV_SM_BAR = KV_SM_STAT + 2 * KV_STAT;
-constexpr int KV_SMEM_BYTES = KV_SM_BAR + 256 + 1024;
-constexpr uint32_t KV_T_ST = 0, KV_T_DPT = 128, KV_T_DV = 256, KV_T_DK = 384;
+// Shared memory and TMEM of the dK/dV kernel for head-dim class DP (64 or 128).
+template <int DP>
+struct KvCfg {
+  static constexpr int TILE = BT * DP * 2;
+  static constexpr int SM_K = 0, SM_V = TILE, SM_Q = 2 * TILE, SM_DO = SM_Q + 2 * TILE;  // Q, dO: 2 stages
+  static constexpr int STAT = 2 * BT * 4;  // per stage: L2 stats [128], then D stats [128]
+  static constexpr int SM_STAT = SM_DO + 2 * TILE;
+  static constexpr int SM_BAR = SM_STAT + 2 * STAT;
+  static constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+  static constexpr uint32_t T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 256 + DP;
+};
 
 struct KvBars {
   uint64_t kv_full, kv_empty, q_full[2], q_empty[2];
@@ -107,13 +116,18 @@ struct KvBars {
   int abort;
 };
 
+template <int DP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    flash_bwd128_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                              FlashBwdArgs args) {
+  using Cfg = KvCfg<DP>;
+  constexpr int TILE = Cfg::TILE, KV_SM_K = Cfg::SM_K, KV_SM_V = Cfg::SM_V, KV_SM_Q = Cfg::SM_Q,
+                KV_SM_DO = Cfg::SM_DO, KV_STAT = Cfg::STAT, KV_SM_STAT = Cfg::SM_STAT;
+  constexpr uint32_t KV_T_ST = Cfg::T_ST, KV_T_DPT = Cfg::T_DPT, KV_T_DV = Cfg::T_DV, KV_T_DK = Cfg::T_DK;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  KvBars* bars = reinterpret_cast<KvBars*>(smem + KV_SM_BAR);
+  KvBars* bars = reinterpret_cast<KvBars*>(smem + Cfg::SM_BAR);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WaitCtx wc{&bars->abort, args.err};
   // Work item w: key tile j = w / BH of head bh = w % BH (key tile 0, which
@@ -173,8 +187,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const Item I = item(w);
         if (!(ok = mbar_wait(&bars->kv_empty, (ic & 1) ^ 1, wc))) break;
         mbar_arrive_expect_tx(&bars->kv_full, 2 * TILE);
-        load_tile(smem + KV_SM_K, &tmK, &bars->kv_full, I.h, I.j * BT, I.b);
-        load_tile(smem + KV_SM_V, &tmV, &bars->kv_full, I.h, I.j * BT, I.b);
+        load_tile<DP>(smem + KV_SM_K, &tmK, &bars->kv_full, I.h, I.j * BT, I.b);
+        load_tile<DP>(smem + KV_SM_V, &tmV, &bars->kv_full, I.h, I.j * BT, I.b);
         ++ic;
         const float* Dstat = args.rowstat + (size_t)I.bh * args.Spad;
         const float* L2stat = args.rowstat + (size_t)args.BH * args.Spad + (size_t)I.bh * args.Spad;
@@ -183,8 +197,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!(ok = mbar_wait(&bars->q_empty[s], ((gt >> 1) & 1) ^ 1, wc))) break;
           mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE + KV_STAT);
           const int row = (I.i0 + it) * BT;
-          load_tile(smem + KV_SM_Q + s * TILE, &tmQ, &bars->q_full[s], I.h, row, I.b);
-          load_tile(smem + KV_SM_DO + s * TILE, &tmdO, &bars->q_full[s], I.h, row, I.b);
+          load_tile<DP>(smem + KV_SM_Q + s * TILE, &tmQ, &bars->q_full[s], I.h, row, I.b);
+          load_tile<DP>(smem + KV_SM_DO + s * TILE, &tmdO, &bars->q_full[s], I.h, row, I.b);
           uint8_t* st = smem + KV_SM_STAT + s * KV_STAT;
           bulk_load(st, L2stat + row, BT * 4, &bars->q_full[s]);
           bulk_load(st + BT * 4, Dstat + row, BT * 4, &bars->q_full[s]);
@@ -197,8 +211,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
    } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA
     if (elect_one_lane()) {
-      constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);    // K-major x K-major, N = 128 queries
-      constexpr uint32_t id_acc = make_idesc(1, 0, 1, 128, 128);  // TMEM A x MN-major B, N = D = 128
+      constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);   // K-major x K-major, N = 128 queries
+      constexpr uint32_t id_acc = make_idesc(1, 0, 1, 128, DP);  // TMEM A x MN-major B, N = DP
       const uint32_t sK = smem_u32(smem + KV_SM_K), sV = smem_u32(smem + KV_SM_V);
       const uint32_t sQ = smem_u32(smem + KV_SM_Q), sdO = smem_u32(smem + KV_SM_DO);
       uint32_t gt = 0, ic = 0;
@@ -210,9 +224,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         // S^T and dP^T of the item's first Q tile: their TMEM was last read by
         // the previous item's final dV / dK MMAs, issued before them.
-        mma_kmajor_d128(tmem + KV_T_ST, sK, sQ + (gt & 1) * TILE, id_s);
+        mma_kmajor<DP>(tmem + KV_T_ST, sK, sQ + (gt & 1) * TILE, id_s);
         tc_commit(&bars->s_full);
-        mma_kmajor_d128(tmem + KV_T_DPT, sV, sdO + (gt & 1) * TILE, id_s);
+        mma_kmajor<DP>(tmem + KV_T_DPT, sV, sdO + (gt & 1) * TILE, id_s);
         tc_commit(&bars->dp_full);
         for (int it = 0; it < I.n; ++it, ++gt) {
           const int s = gt & 1, s1 = (gt + 1) & 1;
@@ -221,19 +235,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // read out the previous item's dV / dK, so dV(0) may overwrite them.
           if (!(ok = mbar_wait(&bars->p_ready, gt & 1, wc))) break;
           tc_fence_after();
-          mma_tmem_a_d128(tmem + KV_T_DV, tmem + KV_T_ST, sdO + s * TILE, id_acc, it == 0);  // dV += P^T dO
+          mma_tmem_a(tmem + KV_T_DV, tmem + KV_T_ST, sdO + s * TILE, id_acc, it == 0);  // dV += P^T dO
           if (next) {
             if (!(ok = mbar_wait(&bars->q_full[s1], ((gt + 1) >> 1) & 1, wc))) break;
             tc_fence_after();
-            mma_kmajor_d128(tmem + KV_T_ST, sK, sQ + s1 * TILE, id_s);  // S^T(i+1), after dV(i) read P^T(i)
+            mma_kmajor<DP>(tmem + KV_T_ST, sK, sQ + s1 * TILE, id_s);  // S^T(i+1), after dV(i) read P^T(i)
             tc_commit(&bars->s_full);
           }
           if (!(ok = mbar_wait(&bars->ds_ready, gt & 1, wc))) break;
           tc_fence_after();
-          mma_tmem_a_d128(tmem + KV_T_DK, tmem + KV_T_DPT, sQ + s * TILE, id_acc, it == 0);  // dK += dS^T Q
+          mma_tmem_a(tmem + KV_T_DK, tmem + KV_T_DPT, sQ + s * TILE, id_acc, it == 0);  // dK += dS^T Q
           tc_commit(&bars->q_empty[s]);
           if (next) {
-            mma_kmajor_d128(tmem + KV_T_DPT, sV, sdO + s1 * TILE, id_s);  // dP^T(i+1), after dK(i) read dS^T(i)
+            mma_kmajor<DP>(tmem + KV_T_DPT, sV, sdO + s1 * TILE, id_s);  // dP^T(i+1), after dK(i) read dS^T(i)
             tc_commit(&bars->dp_full);
           }
         }
@@ -338,12 +352,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(h ? args.dK : args.dV) +
                            ((size_t)I.b * args.S + key) * (h ? args.lddk : args.lddv) + (size_t)I.h * args.D;
 #pragma unroll
-      for (int c0 = 0; c0 < 128; c0 += 64) {
-        uint32_t v[64];
-        tmem_ld32(tmem + lane_off + col + c0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld32(tmem + lane_off + col + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      for (int c0 = 0; c0 < DP; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + col + c0, v);
         tmem_ld_wait();
-        if (kvalid) store_row64(dst, v, c0, args.D, mul);
+        if (kvalid) store_row32(dst, v, c0, args.D, mul);
       }
       tc_fence_before();  // the next item's first dV / dK MMAs follow this warp's next p_ready
     }
@@ -358,10 +371,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ============================================================================ dQ
-constexpr int DQ_SM_Q = 0, DQ_SM_DO = TILE, DQ_SM_K = 2 * TILE, DQ_SM_V = DQ_SM_K + 2 * TILE;  // K, V: 2 stages
-constexpr int DQ_SM_BAR = DQ_SM_V + 2 * TILE;
-constexpr int DQ_SMEM_BYTES = DQ_SM_BAR + 256 + 1024;
-constexpr uint32_t DQ_T_S0 = 0, DQ_T_DP = 128, DQ_T_DQ = 256, DQ_T_S1 = 384;
+// Shared memory and TMEM of the dQ kernel for head-dim class DP.
+template <int DP>
+struct DqCfg {
+  static constexpr int TILE = BT * DP * 2;
+  static constexpr int SM_Q = 0, SM_DO = TILE, SM_K = 2 * TILE, SM_V = SM_K + 2 * TILE;  // K, V: 2 stages
+  static constexpr int SM_BAR = SM_V + 2 * TILE;
+  static constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+  static constexpr uint32_t T_S0 = 0, T_DP = 128, T_DQ = 256, T_S1 = 256 + DP;
+};
 
 struct DqBars {
   uint64_t q_full, q_empty, k_full[2], v_full[2], kv_empty[2];
@@ -370,13 +388,18 @@ struct DqBars {
   int abort;
 };
 
+template <int DP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    flash_bwd128_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                            FlashBwdArgs args) {
+  using Cfg = DqCfg<DP>;
+  constexpr int TILE = Cfg::TILE, DQ_SM_Q = Cfg::SM_Q, DQ_SM_DO = Cfg::SM_DO, DQ_SM_K = Cfg::SM_K,
+                DQ_SM_V = Cfg::SM_V;
+  constexpr uint32_t DQ_T_S0 = Cfg::T_S0, DQ_T_DP = Cfg::T_DP, DQ_T_DQ = Cfg::T_DQ, DQ_T_S1 = Cfg::T_S1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  DqBars* bars = reinterpret_cast<DqBars*>(smem + DQ_SM_BAR);
+  DqBars* bars = reinterpret_cast<DqBars*>(smem + Cfg::SM_BAR);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WaitCtx wc{&bars->abort, args.err};
   // Work item w: query tile i of head bh (causal: the last query tiles, which
@@ -437,16 +460,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const Item I = item(w);
         if (!(ok = mbar_wait(&bars->q_empty, (ic & 1) ^ 1, wc))) break;
         mbar_arrive_expect_tx(&bars->q_full, 2 * TILE);
-        load_tile(smem + DQ_SM_Q, &tmQ, &bars->q_full, I.h, I.i * BT, I.b);
-        load_tile(smem + DQ_SM_DO, &tmdO, &bars->q_full, I.h, I.i * BT, I.b);
+        load_tile<DP>(smem + DQ_SM_Q, &tmQ, &bars->q_full, I.h, I.i * BT, I.b);
+        load_tile<DP>(smem + DQ_SM_DO, &tmdO, &bars->q_full, I.h, I.i * BT, I.b);
         ++ic;
         for (int j = 0; j < I.n; ++j, ++g) {
           const int s = g & 1;
           if (!(ok = mbar_wait(&bars->kv_empty[s], ((g >> 1) & 1) ^ 1, wc))) break;
           mbar_arrive_expect_tx(&bars->k_full[s], TILE);
-          load_tile(smem + DQ_SM_K + s * TILE, &tmK, &bars->k_full[s], I.h, j * BT, I.b);
+          load_tile<DP>(smem + DQ_SM_K + s * TILE, &tmK, &bars->k_full[s], I.h, j * BT, I.b);
           mbar_arrive_expect_tx(&bars->v_full[s], TILE);
-          load_tile(smem + DQ_SM_V + s * TILE, &tmV, &bars->v_full[s], I.h, j * BT, I.b);
+          load_tile<DP>(smem + DQ_SM_V + s * TILE, &tmV, &bars->v_full[s], I.h, j * BT, I.b);
         }
       }
       if (ic > 0) mbar_drain(&bars->q_full, (ic - 1) & 1);
@@ -459,7 +482,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------------------------------------------------------- MMA
     if (elect_one_lane()) {
       constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);   // Q.K^T and dO.V^T: K-major, N = 128 keys
-      constexpr uint32_t id_dq = make_idesc(1, 0, 1, 128, 128);  // dS (TMEM) . K (MN-major), N = D = 128
+      constexpr uint32_t id_dq = make_idesc(1, 0, 1, 128, DP);   // dS (TMEM) . K (MN-major), N = DP
       const uint32_t sQ = smem_u32(smem + DQ_SM_Q), sdO = smem_u32(smem + DQ_SM_DO);
       const uint32_t sK = smem_u32(smem + DQ_SM_K), sV = smem_u32(smem + DQ_SM_V);
       auto t_s = [&](uint32_t g) { return tmem + ((g & 1) ? DQ_T_S1 : DQ_T_S0); };
@@ -469,14 +492,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // warps have read dP(g-1); S(g+2) reuses S(g)'s buffer after dQ(g)
       // (issued before it) has read the dS written there.
       auto issue_s = [&](uint32_t gg) {
-        mma_kmajor_d128(t_s(gg), sQ, sK + (gg & 1) * TILE, id_s);
+        mma_kmajor<DP>(t_s(gg), sQ, sK + (gg & 1) * TILE, id_s);
         tc_commit(&bars->s_full[gg & 1]);
       };
       auto issue_dp = [&](uint32_t gg) {
         if (gg > 0 && !mbar_wait(&bars->dp_free, (gg - 1) & 1, wc)) return false;
         if (!mbar_wait(&bars->v_full[gg & 1], (gg >> 1) & 1, wc)) return false;
         tc_fence_after();
-        mma_kmajor_d128(tmem + DQ_T_DP, sdO, sV + (gg & 1) * TILE, id_s);
+        mma_kmajor<DP>(tmem + DQ_T_DP, sdO, sV + (gg & 1) * TILE, id_s);
         tc_commit(&bars->dp_full);
         return true;
       };
@@ -498,7 +521,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int j = 0; ok && j < I.n; ++j, ++g) {
           if (!(ok = mbar_wait(&bars->ds_ready, g & 1, wc))) break;
           tc_fence_after();
-          mma_tmem_a_d128(tmem + DQ_T_DQ, t_s(g), sK + (g & 1) * TILE, id_dq, j == 0);  // dQ += dS K
+          mma_tmem_a(tmem + DQ_T_DQ, t_s(g), sK + (g & 1) * TILE, id_dq, j == 0);  // dQ += dS K
           tc_commit(&bars->kv_empty[g & 1]);
           if (j + 1 < I.n && !(ok = issue_dp(g + 1))) break;
           if (j + 2 < I.n) {
@@ -580,21 +603,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&bars->ds_ready);
       }
       if (!ok) break;
-      // ---------------------------------------------------------- item epilogue: dQ columns [64h, 64h+64)
+      // ---------------------------------------------------------- item epilogue: dQ columns [h*DP/2, (h+1)*DP/2)
       if (!(ok = mbar_wait(&bars->dq_done, ic & 1, wc))) break;
       tc_fence_after();
-      uint32_t v[64];
-      tmem_ld32(tmem + lane_off + DQ_T_DQ + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32(tmem + lane_off + DQ_T_DQ + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-      tmem_ld_wait();
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.dQ) +
+                           ((size_t)I.b * args.S + query) * args.lddq + (size_t)I.h * args.D;
+#pragma unroll
+      for (int c0 = h * DP / 2; c0 < (h + 1) * DP / 2; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + DQ_T_DQ + c0, v);
+        tmem_ld_wait();
+        if (query < args.S) store_row32(dst, v, c0, args.D, args.scale);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->dq_free);
-      if (query < args.S) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.dQ) +
-                             ((size_t)I.b * args.S + query) * args.lddq + (size_t)I.h * args.D;
-        store_row64(dst, v, 64 * h, args.D, args.scale);
-      }
     }
   }
 
@@ -608,19 +631,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 }  // namespace
 
-// Row pre-pass (flash_bwd.cu) then the two kernels, in order on `s`.
-cudaError_t flash_bwd128_tc(const FlashBwdArgs& a, cudaStream_t s) {
-  CUtensorMap mq{}, mk{}, mv{}, mdo{};
-  if (!make_head_map(&mq, a.Q, a.BH, a.H, a.S, a.D, a.ldq) || !make_head_map(&mk, a.K, a.BH, a.H, a.S, a.D, a.ldk) ||
-      !make_head_map(&mv, a.V, a.BH, a.H, a.S, a.D, a.ldv) ||
-      !make_head_map(&mdo, a.dO, a.BH, a.H, a.S, a.D, a.lddo))
-    return cudaErrorInvalidValue;
+namespace {
+template <int DP>
+cudaError_t launch_split(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                         const FlashBwdArgs& a, cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(flash_bwd128_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         KV_SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(flash_bwd_dkdv_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         KvCfg<DP>::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(flash_bwd128_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM_BYTES);
+    e = cudaFuncSetAttribute(flash_bwd_dq_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DqCfg<DP>::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -631,12 +652,25 @@ cudaError_t flash_bwd128_tc(const FlashBwdArgs& a, cudaStream_t s) {
   const int grid = items < sms ? items : sms;
   {
     TimerScope timer(s);
-    flash_bwd128_dkdv_kernel<<<grid, NUM_THREADS, KV_SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+    flash_bwd_dkdv_kernel<DP><<<grid, NUM_THREADS, KvCfg<DP>::SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  flash_bwd128_dq_kernel<<<grid, NUM_THREADS, DQ_SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
+  flash_bwd_dq_kernel<DP><<<grid, NUM_THREADS, DqCfg<DP>::SMEM_BYTES, s>>>(mq, mk, mv, mdo, a);
   return cudaGetLastError();
+}
+}  // namespace
+
+// Row pre-pass (flash_bwd.cu) then the two kernels, in order on `s`.
+cudaError_t flash_bwd_split_tc(const FlashBwdArgs& a, cudaStream_t s) {
+  CUtensorMap mq{}, mk{}, mv{}, mdo{};
+  if (!make_head_map(&mq, a.Q, a.BH, a.H, a.S, a.D, a.ldq) || !make_head_map(&mk, a.K, a.BH, a.H, a.S, a.D, a.ldk) ||
+      !make_head_map(&mv, a.V, a.BH, a.H, a.S, a.D, a.ldv) ||
+      !make_head_map(&mdo, a.dO, a.BH, a.H, a.S, a.D, a.lddo))
+    return cudaErrorInvalidValue;
+  if (a.D <= 64) return launch_split<64>(mq, mk, mv, mdo, a, s);
+  if (a.D <= 128) return launch_split<128>(mq, mk, mv, mdo, a, s);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace dgx

@@ -182,6 +182,12 @@ def flash_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, causal: bool
     return out, lse
 
 
+def flash_set_deterministic(on: bool) -> None:
+    """Process-wide: backward calls with D <= 64 take the two-kernel form
+    (every gradient bit-reproducible) instead of the one-kernel form."""
+    L.call("dgx_flash_set_deterministic", int(bool(on)))
+
+
 def flash_bwd_workspace_size(BH: int, S: int, D: int) -> int:
     return L.load().dgx_flash_bwd_workspace_size(BH, S, D)
 

@@ -234,6 +234,18 @@ dgx_status dgx_flash_fwd(const void* Q, const void* K, const void* V, void* O, f
                          float scale, int causal, dgx_dtype dtype, void* stream);
 
 /*
+ * Reproducibility of the FlashAttention backward (process-wide, default 0).
+ * Head dims <= 64 normally take one kernel whose dQ sums each key tile's
+ * part by fp32 reduce-adds in completion order: dK and dV are the same bits
+ * on every run, dQ can differ in the last bits. With on = 1 they take the
+ * two-kernel form that 64 < D <= 128 always uses (dK/dV per key tile, dQ per
+ * query tile, no accumulation through memory): every gradient is the same
+ * bits on every run, at the cost of computing S and dP twice. The reference
+ * promises byte-identical seeded runs (tests/16_determinism.dream).
+ */
+dgx_status dgx_flash_set_deterministic(int on);
+
+/*
  * FlashAttention backward: dQ, dK, dV ([BH][S][D], dtype) from Q, K, V, O, dO
  * and the forward's LSE. workspace: at least dgx_flash_bwd_workspace_size()
  * bytes of device scratch (fp32 dQ accumulator and the row terms
