@@ -31,9 +31,18 @@ constexpr int G2_BK = 64;   // one 128-byte swizzled row of bf16 K
 constexpr int G2_A_BYTES = G2_BM * G2_BK * 2;         // 16 KB
 constexpr int G2_B_BYTES = (G2_BN / 2) * G2_BK * 2;   // 16 KB
 constexpr int G2_STAGE = G2_A_BYTES + G2_B_BYTES;     // 32 KB per CTA
-constexpr int G2_STAGES = 6;
-constexpr int G2_OUT_STAGE = 4 * 2 * 4096;
-constexpr int G2_SMEM = G2_STAGES * G2_STAGE + G2_OUT_STAGE + 1024 + 256;
+// Operand stages and output staging per instantiation: 6 stages and two
+// 4 KB staging boxes per epilogue warp; with extra destinations (the
+// column-parallel GEMM's peer stores, four or more TMA stores per box, whose
+// reads of the box wait on NVLink) 5 stages and four boxes per warp, so a
+// warp can stage two more boxes before it waits for earlier stores to leave.
+template <bool EXTRA>
+struct G2Cfg {
+  static constexpr int STAGES = EXTRA ? 5 : 6;
+  static constexpr int OUT_BUFS = EXTRA ? 4 : 2;
+  static constexpr int OUT_STAGE = 4 * OUT_BUFS * 4096;
+  static constexpr int SMEM = STAGES * G2_STAGE + OUT_STAGE + 1024 + 256;
+};
 constexpr uint32_t G2_TMEM_COLS = 512;
 constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;  // shared::cluster address of the pair leader's copy
 
@@ -115,8 +124,9 @@ __global__ void __launch_bounds__(192, 1)
                  GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int G2_STAGES = G2Cfg<EXTRA>::STAGES, OUT_BUFS = G2Cfg<EXTRA>::OUT_BUFS;
   uint8_t* out_stage = smem + G2_STAGES * G2_STAGE;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(out_stage + G2_OUT_STAGE);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(out_stage + G2Cfg<EXTRA>::OUT_STAGE);
   uint64_t* empty_bar = full_bar + G2_STAGES;
   uint64_t* accf_bar = empty_bar + G2_STAGES;  // [2]
   uint64_t* acce_bar = accf_bar + 2;           // [2]
@@ -229,7 +239,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
     const int q = warp & 3;
-    uint8_t* my_stage = out_stage + (warp - 2) * 8192;
+    uint8_t* my_stage = out_stage + (warp - 2) * OUT_BUFS * 4096;
     uint32_t issued = 0, use = 0;
     if (lane == 0) {
       tma_prefetch_desc(&tmC);
@@ -275,8 +285,13 @@ __global__ void __launch_bounds__(192, 1)
         }
         const int n0 = tn * G2_BN + c;
         if (n0 >= args.N) continue;
-        uint8_t* st = my_stage + (issued & 1) * 4096;
-        if (lane == 0 && issued >= 2) bulk_wait_read1();
+        uint8_t* st = my_stage + (issued % OUT_BUFS) * 4096;
+        if (lane == 0 && issued >= (uint32_t)OUT_BUFS) {
+          if constexpr (OUT_BUFS == 4)
+            bulk_wait_read3();
+          else
+            bulk_wait_read1();
+        }
         __syncwarp();
         uint32_t w[32];
         if (args.c_bf16) {
@@ -410,9 +425,10 @@ cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cud
   const bool extra = a.n_extra > 0;  // B stored [K][N] (gemm2_eligible)
   auto kern = extra ? gemm2_kernel<true, true> : b_mn ? gemm2_kernel<true, false> : gemm2_kernel<false, false>;
   const int variant = extra ? 2 : b_mn;
+  const int smem = extra ? G2Cfg<true>::SMEM : G2Cfg<false>::SMEM;
   static bool attr_done[3] = {false, false, false};
   if (!attr_done[variant]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_done[variant] = true;
   }
@@ -421,7 +437,7 @@ cudaError_t gemm2_launch(const GemmArgs& args, const void* A, const void* B, cud
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(192);
-  cfg.dynamicSmemBytes = G2_SMEM;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
