@@ -350,16 +350,19 @@ def run_reference_api_e2e(steps: int):
     before = R.counts()
     step(0)
     walls = []
+    tb = R.times_us()
     for i in range(steps):
         t0 = time.perf_counter()
         step(i + 1)
         walls.append(time.perf_counter() - t0)
     after = R.counts()
+    ta = R.times_us()
     t = statistics.median(walls)
     nbytes = BH * S * D * 8
     return {"value": (FWD_FLOP + BWD_FLOP) / t / 1e12, "unit": "TFLOPS", "ms_per_step": t * 1e3,
             "steps": steps, "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes,
             "device_ops": {k: after[k] - before[k] for k in after},
+            "backend_host_ms_per_step": {k: (ta[k] - tb[k]) / steps / 1e3 for k in ta},
             "path": "reference Dream runtime (its own struct Tensor, ops and autograd) with the B200 backend: "
                     "f64 host tensors Q, K, V, G -> dream_flash_attention + backward(sum(O*G)) -> O, dQ, dK, dV "
                     "as f64 host tensors; host wall time, median over steps"}

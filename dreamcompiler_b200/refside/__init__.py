@@ -61,12 +61,23 @@ def load() -> C.CDLL:
             f.restype = TP
         _rt.dream_b200_count.argtypes = [C.c_int]
         _rt.dream_b200_count.restype = C.c_longlong
+        _rt.dream_b200_time_us.argtypes = [C.c_int]
+        _rt.dream_b200_time_us.restype = C.c_double
     return _rt
 
 
 def counts() -> dict:
     rt = load()
     return {name: rt.dream_b200_count(i) for i, name in enumerate(COUNTS)}
+
+
+TIMES = ["fingerprint", "upload", "download", "ops"]
+
+
+def times_us() -> dict:
+    """Host wall time the backend spent so far, by kind (microseconds)."""
+    rt = load()
+    return {name: rt.dream_b200_time_us(i) for i, name in enumerate(TIMES)}
 
 
 def scalar(v: float):
