@@ -12,8 +12,9 @@
 # (src/main.cpp:994) plus -fPIC. Nothing from the reference is written into
 # this repository except the compiled library under oracle/_ref/.
 set -euo pipefail
-REF=${1:-/root/reference}
 HERE="$(cd "$(dirname "$0")" && pwd)"
+# The reference checkout sits beside this repository unless an argument names it.
+REF=${1:-$(dirname "$(dirname "$HERE")")/reference}
 OUT="$HERE/_ref"
 [ -d "$REF/runtime" ] || { echo "reference runtime not found at $REF/runtime" >&2; exit 2; }
 mkdir -p "$OUT"

@@ -118,3 +118,39 @@ def test_w8a32_extreme_rows(dgx, orc):
             assert not Yh[r].any(), r
         else:
             assert np.linalg.norm(Yh[r] - ref[r]) / nr < 1e-5, r
+
+
+@pytest.mark.parametrize("B,N,K", [
+    (1, 4096, 4096),    # config 5, 4-CTA clusters
+    (16, 4096, 4096),   # 16 rows
+    (5, 384, 8192),     # 8-CTA clusters, 8 K blocks per CTA
+    (11, 130, 4112),    # 7 CTAs per cluster, the last one 3 blocks with a 16-value tail
+    (3, 1000, 1024),    # 8 CTAs of one block each
+])
+def test_w8a8_small_batches_exact(dgx, orc, B, N, K):
+    """Small W8A8 batches (the split-K cluster form) against the oracle's
+    quantiser and exact int32 products, rounded once in fp32: any activation
+    quantised differently moves an output by scale*sx*|w| >> the 4-ulp bound
+    used here. Rows include an all-zero row, a single spike, and values exactly
+    halfway between two steps."""
+    X, W, sc, b = inputs(orc, B, N, K, seed=B * 13 + N + K)
+    if B >= 3:
+        X[1] = 0
+        X[2] = 0
+        X[2, K // 3] = -2.75
+    if B >= 5:
+        # x = (j + 0.5) * sx exactly: ties, which round half away from zero
+        step = np.float32(4.0) / np.float32(127.0)
+        X[4] = 0
+        X[4, 0] = 4.0
+        X[4, 1:9] = (np.arange(8, dtype=np.float32) + np.float32(0.5)) * step * np.float32(np.where(np.arange(8) % 2, -1, 1))
+    Xd, Wd, scd, bd = (torch.from_numpy(a).cuda() for a in (X, W, sc, b))
+    Y = dgx.gemm_w8(Xd, Wd, scd, bd, mode=1)
+    dgx.sync_check()
+    rXq, rsx = orc.quantize_rows(X)
+    racc = orc.i8_gemm(rXq, W).astype(np.float64)
+    x = (sc[None, :] * rsx[:, None]).astype(np.float32).astype(np.float64)  # fp32 scale product, as the kernel
+    ref = x * racc.astype(np.float32).astype(np.float64) + b.astype(np.float64)
+    err = np.abs(Y.cpu().numpy().astype(np.float64) - ref)
+    bound = 4 * 2.0 ** -23 * (np.abs(x * racc) + np.abs(b.astype(np.float64))) + 1e-30
+    assert (err <= bound).all(), (np.argwhere(err > bound)[:5], err.max())
