@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmdO);
       uint32_t gt = 0, ic = 0;
       bool ok = true;
-      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+      for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd)) {
         const Item I = item(w);
         if (!(ok = mbar_wait(&bars->kv_empty, (ic & 1) ^ 1, wc))) break;
         mbar_arrive_expect_tx(&bars->kv_full, 2 * TILE);
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t sQ = smem_u32(smem + KV_SM_Q), sdO = smem_u32(smem + KV_SM_DO);
       uint32_t gt = 0, ic = 0;
       bool ok = true;
-      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+      for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd), ++ic) {
         const Item I = item(w);
         if (!(ok = mbar_wait(&bars->kv_full, ic & 1, wc) && mbar_wait(&bars->q_full[gt & 1], (gt >> 1) & 1, wc)))
           break;
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float sl2 = args.scale * 1.4426950408889634f;
     uint32_t gt = 0, ic = 0;
     bool ok = true;
-    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+    for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd), ++ic) {
       const Item I = item(w);
       const int key = I.j * BT + kr;
       const bool kvalid = key < args.S;
@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmdO);
       uint32_t g = 0, ic = 0;
       bool ok = true;
-      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+      for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd)) {
         const Item I = item(w);
         if (!(ok = mbar_wait(&bars->q_empty, (ic & 1) ^ 1, wc))) break;
         mbar_arrive_expect_tx(&bars->q_full, 2 * TILE);
@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_commit(&bars->dp_full);
         return true;
       };
-      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+      for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd), ++ic) {
         const Item I = item(w);
         const uint32_t g0 = g;
         if (!(ok = mbar_wait(&bars->q_full, ic & 1, wc) && mbar_wait(&bars->k_full[g0 & 1], (g0 >> 1) & 1, wc)))
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float sl2 = args.scale * 1.4426950408889634f;
     uint32_t g = 0, ic = 0;
     bool ok = true;
-    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+    for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd), ++ic) {
       const Item I = item(w);
       const int query = I.i * BT + qr;
       // this row's statistics (rows past S: L2 = +inf, so P = 0)

@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + SM_BAR);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WaitCtx wc{&bars->abort, args.err};
-  // Persistent: this CTA walks items blockIdx.x, +gridDim.x, ...; every
-  // barrier phase counts on across items.
+  // Persistent: this CTA walks the items snake_item(0), snake_item(1), ...;
+  // every barrier phase counts on across items.
   const int nitems = ((args.S + 2 * BLOCK_M - 1) / (2 * BLOCK_M)) * args.BH;
 
   if (threadIdx.x == 0) {
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int hf = 0; hf < Cfg::HALVES; ++hf) tma_load_4d(dst + hf * HALF_BYTES, map, bar, hf * 64, I.h, row, I.b);
       };
-      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+      for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd)) {
         const FwdItem I = fwd_item(args, w);
         const int qb = ic % Q_BUFS;
         if (!(ok = mbar_wait(&bars->q_empty[qb], ((ic / Q_BUFS) & 1) ^ 1, wc))) break;
@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if constexpr (Cfg::ALIAS) return np == 0 || mbar_wait(&bars->pv_done[x], (np - 1) & 1, wc);
         return ns == 0 || mbar_wait(&bars->s_free[x], (ns - 1) & 1, wc);
       };
-      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
+      for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd), ++ic) {
         const FwdItem I = fwd_item(args, w);
         const int qb = ic % Q_BUFS;
         const int n = x ? I.nB : I.nA;
@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // completes nA-1 times per item; B: turn[1], nA times per item).
     uint32_t kbase = 0, tbase = 0;
     bool ok = true;
-    for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+    for (int rnd = 0, w = snake_item(0); ok && w < nitems; w = snake_item(++rnd)) {
       const FwdItem I = fwd_item(args, w);
       const int n = x ? I.nB : I.nA;
       const int qrow = I.q0 + x * BLOCK_M + r;

@@ -313,6 +313,19 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, uint32_t a_major
          | (a_major << 15) | (b_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- persistent work order
+// Item of round r for this CTA in a persistent grid whose items are sorted
+// heaviest first: r*G + c on even rounds, r*G + (G-1-c) on odd ones (G =
+// gridDim.x, c = blockIdx.x). Each round hands the G items out in the
+// opposite order to the round before, so the CTAs' total work stays within
+// about one item of each other (a plain r*G + c gives CTA 0 the heaviest item
+// of every round). Every role of a CTA walks the same sequence; a CTA is done
+// at its first item >= the item count, as every later round is higher.
+__device__ __forceinline__ int snake_item(int r) {
+  const int c = (r & 1) ? (int)(gridDim.x - 1u - blockIdx.x) : (int)blockIdx.x;
+  return r * (int)gridDim.x + c;
+}
+
 // ---------------------------------------------------------------- compile-time loops
 template <int V>
 struct IntC {
