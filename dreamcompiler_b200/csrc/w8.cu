@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(256) w8_kernel(const void* __restrict__ X, con
 __global__ void quant_rows_kernel(const float* __restrict__ X, int8_t* __restrict__ Xq, float* __restrict__ sx,
                                   int K) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the GEMM may start streaming weights
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // X may come from the kernel before (launched as its dependent)
   __shared__ float red[32];
   const int b = blockIdx.x;
   const float* x = X + (size_t)b * K;
@@ -175,6 +176,7 @@ template <int NV>
 __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const float* __restrict__ X, int8_t* __restrict__ Xq,
                                                              float* __restrict__ sx, int K) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float red[8];
   const int b = blockIdx.x;
   const float* x = X + (size_t)b * K;
@@ -227,17 +229,11 @@ cudaError_t w8_simt(const void* X, const int8_t* W, const float* scale, const fl
 
 cudaError_t quantize_rows(const float* X, int8_t* Xq, float* sx, int B, int K, cudaStream_t s) {
   const bool vec = K % 4 == 0 && (((uintptr_t)X | (uintptr_t)Xq) & 15) == 0;
-  if (vec && K <= 1024)
-    quant_rows_reg_kernel<1><<<B, 256, 0, s>>>(X, Xq, sx, K);
-  else if (vec && K <= 2048)
-    quant_rows_reg_kernel<2><<<B, 256, 0, s>>>(X, Xq, sx, K);
-  else if (vec && K <= 4096)
-    quant_rows_reg_kernel<4><<<B, 256, 0, s>>>(X, Xq, sx, K);
-  else if (vec && K <= 8192)
-    quant_rows_reg_kernel<8><<<B, 256, 0, s>>>(X, Xq, sx, K);
-  else
-    quant_rows_kernel<<<B, 256, 0, s>>>(X, Xq, sx, K);
-  return cudaGetLastError();
+  if (vec && K <= 1024) return launch_dependent(quant_rows_reg_kernel<1>, B, 256, s, X, Xq, sx, K);
+  if (vec && K <= 2048) return launch_dependent(quant_rows_reg_kernel<2>, B, 256, s, X, Xq, sx, K);
+  if (vec && K <= 4096) return launch_dependent(quant_rows_reg_kernel<4>, B, 256, s, X, Xq, sx, K);
+  if (vec && K <= 8192) return launch_dependent(quant_rows_reg_kernel<8>, B, 256, s, X, Xq, sx, K);
+  return launch_dependent(quant_rows_kernel, B, 256, s, X, Xq, sx, K);
 }
 
 // W8A8 from already quantised activations: tensor cores when TMA can fetch

@@ -31,6 +31,24 @@ cudaError_t w8_tc_gemm(const int8_t* Xp, int planes, const int8_t* W, const floa
                        const float* rowscale, float* Y, int32_t* acc_out, int B, int N, int K,
                        bool after_producer, cudaStream_t s, const W8Epi& epi = W8Epi());
 
+// Launch `kern` as a programmatic dependent of the kernel issued before it on
+// `s`: it may start while that kernel finishes, and must griddepcontrol.wait
+// before it reads anything that kernel writes (the activation pre-passes do,
+// so a layer's quantisation overlaps the tail of the layer before it).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Split fp32 rows into the three int8 planes above (Xp[3][B][K]) and the
 // power-of-two row scales. K % 16 == 0.
 cudaError_t w8_split_planes(const float* X, int8_t* Xp, float* rowscale, int B, int K, cudaStream_t s);

@@ -139,6 +139,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   float* rs_s = reinterpret_cast<float*>(smem + a.ring_bytes + 256);  // this chunk's row scales
   int32_t* inbox = reinterpret_cast<int32_t*>(smem + a.ring_bytes + 256 + 1024);
 
+  // Small batches (split K over clusters, a few microseconds per layer): the
+  // next layer's activation pre-pass, a programmatic dependent that waits for
+  // this grid before it reads anything, may be scheduled now, so its launch
+  // and its own dependent's weight stream overlap this layer's tail. Larger
+  // batches let it start only at exit: there the next layer's weight stream
+  // competing with this one's costs more than the overlap gains.
+  if (a.splits > 1) grid_dep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x;
   const int m0 = blockIdx.y * TC_BM;
@@ -429,6 +436,7 @@ template <int NV>
 __global__ void __launch_bounds__(256) split_planes_kernel(const float* __restrict__ X, int8_t* __restrict__ Xp,
                                                            float* __restrict__ rowscale, int B, int K) {
   grid_dep_launch();  // the GEMM may start streaming weights now
+  grid_dep_wait();    // X may come from the kernel before (launched as its dependent)
   __shared__ float red[8];
   const int b = blockIdx.x;
   const float* x = X + (size_t)b * K;
@@ -457,6 +465,7 @@ __global__ void __launch_bounds__(256) split_planes_kernel(const float* __restri
 __global__ void __launch_bounds__(256) split_planes_loop_kernel(const float* __restrict__ X, int8_t* __restrict__ Xp,
                                                                 float* __restrict__ rowscale, int B, int K) {
   grid_dep_launch();
+  grid_dep_wait();
   __shared__ float red[8];
   const int b = blockIdx.x;
   const float* x = X + (size_t)b * K;
@@ -597,17 +606,11 @@ cudaError_t w8_tc_gemm(const int8_t* Xp, int planes, const int8_t* W, const floa
 }
 
 cudaError_t w8_split_planes(const float* X, int8_t* Xp, float* rowscale, int B, int K, cudaStream_t s) {
-  if (K <= 1024)
-    split_planes_kernel<1><<<B, 256, 0, s>>>(X, Xp, rowscale, B, K);
-  else if (K <= 2048)
-    split_planes_kernel<2><<<B, 256, 0, s>>>(X, Xp, rowscale, B, K);
-  else if (K <= 4096)
-    split_planes_kernel<4><<<B, 256, 0, s>>>(X, Xp, rowscale, B, K);
-  else if (K <= 8192)
-    split_planes_kernel<8><<<B, 256, 0, s>>>(X, Xp, rowscale, B, K);
-  else
-    split_planes_loop_kernel<<<B, 256, 0, s>>>(X, Xp, rowscale, B, K);
-  return cudaGetLastError();
+  if (K <= 1024) return launch_dependent(split_planes_kernel<1>, B, 256, s, X, Xp, rowscale, B, K);
+  if (K <= 2048) return launch_dependent(split_planes_kernel<2>, B, 256, s, X, Xp, rowscale, B, K);
+  if (K <= 4096) return launch_dependent(split_planes_kernel<4>, B, 256, s, X, Xp, rowscale, B, K);
+  if (K <= 8192) return launch_dependent(split_planes_kernel<8>, B, 256, s, X, Xp, rowscale, B, K);
+  return launch_dependent(split_planes_loop_kernel, B, 256, s, X, Xp, rowscale, B, K);
 }
 
 }  // namespace dgx
