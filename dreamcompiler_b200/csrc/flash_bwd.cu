@@ -40,7 +40,8 @@ namespace {
 constexpr int BKV = 128;  // keys per CTA
 constexpr int BQ = 128;   // queries per step
 constexpr int DP = 64;
-constexpr int Q_STAGES = 2;
+constexpr int Q_STAGES = 3;   // Q tiles (with their row statistics): released after dK
+constexpr int DO_STAGES = 2;  // dO tiles: released after dV
 constexpr int TILE = 128 * DP * 2;  // 16 KB
 // Warps 0-15 compute (four groups of four, one per 32 queries of the Q tile),
 // 16-19 dQ drain, 20 TMA, 21 MMA, 22-23 idle: four compute warps per SM
@@ -52,7 +53,7 @@ constexpr int W_DRAIN = 16, W_TMA = 20, W_MMA = 21;
 constexpr uint32_t REG_COMPUTE = 88, REG_DRAIN = 72, REG_CTRL = 56;
 
 constexpr int SM_K = 0, SM_V = 2 * TILE, SM_Q = 4 * TILE, SM_DO = SM_Q + Q_STAGES * TILE;  // K, V: 2 buffers
-constexpr int SM_DS = SM_DO + Q_STAGES * TILE;  // 128 queries x 128 keys bf16, MN-major (2 x 16 KB)
+constexpr int SM_DS = SM_DO + DO_STAGES * TILE;  // 128 queries x 128 keys bf16, MN-major (2 x 16 KB)
 constexpr int SM_STAT = SM_DS + 2 * TILE;  // per stage: L2 stats [128] then D stats [128] (fp32)
 constexpr int STAT_BYTES = 2 * BQ * 4;
 constexpr int SM_DQ = SM_STAT + Q_STAGES * STAT_BYTES;  // dQ staging: 2 boxes of 128 rows x 32 fp32 (SW128)
@@ -71,7 +72,7 @@ __device__ __forceinline__ float ex2(float x) {
 
 
 struct BwdBars {
-  uint64_t kv_full[2], kv_empty[2], q_full[Q_STAGES], q_empty[Q_STAGES];
+  uint64_t kv_full[2], kv_empty[2], q_full[Q_STAGES], q_empty[Q_STAGES], do_full[DO_STAGES], do_empty[DO_STAGES];
   uint64_t s_full, dp_full, p_ready[4], ds_ready[4], dq_full[2], dq_empty[2], acc_done;
   uint32_t tmem_slot;
   int abort;
@@ -114,6 +115,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->kv_full[b], 1);
       mbar_init(&bars->kv_empty[b], 1);
+    }
+    for (int s = 0; s < DO_STAGES; ++s) {
+      mbar_init(&bars->do_full[s], 1);
+      mbar_init(&bars->do_empty[s], 1);
     }
     for (int s = 0; s < Q_STAGES; ++s) {
       mbar_init(&bars->q_full[s], 1);
@@ -158,7 +163,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmdO);
-      int gt = 0, ic = 0;
+      int gt = 0, ic = 0, gdo = 0;  // gt: Q tiles issued, gdo: dO tiles issued
       bool ok = true;
       uint32_t kv_filled = 0;  // items whose K/V load was issued
       for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x, ++ic) {
@@ -177,24 +182,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float* Dstat = args.rowstat + (size_t)I.bh * args.Spad;
         const float* L2stat = args.rowstat + (size_t)args.BH * args.Spad + (size_t)I.bh * args.Spad;
         for (int it = 0; it < I.n; ++it, ++gt) {
-          const int s = gt % Q_STAGES;
+          const int s = gt % Q_STAGES, d = gt % DO_STAGES;
           if (!(ok = mbar_wait(&bars->q_empty[s], ((gt / Q_STAGES) & 1) ^ 1, wc))) break;
-          mbar_arrive_expect_tx(&bars->q_full[s], 2 * TILE + STAT_BYTES);
-          if (args.dense3d) {
+          mbar_arrive_expect_tx(&bars->q_full[s], TILE + STAT_BYTES);
+          if (args.dense3d)
             tma_load_3d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
-            tma_load_3d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, (I.i0 + it) * BQ, I.bh);
-          } else {
+          else
             tma_load_4d(smem + SM_Q + s * TILE, &tmQ, &bars->q_full[s], 0, I.h, (I.i0 + it) * BQ, I.b);
-            tma_load_4d(smem + SM_DO + s * TILE, &tmdO, &bars->q_full[s], 0, I.h, (I.i0 + it) * BQ, I.b);
-          }
           uint8_t* st = smem + SM_STAT + s * STAT_BYTES;
           bulk_load(st, L2stat + (I.i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
           bulk_load(st + BQ * 4, Dstat + (I.i0 + it) * BQ, BQ * 4, &bars->q_full[s]);
+          if (!(ok = mbar_wait(&bars->do_empty[d], ((gt / DO_STAGES) & 1) ^ 1, wc))) {
+            ++gt;  // the Q copy was issued: the teardown drains it
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->do_full[d], TILE);
+          if (args.dense3d)
+            tma_load_3d(smem + SM_DO + d * TILE, &tmdO, &bars->do_full[d], 0, (I.i0 + it) * BQ, I.bh);
+          else
+            tma_load_4d(smem + SM_DO + d * TILE, &tmdO, &bars->do_full[d], 0, I.h, (I.i0 + it) * BQ, I.b);
+          ++gdo;
         }
       }
       // Teardown: every copy issued must have landed before the CTA leaves.
       for (uint32_t f = kv_filled > 2 ? kv_filled - 2 : 0; f < kv_filled; ++f) mbar_drain(&bars->kv_full[f & 1], (f >> 1) & 1);
       for (int f = max(0, gt - Q_STAGES); f < gt; ++f) mbar_drain(&bars->q_full[f % Q_STAGES], (f / Q_STAGES) & 1);
+      for (int f = max(0, gdo - DO_STAGES); f < gdo; ++f)
+        mbar_drain(&bars->do_full[f % DO_STAGES], (f / DO_STAGES) & 1);
     }
   } else if (warp == W_MMA) {
     // ---------------------------------------------------------------- MMA
@@ -230,13 +244,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         kmajor_pair(tmem + T_ST, sK, sQ + (gt % Q_STAGES) * TILE);
         tc_commit(&bars->s_full);
-        kmajor_pair(tmem + T_DPT, sV, sdO + (gt % Q_STAGES) * TILE);
+        if (!(ok = mbar_wait(&bars->do_full[gt % DO_STAGES], (gt / DO_STAGES) & 1, wc))) break;
+        tc_fence_after();
+        kmajor_pair(tmem + T_DPT, sV, sdO + (gt % DO_STAGES) * TILE);
         tc_commit(&bars->dp_full);
         for (int it = 0; it < I.n; ++it, ++gt) {
-          const int s = gt % Q_STAGES;
-          const uint32_t q_s = sQ + s * TILE, do_s = sdO + s * TILE;
+          const int s = gt % Q_STAGES, d = gt % DO_STAGES;
+          const uint32_t q_s = sQ + s * TILE, do_s = sdO + d * TILE;
           const bool next = it + 1 < I.n;
-          const int s1 = (gt + 1) % Q_STAGES;
+          const int s1 = (gt + 1) % Q_STAGES, d1 = (gt + 1) % DO_STAGES;
           // dV += P^T dO, each query group's 32 queries as soon as its P^T is
           // in TMEM (the groups finish their exponentials at different
           // times). p_ready of an item's first tile also means a group has
@@ -250,6 +266,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_a_acc_g(tmem + T_DV, tmem + T_ST, do_s, it == 0, g);
           }
           if (!ok) break;
+          tc_commit(&bars->do_empty[d]);  // dV(i) is the last MMA that reads dO(i)
           if (next) {
             if (!(ok = mbar_wait(&bars->q_full[s1], ((gt + 1) / Q_STAGES) & 1, wc))) break;
             tc_fence_after();
@@ -263,6 +280,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_a_acc_g(tmem + T_DK, tmem + T_DPT, q_s, it == 0, g);
           }
           if (!ok) break;
+          tc_commit(&bars->q_empty[s]);  // dK(i) is the last MMA that reads Q(i)
           const int b = gt & 1;
           if (!(ok = mbar_wait(&bars->dq_empty[b], ((gt >> 1) & 1) ^ 1, wc))) break;
           tc_fence_after();
@@ -273,9 +291,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               mma_f16_ss(tmem + T_DQ + 64 * b, da + 128 * kk, dk + 128 * kk, id_dq, kk > 0);
           }
           tc_commit(&bars->dq_full[b]);
-          tc_commit(&bars->q_empty[s]);
           if (next) {
-            kmajor_pair(tmem + T_DPT, sV, sdO + s1 * TILE);  // dP^T(i+1)
+            if (!(ok = mbar_wait(&bars->do_full[d1], ((gt + 1) / DO_STAGES) & 1, wc))) break;
+            tc_fence_after();
+            kmajor_pair(tmem + T_DPT, sV, sdO + d1 * TILE);  // dP^T(i+1)
             tc_commit(&bars->dp_full);
           }
         }
