@@ -17,10 +17,16 @@
 //   S^T = K Q^T, dP^T = V dO^T           (TMEM, lanes = keys)
 //   dV += P^T dO, dK += dS^T Q           (P^T, dS^T read from TMEM)
 //   dQ_part = dS K                       (dS staged in shared memory)
-// in the order S(i) dP(i) | dV(i) S(i+1) | dK(i) dQ(i) dP(i+1) so the tensor
-// core overlaps the element-wise work of the 16 compute warps; dV(i) and
-// dK(i) go out in four parts, one per query group of four warps, as each
-// group's P^T or dS^T lands in TMEM. dQ partials go
+// The Q tile's two 64-query halves (query groups 0-1 and 2-3, eight compute
+// warps each) run their own chains: S^T and dP^T are issued per half (N =
+// 64), and the halves take turns on the exponentials (MUFU), so one half's
+// dS work and hand-offs run while the other's exponentials do. The MMA warp
+// issues, per Q tile,
+//   dV(i) of half 0, S(i+1) of half 0 | dV(i) of half 1, S(i+1) of half 1 |
+//   dK(i) of half 0, dP(i+1) of half 0 | dK(i) of half 1, dQ(i), dP(i+1) of
+//   half 1,
+// the order in which the halves' P^T and dS^T hand-offs arrive; dV and dK go
+// out in parts of one query group of four warps each. dQ partials go
 // through two TMEM buffers to 4 drain warps that add them into an fp32
 // accumulator: each partial tile is staged in shared memory and added with one
 // TMA bulk reduce (cp.reduce.async.bulk.tensor .add) per tile; a last kernel
@@ -40,6 +46,10 @@ namespace {
 constexpr int BKV = 128;  // keys per CTA
 constexpr int BQ = 128;   // queries per step
 constexpr int DP = 64;
+// A query half hands the exponentials over to the other half after the
+// first 16 of its 32 columns: the other half's wait ends while these still
+// keep MUFU busy (328 us at config 2, against 333 handing over after all 32).
+constexpr int TURN_CC = 0;
 constexpr int Q_STAGES = 3;   // Q tiles (with their row statistics): released after dK
 constexpr int DO_STAGES = 2;  // dO tiles: released after dV
 constexpr int TILE = 128 * DP * 2;  // 16 KB
@@ -59,7 +69,7 @@ constexpr int STAT_BYTES = 2 * BQ * 4;
 constexpr int SM_DQ = SM_STAT + Q_STAGES * STAT_BYTES;  // dQ staging: 2 boxes of 128 rows x 32 fp32 (SW128)
 constexpr int DQ_BOX = 128 * 128;
 constexpr int SM_BAR = SM_DQ + 2 * DQ_BOX;
-constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+constexpr int SMEM_BYTES = SM_BAR + 512 + 1024;
 
 constexpr uint32_t T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384;  // T_DQ: 2 x 64
 constexpr uint32_t TMEM_COLS = 512;
@@ -73,7 +83,7 @@ __device__ __forceinline__ float ex2(float x) {
 
 struct BwdBars {
   uint64_t kv_full[2], kv_empty[2], q_full[Q_STAGES], q_empty[Q_STAGES], do_full[DO_STAGES], do_empty[DO_STAGES];
-  uint64_t s_full, dp_full, p_ready[4], ds_ready[4], dq_full[2], dq_empty[2], acc_done;
+  uint64_t s_full[2], dp_full[2], turn[2], p_ready[4], ds_ready[4], dq_full[2], dq_empty[2], acc_done, ds_free;
   uint32_t tmem_slot;
   int abort;
 };
@@ -124,8 +134,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bars->q_full[s], 1);
       mbar_init(&bars->q_empty[s], 1);
     }
-    mbar_init(&bars->s_full, 1);
-    mbar_init(&bars->dp_full, 1);
+    for (int x = 0; x < 2; ++x) {  // per query half (groups 0-1, 2-3)
+      mbar_init(&bars->s_full[x], 1);
+      mbar_init(&bars->dp_full[x], 1);
+      mbar_init(&bars->turn[x], 8);
+    }
     for (int g = 0; g < 4; ++g) {  // one per query group (4 warps each)
       mbar_init(&bars->p_ready[g], 4);
       mbar_init(&bars->ds_ready[g], 4);
@@ -135,6 +148,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bars->dq_empty[b], 4);
     }
     mbar_init(&bars->acc_done, 1);
+    mbar_init(&bars->ds_free, 1);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -218,10 +232,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t id_dq = make_idesc(1, 1, 1, 128, DP);   // MN-major dS x MN-major K
       const uint32_t sQ = smem_u32(smem + SM_Q), sdO = smem_u32(smem + SM_DO), sdS = smem_u32(smem + SM_DS);
       // Descriptors advance by adding (byte offset >> 4) to the start field.
-      auto kmajor_pair = [&](uint32_t d, uint32_t a, uint32_t b) {  // d = a . b^T over D
-        const uint64_t da = sw128_desc(a, 16, 1024), db = sw128_desc(b, 16, 1024);
+      // d[:, 64h : 64h+64] = a . b[64h : 64h+64]^T over D: one query half
+      // (b's rows 64h.. are 8 KB into the SW128 tile), N = 64.
+      constexpr uint32_t id_h = make_idesc(1, 0, 0, 128, 64);
+      auto half_pair = [&](uint32_t d, uint32_t a, uint32_t b, int h) {
+        const uint64_t da = sw128_desc(a, 16, 1024), db = sw128_desc(b + h * 8192, 16, 1024);
 #pragma unroll 1
-        for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(d, da + 2 * kk, db + 2 * kk, id_s, kk > 0);
+        for (int kk = 0; kk < DP / 16; ++kk) mma_f16_ss(d + 64 * h, da + 2 * kk, db + 2 * kk, id_h, kk > 0);
       };
       // d += A(tmem) . B over the 32 queries of group g (K steps 2g, 2g+1)
       auto tmem_a_acc_g = [&](uint32_t d, uint32_t a_tmem, uint32_t b, bool first, int g) {
@@ -242,12 +259,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    mbar_wait(&bars->q_full[gt % Q_STAGES], (gt / Q_STAGES) & 1, wc)))
           break;
         tc_fence_after();
-        kmajor_pair(tmem + T_ST, sK, sQ + (gt % Q_STAGES) * TILE);
-        tc_commit(&bars->s_full);
+        for (int h = 0; h < 2; ++h) {
+          half_pair(tmem + T_ST, sK, sQ + (gt % Q_STAGES) * TILE, h);
+          tc_commit(&bars->s_full[h]);
+        }
         if (!(ok = mbar_wait(&bars->do_full[gt % DO_STAGES], (gt / DO_STAGES) & 1, wc))) break;
         tc_fence_after();
-        kmajor_pair(tmem + T_DPT, sV, sdO + (gt % DO_STAGES) * TILE);
-        tc_commit(&bars->dp_full);
+        for (int h = 0; h < 2; ++h) {
+          half_pair(tmem + T_DPT, sV, sdO + (gt % DO_STAGES) * TILE, h);
+          tc_commit(&bars->dp_full[h]);
+        }
         for (int it = 0; it < I.n; ++it, ++gt) {
           const int s = gt % Q_STAGES, d = gt % DO_STAGES;
           const uint32_t q_s = sQ + s * TILE, do_s = sdO + d * TILE;
@@ -260,43 +281,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // which overwrites all of it, waits for all four groups.
           if (it == 0)
             for (int g = 0; ok && g < 4; ++g) ok = mbar_wait(&bars->p_ready[g], gt & 1, wc);
-          for (int g = 0; ok && g < 4; ++g) {
-            if (!(ok = mbar_wait(&bars->p_ready[g], gt & 1, wc))) break;
-            tc_fence_after();
-            tmem_a_acc_g(tmem + T_DV, tmem + T_ST, do_s, it == 0, g);
+          // Each query half runs its own S -> P -> dV -> S(next) and
+          // dP -> dS -> dK -> dP(next) chains; the halves take turns on the
+          // exponentials, so this issue order follows the order their
+          // hand-offs arrive in: P of half 0, P of half 1, dS of half 0, dS
+          // of half 1.
+          for (int h = 0; ok && h < 2; ++h) {
+            for (int g = 2 * h; ok && g < 2 * h + 2; ++g) {  // dV += P^T dO
+              if (!(ok = mbar_wait(&bars->p_ready[g], gt & 1, wc))) break;
+              tc_fence_after();
+              tmem_a_acc_g(tmem + T_DV, tmem + T_ST, do_s, it == 0, g);
+            }
+            if (!ok) break;
+            if (h == 1) tc_commit(&bars->do_empty[d]);  // dV(i) is the last MMA that reads dO(i)
+            if (next) {  // S^T(i+1) of this half, over its P^T(i) that dV has read
+              if (!(ok = mbar_wait(&bars->q_full[s1], ((gt + 1) / Q_STAGES) & 1, wc))) break;
+              tc_fence_after();
+              half_pair(tmem + T_ST, sK, sQ + s1 * TILE, h);
+              tc_commit(&bars->s_full[h]);
+            }
           }
           if (!ok) break;
-          tc_commit(&bars->do_empty[d]);  // dV(i) is the last MMA that reads dO(i)
-          if (next) {
-            if (!(ok = mbar_wait(&bars->q_full[s1], ((gt + 1) / Q_STAGES) & 1, wc))) break;
-            tc_fence_after();
-            kmajor_pair(tmem + T_ST, sK, sQ + s1 * TILE);  // S^T(i+1)
-            tc_commit(&bars->s_full);
-          }
-          // dK += dS^T Q, group by group
-          for (int g = 0; ok && g < 4; ++g) {
-            if (!(ok = mbar_wait(&bars->ds_ready[g], gt & 1, wc))) break;
-            tc_fence_after();
-            tmem_a_acc_g(tmem + T_DK, tmem + T_DPT, q_s, it == 0, g);
-          }
-          if (!ok) break;
-          tc_commit(&bars->q_empty[s]);  // dK(i) is the last MMA that reads Q(i)
-          const int b = gt & 1;
-          if (!(ok = mbar_wait(&bars->dq_empty[b], ((gt >> 1) & 1) ^ 1, wc))) break;
-          tc_fence_after();
-          {
-            const uint64_t da = sw128_desc(sdS, BKV * 128, 1024), dk = sw128_desc(sK, DP * 128, 1024);
+          for (int h = 0; ok && h < 2; ++h) {
+            for (int g = 2 * h; ok && g < 2 * h + 2; ++g) {  // dK += dS^T Q
+              if (!(ok = mbar_wait(&bars->ds_ready[g], gt & 1, wc))) break;
+              tc_fence_after();
+              tmem_a_acc_g(tmem + T_DK, tmem + T_DPT, q_s, it == 0, g);
+            }
+            if (!ok) break;
+            if (h == 1) {
+              tc_commit(&bars->q_empty[s]);  // dK(i) is the last MMA that reads Q(i)
+              // dQ_part = dS K, as soon as both halves' dS(i) are in shared
+              // memory; ds_free tells the compute warps the tile has been read.
+              const int b = gt & 1;
+              if (!(ok = mbar_wait(&bars->dq_empty[b], ((gt >> 1) & 1) ^ 1, wc))) break;
+              tc_fence_after();
+              const uint64_t da = sw128_desc(sdS, BKV * 128, 1024), dk = sw128_desc(sK, DP * 128, 1024);
 #pragma unroll 1
-            for (int kk = 0; kk < BKV / 16; ++kk)  // dQ_part = dS K
-              mma_f16_ss(tmem + T_DQ + 64 * b, da + 128 * kk, dk + 128 * kk, id_dq, kk > 0);
+              for (int kk = 0; kk < BKV / 16; ++kk)
+                mma_f16_ss(tmem + T_DQ + 64 * b, da + 128 * kk, dk + 128 * kk, id_dq, kk > 0);
+              tc_commit(&bars->dq_full[b]);
+              tc_commit(&bars->ds_free);
+            }
+            if (next) {  // dP^T(i+1) of this half, over its dS^T(i) that dK has read
+              if (!(ok = mbar_wait(&bars->do_full[d1], ((gt + 1) / DO_STAGES) & 1, wc))) break;
+              tc_fence_after();
+              half_pair(tmem + T_DPT, sV, sdO + d1 * TILE, h);
+              tc_commit(&bars->dp_full[h]);
+            }
           }
-          tc_commit(&bars->dq_full[b]);
-          if (next) {
-            if (!(ok = mbar_wait(&bars->do_full[d1], ((gt + 1) / DO_STAGES) & 1, wc))) break;
-            tc_fence_after();
-            kmajor_pair(tmem + T_DPT, sV, sdO + d1 * TILE);  // dP^T(i+1)
-            tc_commit(&bars->dp_full);
-          }
+          if (!ok) break;
         }
         if (!ok) break;
         tc_commit(&bars->acc_done);    // dV, dK of this item complete
@@ -376,8 +410,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float* st = reinterpret_cast<const float*>(smem + SM_STAT + (gt % Q_STAGES) * STAT_BYTES);
         const float* Ls = st + 32 * g;
         const float* Ds = st + BQ + 32 * g;
-        if (!(ok = mbar_wait(&bars->s_full, gt & 1, wc))) break;
+        if (!(ok = mbar_wait(&bars->s_full[g >> 1], gt & 1, wc))) break;
         tc_fence_after();
+        // The two query halves take turns on the exponentials (MUFU): half 0
+        // of tile i after half 1 of tile i-1, half 1 after half 0, so one
+        // half's dS work and hand-offs run while the other's exponentials do.
+        if (g < 2 ? gt > 0 : true) {
+          if (!(ok = mbar_wait(&bars->turn[g >> 1], (g < 2 ? gt - 1 : gt) & 1, wc))) break;
+        }
         float p[32];
 #pragma unroll
         for (int cc = 0; cc < 32; cc += 16) {
@@ -393,6 +433,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             p[cc + t] = ex2(a.x);
             p[cc + t + 1] = ex2(a.y);
           });
+          if (cc == TURN_CC) {  // hand the exponentials over to the other half
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->turn[(g >> 1) ^ 1]);
+          }
         }
         if (diag) {
 #pragma unroll
@@ -412,7 +456,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_ready[g]);
-        if (!(ok = mbar_wait(&bars->dp_full, gt & 1, wc))) break;
+        if (!(ok = mbar_wait(&bars->dp_full[g >> 1], gt & 1, wc))) break;
         tc_fence_after();
         uint32_t pk[16];
 #pragma unroll
@@ -432,7 +476,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tmem_st16(tmem + lane_off + T_DPT + 32 * g, pk);
         // dS tile for the dQ MMA: row = key kr, 128-byte row holds queries
-        // [64(g/2), 64(g/2)+64), 16-byte units XOR-swizzled by (kr & 7).
+        // [64(g/2), 64(g/2)+64), 16-byte units XOR-swizzled by (kr & 7). The
+        // previous dQ must have read it (the other half may still be on the
+        // previous tile's dS when this half reaches here).
+        if (!(ok = mbar_wait(&bars->ds_free, (gt & 1) ^ 1, wc))) break;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int unit = unit0 + u;
