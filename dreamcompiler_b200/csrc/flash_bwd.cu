@@ -227,7 +227,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == W_MMA) {
     // ---------------------------------------------------------------- MMA
     if (elect_one_lane()) {
-      constexpr uint32_t id_s = make_idesc(1, 0, 0, 128, 128);   // K-major x K-major, N = 128 queries
       constexpr uint32_t id_acc = make_idesc(1, 0, 1, 128, DP);  // TMEM A x MN-major B, N = D
       constexpr uint32_t id_dq = make_idesc(1, 1, 1, 128, DP);   // MN-major dS x MN-major K
       const uint32_t sQ = smem_u32(smem + SM_Q), sdO = smem_u32(smem + SM_DO), sdS = smem_u32(smem + SM_DS);
