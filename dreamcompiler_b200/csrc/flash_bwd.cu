@@ -536,9 +536,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // D_i = dO_i . O_i (fp32), L2_i = LSE_i * log2(e) in the padded [BH][Spad]
 // layout (rows past S: D = 0, L2 = +inf so that exp2(s - L2) = 0). Eight
 // lanes per row, 16-byte loads when D % 8 == 0.
+//
+// With zero_acc it first zeroes the fp32 dQ accumulator. In the fused
+// backward it is launched as a programmatic dependent of the kernel before
+// it (typically the forward, which lets its dependents start at once): the
+// zeroing reads nothing that kernel writes, so it runs before the wait and
+// overlaps that kernel's tail; the accumulator is this backward's own
+// workspace, which no kernel of the library that starts its dependents
+// early uses.
 __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
   // The main kernel may be scheduled now; it waits for this grid's results.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (a.zero_acc) {  // fresh fp32 dQ accumulator [BH][S][D] for the bulk reduce-adds
+    const long long n = (long long)a.BH * a.S * a.D;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (((uintptr_t)a.dq_acc & 15) == 0) {
+      for (; i < n / 4; i += stride) reinterpret_cast<float4*>(a.dq_acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      i = n / 4 * 4 + blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    }
+    for (; i < n; i += stride) a.dq_acc[i] = 0.f;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // O, dO and LSE come from the kernels before
   const long long rows = (long long)a.BH * a.Spad;
   const int sub = threadIdx.x & 7;
   const long long groups = (long long)gridDim.x * (blockDim.x >> 3);
@@ -569,13 +588,6 @@ __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
     s += __shfl_xor_sync(0xffffffffu, s, 4);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
     s += __shfl_xor_sync(0xffffffffu, s, 1);
-    if (a.zero_acc && q < a.S) {  // fresh fp32 dQ accumulator rows for the bulk reduce-adds
-      float* acc = a.dq_acc + ((long long)bh * a.S + q) * a.D;
-      if (vec)
-        for (int c = sub * 4; c < a.D; c += 32) *reinterpret_cast<float4*>(acc + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-      else
-        for (int c = sub; c < a.D; c += 8) acc[c] = 0.f;
-    }
     if (sub == 0) {
       a.rowstat[r] = q < a.S ? s : 0.f;
       a.rowstat[rows + r] = q < a.S ? a.lse[(long long)bh * a.S + q] * 1.4426950408889634f : INFINITY;
@@ -696,10 +708,19 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
   // predecessor's results; only its launch overlaps the predecessor's tail.
   FlashBwdArgs pa = a;
   pa.zero_acc = 1;
-  flash_bwd_pre_kernel<<<8 * sms, 256, 0, s>>>(pa);
   cudaLaunchAttribute pdl[1];
   pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(8 * sms);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    const cudaError_t e0 = cudaLaunchKernelEx(&cfg, flash_bwd_pre_kernel, pa);
+    if (e0 != cudaSuccess) return e0;
+  }
   const int nkv = (a.S + BKV - 1) / BKV;
   cudaError_t e;
   {

@@ -148,6 +148,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int SM_Q = Cfg::SM_Q, SM_K = Cfg::SM_K, SM_V = Cfg::SM_V, SM_BAR = Cfg::SM_BAR;
   constexpr uint32_t T_S0 = Cfg::T_S0, T_S1 = Cfg::T_S1, T_O0 = Cfg::T_O0, T_O1 = Cfg::T_O1, T_P0 = Cfg::T_P0,
                      T_P1 = Cfg::T_P1;
+  // A programmatic dependent launched after this grid (the backward's row
+  // pre-pass, which zeroes its accumulator before it waits for this grid's
+  // results) may be scheduled now.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + SM_BAR);
