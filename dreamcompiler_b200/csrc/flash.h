@@ -45,6 +45,7 @@ struct FlashBwdArgs {
   int H;                                        // heads per batch row (1: [BH][S][D])
   int ldq, ldk, ldv, ldo, lddo, lddq, lddk, lddv;  // row pitches (elements); dq_acc stays [BH][S][D]
   int dense3d;     // set by the launcher: every tensor is [BH][S][D], loaded through 3-D maps
+  int own_ws;      // the caller's workspace (not library scratch): its zeroing may overlap the kernel before
 };
 
 // The [BH][S][D] layout for every tensor.

@@ -52,6 +52,7 @@ dgx_status dgx_flash_bwd(const void* Q, const void* K, const void* V, const void
   if (!ws) return set_error(DGX_ENOMEM, "dgx_flash_bwd: cannot allocate %zu bytes of scratch", need);
   FlashBwdArgs a{Q, K, V, O, dO, LSE, dQ, dK, dV, (float*)ws, (float*)ws + (size_t)BH * S * D,
                  BH, S, D, flash_spad(S), scale, causal ? 1 : 0, device_error_word()};
+  a.own_ws = workspace != nullptr;
   flash_dense_layout(a);
   const void* ptrs[9] = {Q, K, V, O, dO, dQ, dK, dV, LSE};
   if (flash_tc_supported(D, kFlashBwdMaxD, ptrs, 9)) return cuda_status(flash_bwd_tc(a, s), "dgx_flash_bwd");
@@ -114,6 +115,7 @@ dgx_status dgx_flash_bwd_rows(const void* Q, int ldq, const void* K, int ldk, co
   if (!ws) return set_error(DGX_ENOMEM, "dgx_flash_bwd_rows: cannot allocate %zu bytes of scratch", need);
   FlashBwdArgs a{Q, K, V, O, dO, LSE, dQ, dK, dV, (float*)ws, (float*)ws + (size_t)BH * S * D,
                  BH, S, D, flash_spad(S), scale, causal ? 1 : 0, device_error_word()};
+  a.own_ws = workspace != nullptr;
   a.H = H;
   a.ldq = ldq;
   a.ldk = ldk;

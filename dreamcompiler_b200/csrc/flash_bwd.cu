@@ -538,12 +538,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // lanes per row, 16-byte loads when D % 8 == 0.
 //
 // With zero_acc it first zeroes the fp32 dQ accumulator. In the fused
-// backward it is launched as a programmatic dependent of the kernel before
-// it (typically the forward, which lets its dependents start at once): the
-// zeroing reads nothing that kernel writes, so it runs before the wait and
-// overlaps that kernel's tail; the accumulator is this backward's own
-// workspace, which no kernel of the library that starts its dependents
-// early uses.
+// backward with a caller-provided workspace it is launched as a programmatic
+// dependent of the kernel before it (typically the forward, which lets its
+// dependents start at once): the zeroing reads nothing that kernel writes,
+// so it runs before the wait and overlaps that kernel's tail. No kernel of
+// the library that starts its dependents early uses such a workspace (the
+// int8 kernels, which do, use the library's own scratch, so a backward on
+// library scratch is launched in stream order).
 __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
   // The main kernel may be scheduled now; it waits for this grid's results.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -598,6 +599,9 @@ __global__ void flash_bwd_pre_kernel(FlashBwdArgs a) {
 // dQ = bf16(scale * dQ_acc), four elements per thread step. Launched as a
 // programmatic dependent of the main kernel: it starts on SMs the main
 // kernel has left and waits here for that grid to finish.
+// It does not let its own dependents start early: the next backward's row
+// pre-pass zeroes the accumulator this kernel reads before that pre-pass
+// waits for it.
 __global__ void flash_bwd_post_kernel(FlashBwdArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long total = (long long)a.BH * a.S * a.D;
@@ -717,7 +721,7 @@ cudaError_t flash_bwd_tc(const FlashBwdArgs& a, cudaStream_t s) {
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cfg.attrs = pdl;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = a.own_ws ? 1 : 0;
     const cudaError_t e0 = cudaLaunchKernelEx(&cfg, flash_bwd_pre_kernel, pa);
     if (e0 != cudaSuccess) return e0;
   }

@@ -250,6 +250,8 @@ dgx_status dgx_flash_set_deterministic(int on);
  * and the forward's LSE. workspace: at least dgx_flash_bwd_workspace_size()
  * bytes of device scratch (fp32 dQ accumulator and the row terms
  * D_i = dO_i . O_i); NULL lets the library use its own per-device buffer.
+ * A workspace of the caller's is cleared while the kernel issued just before
+ * the call may still be running (it must not be that kernel's operand).
  * Replaces the "flash_attention" backward branch
  * (runtime/ops/autograd.inc:779-840), without its 3-pass recompute.
  */
