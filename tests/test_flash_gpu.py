@@ -232,3 +232,25 @@ def test_head_rows_rejects_unsupported(dgx):
     o = torch.zeros(256, 80, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(dgx.DgxError):  # D = 48 is fine, but O's pitch 80 < H*D = 96 is not
         dgx.flash_fwd_rows(x[:, :80], x[:, 80:160], x[:, 160:], o, torch.empty(2, 256, device="cuda"), 1, 2, 256, 48)
+
+
+@pytest.mark.parametrize("BH,S,D,causal", [(8, 1024, 64, True), (3, 300, 32, False)])
+def test_caller_workspace_cleared_behind_the_forward(dgx, BH, S, D, causal):
+    """With a workspace of the caller's, the backward's row pre-pass clears the
+    fp32 dQ accumulator in it before waiting for the kernel issued just before
+    (here the forward). A workspace full of NaN before every step must give
+    the dK, dV bits of the library-scratch path and its dQ up to the order of
+    the fp32 reduce-adds, on back-to-back steps with alternating inputs."""
+    g = torch.Generator(device="cuda").manual_seed(31 + S)
+    sets = [[torch.randn(BH, S, D, device="cuda", generator=g).bfloat16() for _ in range(4)] for _ in range(2)]
+    ws = torch.empty(dgx.flash_bwd_workspace_size(BH, S, D) // 4 + 1, device="cuda")
+    for step in range(4):
+        q, k, v, do = sets[step & 1]
+        ws.fill_(float("nan"))
+        O, L = dgx.flash_fwd(q, k, v, causal=causal)
+        a = dgx.flash_bwd(q, k, v, O, do, L, causal=causal, workspace=ws)
+        ref = dgx.flash_bwd(q, k, v, O, do, L, causal=causal)
+        dgx.sync_check()
+        assert torch.equal(a[1], ref[1]) and torch.equal(a[2], ref[2])
+        assert torch.isfinite(a[0].float()).all()
+        assert normwise(host(a[0]), host(ref[0])) < 1e-2
